@@ -1,0 +1,186 @@
+/*
+ * streamlx_cuda.h -- C ABI of libstreamlx_cuda.so, the sm_100a (B200) kernels
+ * behind the streamlx quantized mixture-of-experts expert path.
+ *
+ * Conventions
+ *   - Every pointer argument named x / w / out / scratch / status ... is a
+ *     DEVICE pointer unless the comment says "host".  bf16 data is passed as
+ *     raw 16-bit words (uint16_t / void*), quantized weights as raw bytes.
+ *   - Quantized weights use the MLX "affine" layout: a matrix [out, in] is
+ *     `weight` uint32 [out, in*bits/32] (codes packed low bits first),
+ *     `scales` and `biases` bf16 [out, in/group_size]; w = scale*q + bias.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default).
+ *   - Every call is asynchronous on `stream`, allocates nothing and does not
+ *     synchronise.  The return value is 0 (SLX_OK) or a negative SLX_ERR_*;
+ *     errors found on the device (unmapped expert, out-of-range index, a
+ *     bounded wait that expired) are written to the int32 `status` word
+ *     (first error wins) -- read it after the stream completes.
+ *   - Thread-compatible: concurrent calls need distinct streams / scratch.
+ *
+ * Reference interfaces these replace are cited per entry point
+ * (paths inside the streamlx project).
+ */
+#ifndef STREAMLX_CUDA_H_
+#define STREAMLX_CUDA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SLX_OK 0
+#define SLX_ERR_INVALID (-1)         /* bad argument (host-side check) */
+#define SLX_ERR_UNSUPPORTED (-2)     /* shape / bit width not implemented */
+#define SLX_ERR_CUDA (-3)            /* CUDA runtime error (see string) */
+#define SLX_ERR_OUT_OF_RANGE (-4)    /* device: index outside its table */
+#define SLX_ERR_UNMAPPED_EXPERT (-5) /* device: expert id has no pool slot */
+#define SLX_ERR_DEVICE_TIMEOUT (-6)  /* device: a bounded wait expired */
+#define SLX_ERR_SCRATCH (-7)         /* scratch buffer too small */
+
+#define SLX_GEMV_GLU 0
+#define SLX_GEMV_LINEAR 1
+
+/* One quantized matrix in the MLX affine layout. */
+typedef struct slx_qmat {
+  const void* weight; /* uint32 codes */
+  const void* scales; /* bf16 */
+  const void* biases; /* bf16 */
+} slx_qmat;
+
+/* HBM slot pool of one MoE layer, every slot one expert in the TILE format
+ * produced by slx_pack_experts (16-row tiles streamed by the kernels in one
+ * piece; see streamlx_b200/csrc/slx_tiles.cuh).  Replaces the per-part slot
+ * tensors of streamlx/pool.py:71-77 (StreamingSwitchMLP.pool[proj][part]). */
+typedef struct slx_expert_bank {
+  const void* base;    /* n_slots x slot_stride bytes */
+  int64_t slot_stride; /* >= slx_expert_tiled_bytes(...), multiple of 16 */
+  int32_t n_slots;
+  int32_t hidden;
+  int32_t inter;
+  int32_t bits; /* 2, 4 or 8; group size is 64 */
+} slx_expert_bank;
+
+/* Always-on shared expert (weight 1.0 in the combine), tile format, same
+ * hidden size and bit width as the routed experts. */
+typedef struct slx_shared_expert {
+  const void* base;
+  int32_t inter;
+} slx_shared_expert;
+
+int slx_version(void);
+
+/* Last host-side error message of the calling thread ("" if none). */
+const char* slx_last_error_string(void);
+
+/* Bytes of one expert (gate/up/down, group 64) in the tile format; equal to
+ * its bytes in the MLX layout. */
+size_t slx_expert_tiled_bytes(int hidden, int inter, int bits);
+
+/* Bytes of a dense [out, in] quantized matrix in the tile format (rows
+ * padded to a multiple of 32). */
+size_t slx_dense_tiled_bytes(int out_features, int in_features, int bits);
+
+/* Repack n experts from the MLX affine layout (the safetensors row ranges of
+ * streamlx/stindex.py:31-39, already in device memory) into tile-format
+ * slots dst[i] (device pointers, 16-byte aligned).  gate/up/down/dst are
+ * HOST arrays of n entries.  The slot-fill step of the pool
+ * (streamlx/pool.py:196-199, 295-297). */
+int slx_pack_experts(const slx_qmat* gate, const slx_qmat* up,
+                     const slx_qmat* down, int n, int hidden, int inter,
+                     int bits, void* const* dst, void* stream);
+
+/* Repack a dense [out, in] matrix (MLX layout, device) into the tile format
+ * at dst (slx_dense_tiled_bytes bytes). */
+int slx_pack_dense(const slx_qmat* w, int out_features, int in_features,
+                   int bits, void* dst, void* stream);
+
+/* Scratch bytes slx_switchglu needs for T tokens (activations h). */
+size_t slx_switchglu_scratch_bytes(int T, int k, int inter, int shared_inter);
+
+/* Fused quantized SwitchGLU for decode / small batches (K2).
+ * Replaces streamlx/pool.py:30-50 switch_forward (three gather_qmm + swiglu)
+ * together with the id->slot remap of streamlx/integrate.py:90-95 and the
+ * score-weighted combine of the mlx-lm MoE block (streamlx/integrate.py:5-7).
+ *   x        [T, hidden] bf16
+ *   ids      [T, k] int32 expert ids (or slot ids when slot_table == NULL)
+ *   slot_table [n_table] int32 expert -> slot (-1 = not resident) or NULL
+ *   scores   [T, k] fp32 router weights, or NULL for the drop-in mode that
+ *            returns per-expert UNWEIGHTED outputs out[T, k, hidden]
+ *            (SwitchGLU.__call__ semantics); with scores, out is the combined
+ *            [T, hidden] = sum_j scores*expert_j(x) (+ shared expert).
+ *   shared   optional shared expert (ignored when scores == NULL)
+ *   scratch  >= slx_switchglu_scratch_bytes(...) device bytes
+ * An id without a slot sets SLX_ERR_UNMAPPED_EXPERT in *status and
+ * contributes zeros. */
+int slx_switchglu(const slx_expert_bank* bank, const slx_shared_expert* shared,
+                  const void* x, int T, int k, const int32_t* ids,
+                  const float* scores, const int32_t* slot_table, int n_table,
+                  void* out, void* scratch, size_t scratch_bytes,
+                  int32_t* status, void* stream);
+
+/* Dense quantized linear y[T, out] = x[T, in] @ dequant(W)^T (bf16 out,
+ * fp32 accumulate) over a tile-format matrix (slx_pack_dense).  Trunk
+ * projections of the decoder around the expert path (no reference
+ * counterpart: mlx-lm's QuantizedLinear). */
+int slx_qlinear(const void* w_tiled, int out_features, int in_features,
+                int bits, const void* x, int T, void* y, int32_t* status,
+                void* stream);
+
+/* Bit-exact affine dequantisation of rows `rows[0..nrows)` (device int32
+ * indices, or NULL for rows 0..nrows-1) of a quantized [n_src_rows, in]
+ * matrix into fp32 (out_bf16 = 0) or bf16 (1) out[nrows, in].  The MLX
+ * affine semantics of mx.gather_qmm's weight operand (streamlx/pool.py:43-45);
+ * also the quantized embedding lookup. */
+int slx_dequant_rows(const slx_qmat* w, int in_features, int bits,
+                     int group_size, const int32_t* rows, int nrows,
+                     int n_src_rows, void* out, int out_bf16, int32_t* status,
+                     void* stream);
+
+/* Scratch bytes slx_router_topk needs (logits + per-token tickets).  The
+ * ticket part must be zero before the first call; every call leaves it zero. */
+size_t slx_router_scratch_bytes(int T, int n_experts);
+
+/* Router GEMV + softmax + top-k (K1).  Replaces the mlx-lm MoE router that
+ * produces `indices` for streamlx/integrate.py:234 and the next-layer
+ * predictor streamlx/integrate.py:60-88 (pass ratio = bf16(w_next/w_this)).
+ *   x [T, H] bf16, ratio [H] bf16 or NULL, w_gate [E, H] bf16, bias [E] fp32
+ *   or NULL.  logits = fp32(fp64 dot) + bias; ids = top-k by logit,
+ *   descending, ties to the lower id; scores = softmax(logits)[ids]
+ *   (renormalised to sum 1 when norm_topk).  force [T] (nullable) selects
+ *   tokens whose ids are copied from forced_ids [T, k] instead (the
+ *   temporal-reuse routing override); their scores still come from this
+ *   token's softmax.  out_ids may alias forced_ids. */
+int slx_router_topk(const void* x, const void* ratio, const void* w_gate,
+                    const float* bias, int T, int H, int E, int k,
+                    int norm_topk, const int32_t* force,
+                    const int32_t* forced_ids, int32_t* out_ids,
+                    float* out_scores, void* scratch, size_t scratch_bytes,
+                    int32_t* status, void* stream);
+
+/* Trunk helpers (no reference counterpart; mlx-lm's model code). */
+int slx_add_rmsnorm(void* h, const void* delta, const void* weight, int T,
+                    int H, float eps, void* y, void* stream);
+int slx_qk_norm_rope_cache(void* qkv, int T, int n_q, int n_kv, int head_dim,
+                           const void* q_norm, const void* k_norm, float eps,
+                           const float* inv_freq, const int32_t* pos,
+                           int max_len, void* k_cache, void* v_cache,
+                           int32_t* status, void* stream);
+int slx_attn_decode(const void* qkv, int T, int n_q, int n_kv, int head_dim,
+                    const void* k_cache, const void* v_cache,
+                    const int32_t* pos, int max_len, void* out, void* stream);
+int slx_argmax(const void* logits, int T, int V, int32_t* out, void* stream);
+
+/* Issue n host->device / device->device / device->host copies, one
+ * cudaMemcpyAsync each, on `stream` (host arrays of device/host pointers).
+ * The slot-fill path of the pool (streamlx/pool.py:196-199 slot writes,
+ * pinned staging -> HBM). */
+int slx_copy_many(void* const* dst, const void* const* src,
+                  const size_t* bytes, int n, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* STREAMLX_CUDA_H_ */

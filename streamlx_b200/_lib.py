@@ -1,0 +1,295 @@
+"""ctypes binding of libstreamlx_cuda.so (include/streamlx_cuda.h).
+
+The product path has no CPU fallback: if the shared object is missing or a
+call fails, an exception is raised.  Tensors passed here must be CUDA tensors
+(except the host arrays of ``copy_many``).
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libstreamlx_cuda.so")
+
+SLX_OK = 0
+ERRORS = {
+    -1: "SLX_ERR_INVALID", -2: "SLX_ERR_UNSUPPORTED", -3: "SLX_ERR_CUDA",
+    -4: "SLX_ERR_OUT_OF_RANGE", -5: "SLX_ERR_UNMAPPED_EXPERT",
+    -6: "SLX_ERR_DEVICE_TIMEOUT", -7: "SLX_ERR_SCRATCH",
+}
+GEMV_GLU, GEMV_LINEAR = 0, 1
+
+# every symbol the header declares (the CPU test checks they are exported)
+EXPORTS = (
+    "slx_version", "slx_last_error_string", "slx_expert_tiled_bytes",
+    "slx_dense_tiled_bytes", "slx_pack_experts", "slx_pack_dense",
+    "slx_switchglu_scratch_bytes",
+    "slx_switchglu", "slx_qlinear", "slx_dequant_rows",
+    "slx_router_scratch_bytes", "slx_router_topk", "slx_add_rmsnorm",
+    "slx_qk_norm_rope_cache", "slx_attn_decode", "slx_argmax",
+    "slx_copy_many",
+)
+
+
+class slx_qmat(C.Structure):
+    _fields_ = [("weight", C.c_void_p), ("scales", C.c_void_p),
+                ("biases", C.c_void_p)]
+
+
+class slx_expert_bank(C.Structure):
+    _fields_ = [("base", C.c_void_p), ("slot_stride", C.c_int64),
+                ("n_slots", C.c_int32), ("hidden", C.c_int32),
+                ("inter", C.c_int32), ("bits", C.c_int32)]
+
+
+class slx_shared_expert(C.Structure):
+    _fields_ = [("base", C.c_void_p), ("inter", C.c_int32)]
+
+
+class SlxError(RuntimeError):
+    def __init__(self, fn: str, rc: int, msg: str):
+        super().__init__(f"{fn} failed: {ERRORS.get(rc, rc)}: {msg}")
+        self.rc = rc
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """Load the shared object (raises if it is not built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(
+                f"{LIB_PATH} is missing: build it with "
+                "`python -m streamlx_b200.build` (there is no CPU fallback)")
+        L = C.CDLL(LIB_PATH)
+        vp, i32, sz = C.c_void_p, C.c_int, C.c_size_t
+        L.slx_version.restype = i32
+        L.slx_last_error_string.restype = C.c_char_p
+        L.slx_expert_tiled_bytes.restype = sz
+        L.slx_expert_tiled_bytes.argtypes = [i32, i32, i32]
+        L.slx_dense_tiled_bytes.restype = sz
+        L.slx_dense_tiled_bytes.argtypes = [i32, i32, i32]
+        L.slx_pack_experts.restype = i32
+        L.slx_pack_experts.argtypes = [C.POINTER(slx_qmat), C.POINTER(slx_qmat),
+                                       C.POINTER(slx_qmat), i32, i32, i32,
+                                       i32, vp, vp]
+        L.slx_pack_dense.restype = i32
+        L.slx_pack_dense.argtypes = [C.POINTER(slx_qmat), i32, i32, i32, vp, vp]
+        L.slx_switchglu_scratch_bytes.restype = sz
+        L.slx_switchglu_scratch_bytes.argtypes = [i32, i32, i32, i32]
+        L.slx_switchglu.restype = i32
+        L.slx_switchglu.argtypes = [C.POINTER(slx_expert_bank),
+                                    C.POINTER(slx_shared_expert), vp, i32,
+                                    i32, vp, vp, vp, i32, vp, vp, sz, vp, vp]
+        L.slx_qlinear.restype = i32
+        L.slx_qlinear.argtypes = [vp, i32, i32, i32, vp, i32, vp, vp, vp]
+        L.slx_dequant_rows.restype = i32
+        L.slx_dequant_rows.argtypes = [C.POINTER(slx_qmat), i32, i32, i32, vp,
+                                       i32, i32, vp, i32, vp, vp]
+        L.slx_router_scratch_bytes.restype = sz
+        L.slx_router_scratch_bytes.argtypes = [i32, i32]
+        L.slx_router_topk.restype = i32
+        L.slx_router_topk.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, i32,
+                                      vp, vp, vp, vp, vp, sz, vp, vp]
+        L.slx_add_rmsnorm.restype = i32
+        L.slx_add_rmsnorm.argtypes = [vp, vp, vp, i32, i32, C.c_float, vp, vp]
+        L.slx_qk_norm_rope_cache.restype = i32
+        L.slx_qk_norm_rope_cache.argtypes = [vp, i32, i32, i32, i32, vp, vp,
+                                             C.c_float, vp, vp, i32, vp, vp,
+                                             vp, vp]
+        L.slx_attn_decode.restype = i32
+        L.slx_attn_decode.argtypes = [vp, i32, i32, i32, i32, vp, vp, vp, i32,
+                                      vp, vp]
+        L.slx_argmax.restype = i32
+        L.slx_argmax.argtypes = [vp, i32, i32, vp, vp]
+        L.slx_copy_many.restype = i32
+        L.slx_copy_many.argtypes = [vp, vp, vp, i32, vp]
+        _lib = L
+    return _lib
+
+
+def _check(fn: str, rc: int) -> None:
+    if rc != SLX_OK:
+        raise SlxError(fn, rc, lib().slx_last_error_string().decode())
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    if t is None:
+        return None
+    return t.data_ptr()
+
+
+def stream_ptr(stream: torch.cuda.Stream | None = None) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def qmat(w: torch.Tensor, s: torch.Tensor, b: torch.Tensor) -> slx_qmat:
+    return slx_qmat(w.data_ptr(), s.data_ptr(), b.data_ptr())
+
+
+def expert_tiled_bytes(hidden: int, inter: int, bits: int) -> int:
+    return int(lib().slx_expert_tiled_bytes(hidden, inter, bits))
+
+
+def dense_tiled_bytes(out_features: int, in_features: int, bits: int) -> int:
+    return int(lib().slx_dense_tiled_bytes(out_features, in_features, bits))
+
+
+def slot_stride(hidden: int, inter: int, bits: int) -> int:
+    """Bytes between pool slots: the tiled expert size rounded to 256."""
+    n = expert_tiled_bytes(hidden, inter, bits)
+    return (n + 255) // 256 * 256
+
+
+def pack_experts(experts: list, hidden: int, inter: int, bits: int,
+                 dst_ptrs: list[int],
+                 stream: torch.cuda.Stream | None = None) -> None:
+    """experts: list of (gate3, up3, down3), each a (weight, scales, biases)
+    tuple of CUDA tensors in the MLX layout; dst_ptrs: device addresses."""
+    n = len(experts)
+    if n == 0:
+        return
+    G = (slx_qmat * n)(*[qmat(*e[0]) for e in experts])
+    U = (slx_qmat * n)(*[qmat(*e[1]) for e in experts])
+    D = (slx_qmat * n)(*[qmat(*e[2]) for e in experts])
+    P = (C.c_void_p * n)(*dst_ptrs)
+    rc = lib().slx_pack_experts(G, U, D, n, hidden, inter, bits, P,
+                                stream_ptr(stream))
+    _check("slx_pack_experts", rc)
+
+
+def pack_dense(w3, out_features: int, in_features: int, bits: int,
+               dst: torch.Tensor, stream: torch.cuda.Stream | None = None
+               ) -> None:
+    m = qmat(*w3)
+    rc = lib().slx_pack_dense(C.byref(m), out_features, in_features, bits,
+                              dst.data_ptr(), stream_ptr(stream))
+    _check("slx_pack_dense", rc)
+
+
+def bank_struct(pool: torch.Tensor, n_slots: int, hidden: int, inter: int,
+                bits: int, stride: int | None = None) -> slx_expert_bank:
+    """pool: uint8 CUDA tensor holding n_slots tiled experts."""
+    st = stride if stride is not None else slot_stride(hidden, inter, bits)
+    return slx_expert_bank(pool.data_ptr(), st, n_slots, hidden, inter, bits)
+
+
+def shared_struct(buf: torch.Tensor, inter: int) -> slx_shared_expert:
+    return slx_shared_expert(buf.data_ptr(), inter)
+
+
+def switchglu_scratch_bytes(T: int, k: int, inter: int, shared_inter: int = 0
+                            ) -> int:
+    return int(lib().slx_switchglu_scratch_bytes(T, k, inter, shared_inter))
+
+
+def switchglu(bank: slx_expert_bank, x: torch.Tensor, ids: torch.Tensor,
+              out: torch.Tensor, scratch: torch.Tensor, status: torch.Tensor,
+              scores: torch.Tensor | None = None,
+              slot_table: torch.Tensor | None = None,
+              shared: slx_shared_expert | None = None,
+              stream: torch.cuda.Stream | None = None) -> None:
+    T, k = ids.shape[-2], ids.shape[-1]
+    rc = lib().slx_switchglu(
+        C.byref(bank), C.byref(shared) if shared is not None else None,
+        x.data_ptr(), T, k, ids.data_ptr(), ptr(scores), ptr(slot_table),
+        int(slot_table.numel()) if slot_table is not None else 0,
+        out.data_ptr(), scratch.data_ptr(), scratch.numel() * scratch.element_size(),
+        status.data_ptr(), stream_ptr(stream))
+    _check("slx_switchglu", rc)
+
+
+def qlinear(w_tiled: torch.Tensor, out_features: int, in_features: int,
+            bits: int, x: torch.Tensor, y: torch.Tensor, status: torch.Tensor,
+            T: int | None = None,
+            stream: torch.cuda.Stream | None = None) -> None:
+    rc = lib().slx_qlinear(w_tiled.data_ptr(), out_features, in_features, bits,
+                           x.data_ptr(), T if T is not None else x.shape[0],
+                           y.data_ptr(), status.data_ptr(), stream_ptr(stream))
+    _check("slx_qlinear", rc)
+
+
+def dequant_rows(w3, in_features: int, bits: int, rows: torch.Tensor | None,
+                 nrows: int, n_src_rows: int, out: torch.Tensor,
+                 status: torch.Tensor, group_size: int = 64,
+                 stream: torch.cuda.Stream | None = None) -> None:
+    m = qmat(*w3)
+    rc = lib().slx_dequant_rows(C.byref(m), in_features, bits, group_size,
+                                ptr(rows), nrows, n_src_rows, out.data_ptr(),
+                                1 if out.dtype == torch.bfloat16 else 0,
+                                status.data_ptr(), stream_ptr(stream))
+    _check("slx_dequant_rows", rc)
+
+
+def router_scratch_bytes(T: int, E: int) -> int:
+    return int(lib().slx_router_scratch_bytes(T, E))
+
+
+def router_topk(x: torch.Tensor, w_gate: torch.Tensor, bias, k: int,
+                norm_topk: bool, out_ids: torch.Tensor,
+                out_scores: torch.Tensor, scratch: torch.Tensor,
+                status: torch.Tensor, ratio: torch.Tensor | None = None,
+                force: torch.Tensor | None = None,
+                forced_ids: torch.Tensor | None = None,
+                stream: torch.cuda.Stream | None = None) -> None:
+    T, H = x.shape[-2], x.shape[-1]
+    E = w_gate.shape[0]
+    rc = lib().slx_router_topk(
+        x.data_ptr(), ptr(ratio), w_gate.data_ptr(), ptr(bias), T, H, E, k,
+        1 if norm_topk else 0, ptr(force), ptr(forced_ids), out_ids.data_ptr(),
+        out_scores.data_ptr(), scratch.data_ptr(),
+        scratch.numel() * scratch.element_size(), status.data_ptr(),
+        stream_ptr(stream))
+    _check("slx_router_topk", rc)
+
+
+def add_rmsnorm(h, delta, weight, eps: float, y, stream=None) -> None:
+    T, H = h.shape[-2], h.shape[-1]
+    rc = lib().slx_add_rmsnorm(h.data_ptr(), ptr(delta), weight.data_ptr(), T,
+                               H, eps, y.data_ptr(), stream_ptr(stream))
+    _check("slx_add_rmsnorm", rc)
+
+
+def qk_norm_rope_cache(qkv, n_q, n_kv, hd, q_norm, k_norm, eps, inv_freq,
+                       pos, k_cache, v_cache, status, stream=None) -> None:
+    rc = lib().slx_qk_norm_rope_cache(
+        qkv.data_ptr(), qkv.shape[0], n_q, n_kv, hd, q_norm.data_ptr(),
+        k_norm.data_ptr(), eps, inv_freq.data_ptr(), pos.data_ptr(),
+        k_cache.shape[0], k_cache.data_ptr(), v_cache.data_ptr(),
+        status.data_ptr(), stream_ptr(stream))
+    _check("slx_qk_norm_rope_cache", rc)
+
+
+def attn_decode(qkv, n_q, n_kv, hd, k_cache, v_cache, pos, out,
+                stream=None) -> None:
+    rc = lib().slx_attn_decode(qkv.data_ptr(), qkv.shape[0], n_q, n_kv, hd,
+                               k_cache.data_ptr(), v_cache.data_ptr(),
+                               pos.data_ptr(), k_cache.shape[0], out.data_ptr(),
+                               stream_ptr(stream))
+    _check("slx_attn_decode", rc)
+
+
+def argmax(logits, out, stream=None) -> None:
+    T, V = logits.shape[-2], logits.shape[-1]
+    rc = lib().slx_argmax(logits.data_ptr(), T, V, out.data_ptr(),
+                          stream_ptr(stream))
+    _check("slx_argmax", rc)
+
+
+def copy_many(dsts: list[int], srcs: list[int], sizes: list[int],
+              stream: torch.cuda.Stream | None = None) -> None:
+    n = len(dsts)
+    if n == 0:
+        return
+    D = (C.c_void_p * n)(*dsts)
+    S = (C.c_void_p * n)(*srcs)
+    Z = (C.c_size_t * n)(*sizes)
+    rc = lib().slx_copy_many(D, S, Z, n, stream_ptr(stream))
+    _check("slx_copy_many", rc)

@@ -1,0 +1,387 @@
+// extern "C" entry points of libstreamlx_cuda.so (declared in
+// include/streamlx_cuda.h).  Host-side argument checks, then the launchers.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include <vector>
+
+#include "slx_kernels.cuh"
+#include "slx_tiles.cuh"
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+int cuda_check(int rc, const char* what) {
+  if (rc == SLX_ERR_CUDA) {
+    cudaError_t e = cudaGetLastError();
+    return fail(rc, "%s: %s", what, cudaGetErrorString(e));
+  }
+  if (rc == SLX_ERR_UNSUPPORTED) return fail(rc, "%s: unsupported shape", what);
+  if (rc != SLX_OK) return fail(rc, "%s: error %d", what, rc);
+  return SLX_OK;
+}
+
+bool aligned16(const void* p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+bool qmat_ok(const slx_qmat& m) {
+  return m.weight && m.scales && m.biases && aligned16(m.weight) &&
+         aligned16(m.scales) && aligned16(m.biases);
+}
+
+size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
+
+}  // namespace
+
+extern "C" {
+
+int slx_version(void) { return 1; }
+
+const char* slx_last_error_string(void) { return g_err.c_str(); }
+
+// scratch = SwiGLU output of every routed unit and of the shared expert, in
+// the down projection's fragment layout: per unit (in/64) x 32 words of fp16
+// pairs + (in/64) x 4 partial sums.
+size_t slx_switchglu_scratch_bytes(int T, int k, int inter, int shared_inter) {
+  if (T < 0 || k < 0 || inter < 0 || shared_inter < 0) return 0;
+  const size_t u = (size_t)T * k, ng = inter / 64, ngs = shared_inter / 64;
+  return align256(u * ng * 128) + align256(u * ng * 16) +
+         align256((size_t)T * ngs * 128) + align256((size_t)T * ngs * 16);
+}
+
+size_t slx_expert_tiled_bytes(int hidden, int inter, int bits) {
+  if (hidden <= 0 || inter <= 0 || hidden % 64 || inter % 64) return 0;
+  return slx::expert_tiled_bytes(hidden, inter, bits);
+}
+
+size_t slx_dense_tiled_bytes(int out_features, int in_features, int bits) {
+  if (out_features <= 0 || in_features <= 0 || in_features % 64) return 0;
+  return slx::dense_tiled_bytes(out_features, in_features, bits);
+}
+
+int slx_pack_experts(const slx_qmat* gate, const slx_qmat* up,
+                     const slx_qmat* down, int n, int hidden, int inter,
+                     int bits, void* const* dst, void* stream) {
+  g_err.clear();
+  if (n < 0 || (n > 0 && (!gate || !up || !down || !dst)))
+    return fail(SLX_ERR_INVALID, "pack_experts: bad arrays");
+  if (bits != 2 && bits != 4 && bits != 8)
+    return fail(SLX_ERR_UNSUPPORTED, "bits %d", bits);
+  if (hidden <= 0 || inter <= 0 || hidden % 64 || inter % 64)
+    return fail(SLX_ERR_INVALID, "hidden %d inter %d", hidden, inter);
+  std::vector<const void*> v[9];
+  for (int e = 0; e < n; ++e) {
+    const slx_qmat* m[3] = {&gate[e], &up[e], &down[e]};
+    for (int p = 0; p < 3; ++p) {
+      if (!qmat_ok(*m[p])) return fail(SLX_ERR_INVALID, "expert %d part %d", e, p);
+      v[3 * p].push_back(m[p]->weight);
+      v[3 * p + 1].push_back(m[p]->scales);
+      v[3 * p + 2].push_back(m[p]->biases);
+    }
+    if (!dst[e] || !aligned16(dst[e]))
+      return fail(SLX_ERR_INVALID, "dst[%d] NULL or misaligned", e);
+  }
+  if (n == 0) return SLX_OK;
+  const int rc = slx::launch_pack_experts(
+      v[0].data(), v[1].data(), v[2].data(), v[3].data(), v[4].data(),
+      v[5].data(), v[6].data(), v[7].data(), v[8].data(), dst, n, hidden,
+      inter, bits, reinterpret_cast<cudaStream_t>(stream));
+  return rc ? cuda_check(rc, "slx_pack_experts") : SLX_OK;
+}
+
+int slx_pack_dense(const slx_qmat* w, int out_features, int in_features,
+                   int bits, void* dst, void* stream) {
+  g_err.clear();
+  if (!w || !qmat_ok(*w) || !dst || !aligned16(dst))
+    return fail(SLX_ERR_INVALID, "pack_dense: bad pointers");
+  if (bits != 2 && bits != 4 && bits != 8)
+    return fail(SLX_ERR_UNSUPPORTED, "bits %d", bits);
+  if (out_features <= 0 || in_features <= 0 || in_features % 64)
+    return fail(SLX_ERR_INVALID, "pack_dense shape %d x %d", out_features,
+                in_features);
+  const int rc = slx::launch_pack_dense(w->weight, w->scales, w->biases,
+                                        out_features, in_features, bits, dst,
+                                        reinterpret_cast<cudaStream_t>(stream));
+  return rc ? cuda_check(rc, "slx_pack_dense") : SLX_OK;
+}
+
+int slx_switchglu(const slx_expert_bank* bank, const slx_shared_expert* shared,
+                  const void* x, int T, int k, const int32_t* ids,
+                  const float* scores, const int32_t* slot_table, int n_table,
+                  void* out, void* scratch, size_t scratch_bytes,
+                  int32_t* status, void* stream) {
+  g_err.clear();
+  if (!bank) return fail(SLX_ERR_INVALID, "slx_switchglu: bank is NULL");
+  const int H = bank->hidden, I = bank->inter, bits = bank->bits;
+  if (bits != 2 && bits != 4 && bits != 8)
+    return fail(SLX_ERR_UNSUPPORTED, "bits %d (2/4/8)", bits);
+  if (H <= 0 || I <= 0 || H % 64 || I % 64)
+    return fail(SLX_ERR_INVALID, "hidden %d / inter %d must be multiples of 64",
+                H, I);
+  if (T < 0 || k < 1 || bank->n_slots < 1)
+    return fail(SLX_ERR_INVALID, "T %d k %d n_slots %d", T, k, bank->n_slots);
+  if (bank->slot_stride < (int64_t)slx::expert_tiled_bytes(H, I, bits) ||
+      bank->slot_stride % 16)
+    return fail(SLX_ERR_INVALID, "slot_stride %lld", (long long)bank->slot_stride);
+  if (T == 0) return SLX_OK;
+  if (!x || !ids || !out || !aligned16(x) || !aligned16(out))
+    return fail(SLX_ERR_INVALID, "x/ids/out NULL or not 16-byte aligned");
+  if (!bank->base || !aligned16(bank->base))
+    return fail(SLX_ERR_INVALID, "bank base NULL or misaligned");
+  if (slot_table && n_table < 1)
+    return fail(SLX_ERR_INVALID, "n_table %d", n_table);
+  const bool use_shared = scores && shared;
+  const int Is = use_shared ? shared->inter : 0;
+  if (use_shared) {
+    if (Is <= 0 || Is % 64) return fail(SLX_ERR_INVALID, "shared inter %d", Is);
+    if (!shared->base || !aligned16(shared->base))
+      return fail(SLX_ERR_INVALID, "shared expert base NULL or misaligned");
+  }
+  const size_t need = slx_switchglu_scratch_bytes(T, k, I, Is);
+  if (!scratch || scratch_bytes < need || !aligned16(scratch))
+    return fail(SLX_ERR_SCRATCH, "scratch %zu < %zu bytes", scratch_bytes, need);
+  const size_t nu = (size_t)T * k, ng = I / 64, ngs = Is / 64;
+  uint8_t* sp = reinterpret_cast<uint8_t*>(scratch);
+  uint32_t* hfrag = reinterpret_cast<uint32_t*>(sp);
+  sp += align256(nu * ng * 128);
+  float* hpart = reinterpret_cast<float*>(sp);
+  sp += align256(nu * ng * 16);
+  uint32_t* hfrag_sh = reinterpret_cast<uint32_t*>(sp);
+  sp += align256((size_t)T * ngs * 128);
+  float* hpart_sh = reinterpret_cast<float*>(sp);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+
+  slx::GemvArgs a = {};
+  a.mode = SLX_GEMV_GLU;
+  a.x = reinterpret_cast<const uint16_t*>(x);
+  a.T = T;
+  a.in = H;
+  a.ids = ids;
+  a.k = k;
+  a.slot_table = slot_table;
+  a.n_table = n_table;
+  a.n_slots = bank->n_slots;
+  a.bank = reinterpret_cast<const uint8_t*>(bank->base);
+  a.slot_stride = bank->slot_stride;
+  a.I = I;
+  a.shared = use_shared ? reinterpret_cast<const uint8_t*>(shared->base) : nullptr;
+  a.Is = Is;
+  a.hfrag = hfrag;
+  a.hpart = hpart;
+  a.hfrag_sh = hfrag_sh;
+  a.hpart_sh = hpart_sh;
+  a.unit_frag_words = (int)ng * 32;
+  a.unit_part_floats = (int)ng * 4;
+  a.shared_frag_words = (int)ngs * 32;
+  a.shared_part_floats = (int)ngs * 4;
+  a.status = status;
+  a.n_tiles = T * k * (I / 16) + T * (Is / 16);
+  int rc = slx::launch_gemv(a, bits, s, /*pdl_secondary=*/true);
+  if (rc) return cuda_check(rc, "slx_switchglu gate/up");
+
+  slx::DownArgs d = {};
+  d.T = T;
+  d.k = k;
+  d.H = H;
+  d.I = I;
+  d.Is = Is;
+  d.ids = ids;
+  d.slot_table = slot_table;
+  d.n_table = n_table;
+  d.n_slots = bank->n_slots;
+  d.scores = scores;
+  d.bank = a.bank;
+  d.slot_stride = bank->slot_stride;
+  d.shared = a.shared;
+  d.hfrag = hfrag;
+  d.hpart = hpart;
+  d.hfrag_sh = hfrag_sh;
+  d.hpart_sh = hpart_sh;
+  d.unit_frag_words = a.unit_frag_words;
+  d.unit_part_floats = a.unit_part_floats;
+  d.shared_frag_words = a.shared_frag_words;
+  d.shared_part_floats = a.shared_part_floats;
+  d.out = reinterpret_cast<uint16_t*>(out);
+  d.status = status;
+  d.n_items = T * (H / 16);
+  d.n_units = k + (Is > 0 ? 1 : 0);
+  d.pdl = 1;
+  rc = slx::launch_down(d, bits, s);
+  return rc ? cuda_check(rc, "slx_switchglu down") : SLX_OK;
+}
+
+int slx_qlinear(const void* w_tiled, int out_features, int in_features,
+                int bits, const void* x, int T, void* y, int32_t* status,
+                void* stream) {
+  g_err.clear();
+  if (!w_tiled || !aligned16(w_tiled))
+    return fail(SLX_ERR_INVALID, "qlinear: weight NULL or misaligned");
+  if (bits != 2 && bits != 4 && bits != 8)
+    return fail(SLX_ERR_UNSUPPORTED, "bits %d", bits);
+  if (in_features <= 0 || in_features % 64 || out_features <= 0 ||
+      out_features % 16)
+    return fail(SLX_ERR_INVALID, "qlinear shape out %d in %d", out_features,
+                in_features);
+  if (T < 0) return fail(SLX_ERR_INVALID, "T %d", T);
+  if (T == 0) return SLX_OK;
+  if (!x || !y || !aligned16(x)) return fail(SLX_ERR_INVALID, "x/y");
+  slx::GemvArgs a = {};
+  a.mode = SLX_GEMV_LINEAR;
+  a.x = reinterpret_cast<const uint16_t*>(x);
+  a.T = T;
+  a.in = in_features;
+  a.lin = reinterpret_cast<const uint8_t*>(w_tiled);
+  a.out_features = out_features;
+  a.y = reinterpret_cast<uint16_t*>(y);
+  a.status = status;
+  a.n_tiles = T * ((out_features + 31) / 32);
+  const int rc = slx::launch_gemv(a, bits, reinterpret_cast<cudaStream_t>(stream),
+                                  /*pdl_secondary=*/false);
+  return rc ? cuda_check(rc, "slx_qlinear") : SLX_OK;
+}
+
+int slx_dequant_rows(const slx_qmat* w, int in_features, int bits,
+                     int group_size, const int32_t* rows, int nrows,
+                     int n_src_rows, void* out, int out_bf16, int32_t* status,
+                     void* stream) {
+  g_err.clear();
+  if (!w || !w->weight || !w->scales || !w->biases || !out)
+    return fail(SLX_ERR_INVALID, "dequant: NULL pointer");
+  if (bits != 2 && bits != 4 && bits != 8)
+    return fail(SLX_ERR_UNSUPPORTED, "bits %d", bits);
+  if (group_size <= 0 || in_features % group_size || (in_features * bits) % 32)
+    return fail(SLX_ERR_INVALID, "dequant shape in %d gs %d", in_features,
+                group_size);
+  if (nrows < 0 || n_src_rows < 0) return fail(SLX_ERR_INVALID, "rows");
+  const int rc = slx::launch_dequant_rows(
+      (const uint32_t*)w->weight, (const uint16_t*)w->scales,
+      (const uint16_t*)w->biases, in_features, bits, group_size, rows, nrows,
+      n_src_rows, out, out_bf16, status, reinterpret_cast<cudaStream_t>(stream));
+  return rc ? cuda_check(rc, "slx_dequant_rows") : SLX_OK;
+}
+
+size_t slx_router_scratch_bytes(int T, int n_experts) {
+  if (T < 0 || n_experts < 0) return 0;
+  return align256((size_t)T * n_experts * 4) + align256((size_t)T * 4);
+}
+
+int slx_router_topk(const void* x, const void* ratio, const void* w_gate,
+                    const float* bias, int T, int H, int E, int k,
+                    int norm_topk, const int32_t* force,
+                    const int32_t* forced_ids, int32_t* out_ids,
+                    float* out_scores, void* scratch, size_t scratch_bytes,
+                    int32_t* status, void* stream) {
+  g_err.clear();
+  if (!x || !w_gate || !out_ids || !out_scores)
+    return fail(SLX_ERR_INVALID, "router: NULL pointer");
+  if (!aligned16(x) || !aligned16(w_gate) || (ratio && !aligned16(ratio)))
+    return fail(SLX_ERR_INVALID, "router: x / w_gate / ratio not 16-byte aligned");
+  if (T < 0 || H <= 0 || H % 8 || E < 1 || k < 1 || k > E)
+    return fail(SLX_ERR_INVALID, "router shape T %d H %d E %d k %d", T, H, E, k);
+  if (force && !forced_ids) return fail(SLX_ERR_INVALID, "force without ids");
+  if (T == 0) return SLX_OK;
+  const size_t need = slx_router_scratch_bytes(T, E);
+  if (!scratch || scratch_bytes < need)
+    return fail(SLX_ERR_SCRATCH, "router scratch %zu < %zu", scratch_bytes, need);
+  slx::RouterArgs a = {};
+  a.x = (const uint16_t*)x;
+  a.ratio = (const uint16_t*)ratio;
+  a.w = (const uint16_t*)w_gate;
+  a.bias = bias;
+  a.T = T;
+  a.H = H;
+  a.E = E;
+  a.k = k;
+  a.norm_topk = norm_topk;
+  a.force = force;
+  a.forced_ids = forced_ids;
+  a.out_ids = out_ids;
+  a.out_scores = out_scores;
+  a.logits = reinterpret_cast<float*>(scratch);
+  a.tickets = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(scratch) +
+                                         align256((size_t)T * E * 4));
+  a.status = status;
+  const int rc = slx::launch_router(a, reinterpret_cast<cudaStream_t>(stream));
+  return rc ? cuda_check(rc, "slx_router_topk") : SLX_OK;
+}
+
+int slx_add_rmsnorm(void* h, const void* delta, const void* weight, int T,
+                    int H, float eps, void* y, void* stream) {
+  g_err.clear();
+  if (!h || !weight || !y) return fail(SLX_ERR_INVALID, "rmsnorm: NULL");
+  const int rc = slx::launch_add_rmsnorm(
+      (uint16_t*)h, (const uint16_t*)delta, (const uint16_t*)weight, T, H, eps,
+      (uint16_t*)y, reinterpret_cast<cudaStream_t>(stream));
+  return rc ? cuda_check(rc, "slx_add_rmsnorm") : SLX_OK;
+}
+
+int slx_qk_norm_rope_cache(void* qkv, int T, int n_q, int n_kv, int head_dim,
+                           const void* q_norm, const void* k_norm, float eps,
+                           const float* inv_freq, const int32_t* pos,
+                           int max_len, void* k_cache, void* v_cache,
+                           int32_t* status, void* stream) {
+  g_err.clear();
+  if (!qkv || !q_norm || !k_norm || !inv_freq || !pos || !k_cache || !v_cache)
+    return fail(SLX_ERR_INVALID, "rope: NULL");
+  if (n_q < 1 || n_kv < 1 || n_q % n_kv) return fail(SLX_ERR_INVALID, "heads");
+  const int rc = slx::launch_qk_rope_cache(
+      (uint16_t*)qkv, T, n_q, n_kv, head_dim, (const uint16_t*)q_norm,
+      (const uint16_t*)k_norm, eps, inv_freq, pos, max_len,
+      (uint16_t*)k_cache, (uint16_t*)v_cache, status,
+      reinterpret_cast<cudaStream_t>(stream));
+  return rc ? cuda_check(rc, "slx_qk_norm_rope_cache") : SLX_OK;
+}
+
+int slx_attn_decode(const void* qkv, int T, int n_q, int n_kv, int head_dim,
+                    const void* k_cache, const void* v_cache,
+                    const int32_t* pos, int max_len, void* out, void* stream) {
+  g_err.clear();
+  if (!qkv || !k_cache || !v_cache || !pos || !out)
+    return fail(SLX_ERR_INVALID, "attn: NULL");
+  if (n_q < 1 || n_kv < 1 || n_q % n_kv) return fail(SLX_ERR_INVALID, "heads");
+  const int rc = slx::launch_attn_decode(
+      (const uint16_t*)qkv, T, n_q, n_kv, head_dim, (const uint16_t*)k_cache,
+      (const uint16_t*)v_cache, pos, max_len, (uint16_t*)out,
+      reinterpret_cast<cudaStream_t>(stream));
+  return rc ? cuda_check(rc, "slx_attn_decode") : SLX_OK;
+}
+
+int slx_argmax(const void* logits, int T, int V, int32_t* out, void* stream) {
+  g_err.clear();
+  if (!logits || !out || V < 1) return fail(SLX_ERR_INVALID, "argmax");
+  const int rc = slx::launch_argmax((const uint16_t*)logits, T, V, out,
+                                    reinterpret_cast<cudaStream_t>(stream));
+  return rc ? cuda_check(rc, "slx_argmax") : SLX_OK;
+}
+
+int slx_copy_many(void* const* dst, const void* const* src,
+                  const size_t* bytes, int n, void* stream) {
+  g_err.clear();
+  if (n < 0 || (n > 0 && (!dst || !src || !bytes)))
+    return fail(SLX_ERR_INVALID, "copy_many: bad arrays");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  for (int i = 0; i < n; ++i) {
+    if (!bytes[i]) continue;
+    const cudaError_t e =
+        cudaMemcpyAsync(dst[i], src[i], bytes[i], cudaMemcpyDefault, s);
+    if (e != cudaSuccess)
+      return fail(SLX_ERR_CUDA, "copy_many[%d]: %s", i, cudaGetErrorString(e));
+  }
+  return SLX_OK;
+}
+
+}  // extern "C"

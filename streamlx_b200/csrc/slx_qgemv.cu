@@ -1,0 +1,809 @@
+// Quantized (MLX affine 2/4/8-bit, group 64) GEMV engine for sm_100a.
+//
+// Replaces, for batch-1 decode, the three `mx.gather_qmm` calls plus
+// `swiglu` of the reference's `switch_forward` (streamlx/pool.py:30-50), the
+// id->slot remap (streamlx/integrate.py:90-95) and the score-weighted combine
+// of the mlx-lm MoE block around it (streamlx/integrate.py:5-7).  Two
+// kernels, chained with programmatic dependent launch so the second one's
+// weight stream starts while the first is still running:
+//
+//   k_qgemv<BITS>  (phase A)  gate+up pair tiles of every routed expert (and
+//                  the optional shared expert) -> h = bf16(silu(bf16 g) *
+//                  bf16 u) into a small scratch buffer.  The same kernel in
+//                  LINEAR mode is the trunk's dense quantized linear.
+//   k_down<BITS>   (phase B)  down single tiles of every routed expert,
+//                  per-expert bf16 rounding (MLX returns bf16 from
+//                  gather_qmm), then the router-score-weighted sum (+ shared
+//                  expert) with one bf16 rounding.  Each output row is owned
+//                  by one CTA: the combine is deterministic, no atomics.
+//
+// Weights are read in the tile format of slx_tiles.cuh, so one 16-row tile
+// arrives in a single bulk copy; requests are issued many per instruction
+// (the copy engine's cost is per request and per issuing instruction).
+//
+// Warp specialisation: warp 0 issues the bulk copies (TMA engine, L2
+// evict-first, mbarrier completion); warps 1..8 split a tile's 64-column
+// groups.  Codes are unpacked in registers by one AND per fp16 pair (the
+// code becomes an exact fp16 subnormal, slx_common.cuh) and multiplied on
+// the tensor cores (mma.sync m16n8k16, fp32 accumulate) against the
+// activation, which sits in shared memory as ready-made B fragments with the
+// unpack's power-of-two factors folded in.  Per group the fp32 result is
+// folded with the MLX affine identity
+//     sum_c x_c (s q_c + b) = s * sum_c q_c x_c + b * sum_c x_c,
+// so no dequantised weight is ever materialised.
+// Every mbarrier wait is bounded (slx_common.cuh: mbar_wait).
+#include "slx_kernels.cuh"
+#include "slx_tiles.cuh"
+
+#ifdef SLX_TRACE
+__device__ unsigned long long g_slx_trace[3][160][16];
+extern "C" int slx_trace_read(unsigned long long* host) {
+  return cudaMemcpyFromSymbol(host, g_slx_trace, sizeof(g_slx_trace)) ==
+                 cudaSuccess ? 0 : -1;
+}
+#endif
+
+namespace slx {
+
+constexpr int kNW = 8;                    // consumer warps
+constexpr int kThreads = 32 * (kNW + 1);  // + producer warp
+constexpr int kMaxStages = 32;
+constexpr int kRows = 16;
+
+struct TileInfo {
+  int token;
+  int unit;               // routed unit u = token*k + pick; -1-token: shared
+  int ti;                 // 16-row tile index inside the unit
+  int valid;
+  int valid1;             // LINEAR: second 16-row half inside the matrix
+  const uint8_t* src;     // tile in global memory
+  uint16_t* out;          // GLU: h + row0; LINEAR: y + row0
+};
+
+SLX_DEV int lookup_slot(const int32_t* ids, int u, const int32_t* table,
+                        int n_table, int n_slots) {
+  const int e = ids[u];
+  int s = e;
+  if (table) s = (e >= 0 && e < n_table) ? table[e] : -1;
+  return (s >= 0 && s < n_slots) ? s : -1;
+}
+
+// Remembers the last unit's slot so consecutive tiles of one expert cost no
+// global loads.
+struct SlotCache {
+  int unit = -1;
+  int slot = -1;
+};
+
+SLX_DEV TileInfo gemv_tile(const GemvArgs& a, int q, SlotCache& sc) {
+  TileInfo t{};
+  if (a.mode == SLX_GEMV_LINEAR) {
+    const int tpu = (a.out_features + 31) / 32;
+    t.token = q / tpu;
+    const int ti = q % tpu;
+    t.valid = 1;
+    t.valid1 = (32 * ti + 16) < a.out_features;
+    t.src = a.lin + (size_t)ti * a.tile_bytes;
+    t.out = a.y + (size_t)t.token * a.out_features + 32 * ti;
+    return t;
+  }
+  const int tpu = a.I / kRows;
+  const int routed = a.T * a.k * tpu;
+  if (q < routed) {
+    const int u = q / tpu, ti = q % tpu;
+    t.token = u / a.k;
+    if (u != sc.unit) {
+      sc.unit = u;
+      sc.slot = lookup_slot(a.ids, u, a.slot_table, a.n_table, a.n_slots);
+    }
+    const int slot = sc.slot;
+    t.valid = t.valid1 = slot >= 0;
+    t.unit = u;
+    t.ti = ti;
+    t.src = a.bank + (size_t)(slot < 0 ? 0 : slot) * a.slot_stride +
+            (size_t)ti * a.tile_bytes;
+    t.out = nullptr;
+    return t;
+  }
+  const int qs = q - routed, tps = a.Is / kRows;
+  t.token = qs / tps;
+  const int ti = qs % tps;
+  t.valid = t.valid1 = 1;
+  t.unit = -1 - t.token;  // shared expert of token t
+  t.ti = ti;
+  t.src = a.shared + (size_t)ti * a.tile_bytes;
+  t.out = nullptr;
+  return t;
+}
+
+// ------------------------------------------------- activation fragments ---
+//
+// frag[G][tig][8]: fp16 pairs matching unpack register j of a thread with
+// this tig (columns 64G + 16 tig + col_lo/hi(j)), each multiplied by
+// act_scale (a power of two: exact); xsum[G] = sum of the group's 64
+// activations (the bias term of the affine identity).  One (group, tig)
+// task per thread, all units at once: a single round of global loads.
+template <int BITS>
+SLX_DEV void frag_task(const uint16_t* __restrict__ x, int G, int tig,
+                       uint32_t* frag, float* part) {
+  const uint4* src = reinterpret_cast<const uint4*>(x + 64 * G + 16 * tig);
+  const uint4 q0 = src[0], q1 = src[1];
+  const uint32_t w8[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int cl = col_lo(BITS, j), ch = col_hi(BITS, j);
+    const float xl = (cl & 1) ? bf16_hi(w8[cl >> 1]) : bf16_lo(w8[cl >> 1]);
+    const float xh = (ch & 1) ? bf16_hi(w8[ch >> 1]) : bf16_lo(w8[ch >> 1]);
+    frag[(G * 4 + tig) * 8 + j] =
+        pack_f16x2(xl * act_scale(BITS, cl), xh * act_scale(BITS, ch));
+    s += xl + xh;
+  }
+  part[G * 4 + tig] = s;
+}
+
+// Sum the four per-tig partials of every group (fixed order).
+SLX_DEV void frag_sums(const float* part, float* xsum, int n, int tid,
+                       int nthr) {
+  for (int i = tid; i < n; i += nthr)
+    xsum[i] = (part[4 * i] + part[4 * i + 1]) + (part[4 * i + 2] + part[4 * i + 3]);
+}
+
+SLX_DEV void load_frag(const uint32_t* frag, int G, int tig, uint32_t (&b)[8]) {
+  const uint4* fp = reinterpret_cast<const uint4*>(frag + (G * 4 + tig) * 8);
+  const uint4 f0 = fp[0], f1 = fp[1];
+  b[0] = f0.x; b[1] = f0.y; b[2] = f0.z; b[3] = f0.w;
+  b[4] = f1.x; b[5] = f1.y; b[6] = f1.z; b[7] = f1.w;
+}
+
+// The thread's packed codes of row `row` (tile row block `blk`), group G.
+template <int BITS>
+SLX_DEV void load_unpack(const uint8_t* blk, int row, int G, int tig, int RB,
+                         bool swz, uint32_t (&r)[8]) {
+  const int off = swz_offset(row, 8 * BITS * G + 2 * BITS * tig, RB, swz);
+  const uint8_t* p = blk + off;
+  if constexpr (BITS == 2) {
+    unpack2(*reinterpret_cast<const uint32_t*>(p), r);
+  } else if constexpr (BITS == 4) {
+    const uint2 w = *reinterpret_cast<const uint2*>(p);
+    unpack4(w.x, w.y, r);
+  } else {
+    const uint4 w = *reinterpret_cast<const uint4*>(p);
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    unpack8(ws, r);
+  }
+}
+
+// 16 rows x 64 columns of one row block against the activation fragment:
+// d = 2^-24 * sum_c q[row, c] * x[c]  (rows g and g+8 in d[0..1] / d[2..3]).
+template <int BITS>
+SLX_DEV void group_mma(const uint8_t* blk, int RB, bool swz, int G, int g,
+                       int tig, const uint32_t (&b)[8], float (&d)[4]) {
+  uint32_t ra[8], rb[8];
+  load_unpack<BITS>(blk, g, G, tig, RB, swz, ra);
+  load_unpack<BITS>(blk, g + 8, G, tig, RB, swz, rb);
+  // four independent k16 products (no accumulator chain), summed in fp32
+  const float z[4] = {0.f, 0.f, 0.f, 0.f};
+  float p[4][4];
+#pragma unroll
+  for (int m = 0; m < 4; ++m)
+    mma_f16_16816(p[m], ra[2 * m], rb[2 * m], ra[2 * m + 1], rb[2 * m + 1],
+                  b[2 * m], b[2 * m + 1], z);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) d[i] = (p[0][i] + p[1][i]) + (p[2][i] + p[3][i]);
+}
+
+SLX_DEV void named_bar_consumers() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kNW * 32) : "memory");
+}
+
+// fold one group: acc += scale * sum(q*x) + bias * sum(x); sb = scale|bias
+SLX_DEV float fold(float acc, float d, uint32_t sb, float xs) {
+  acc = fmaf(bf16_lo(sb) * kSubnormalUnit, d, acc);
+  return fmaf(bf16_hi(sb), xs, acc);
+}
+
+// ------------------------------------------------------- phase A kernel ---
+//
+// Pipeline without CTA-wide barriers in the steady state:
+//   consumer warps: wait full[s] -> MMA over their groups -> partial dot to
+//     red[s][warp] -> arrive redfull[s];
+//   warp 0: issues tile copies; per tile, waits redfull[s] (which also means
+//     stage s is free), refills stage s, reduces the 8 partials, runs the
+//     epilogue (SwiGLU -> down-projection fragments, or the LINEAR output)
+//     and arrives redempty[s] so consumers may reuse red[s].
+
+template <int BITS>
+SLX_DEV void gemv_issue(const GemvArgs& a, const TileInfo& t, uint8_t* dst,
+                        uint64_t* bar, uint64_t pol) {
+  if (t.valid) {
+    mbar_arrive_expect_tx(bar, a.tile_bytes);
+    bulk_g2s(dst, t.src, a.tile_bytes, bar, pol);
+  } else {
+    mbar_arrive(bar);
+  }
+}
+
+// Reduce the tile's partials (red[w][lane], w < kNW) and write its output.
+// Lane (g, tig): tig>>1 selects the matrix (gate/up or rows 0-15/16-31),
+// tig&1 the row half.  All 32 lanes must call this.
+template <int BITS>
+SLX_DEV void gemv_epilogue(const GemvArgs& a, const TileInfo& t,
+                           const float* red, int lane) {
+  const int g = lane >> 2, tig = lane & 3;
+  float v = 0.f;
+#pragma unroll
+  for (int w = 0; w < kNW; ++w) v += red[w * 32 + lane];
+  if (a.mode != SLX_GEMV_GLU) {
+    const int mat = tig >> 1;
+    const int r = 16 * mat + g + 8 * (tig & 1);
+    if (mat == 0 || t.valid1) t.out[r] = f32_to_bf16(v);
+    return;
+  }
+  // h for the tile's 16 rows = 16 activation columns of the down
+  // projection, i.e. exactly fragment block (G = ti/4, tig = ti%4) of phase
+  // B.  Lane (g, t<2) holds h[row g + 8t].
+  const float up = __shfl_down_sync(0xffffffffu, v, 2);
+  float hv = 0.f;
+  if (tig < 2) {
+    const float gb = round_bf16(v), ubf = round_bf16(up);
+    hv = t.valid ? round_bf16(gb / (1.f + expf(-gb)) * ubf) : 0.f;
+  }
+  const int j = lane & 7;
+  const int cl = col_lo(BITS, j), ch = col_hi(BITS, j);
+  const float lo = __shfl_sync(0xffffffffu, hv, (cl & 7) * 4 + (cl >> 3));
+  const float hi = __shfl_sync(0xffffffffu, hv, (ch & 7) * 4 + (ch >> 3));
+  const uint32_t word =
+      pack_f16x2(lo * act_scale(BITS, cl), hi * act_scale(BITS, ch));
+  float hsum = hv;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) hsum += __shfl_xor_sync(0xffffffffu, hsum, o);
+  uint32_t* fr;
+  float* pt;
+  if (t.unit >= 0) {
+    fr = a.hfrag + (size_t)t.unit * a.unit_frag_words;
+    pt = a.hpart + (size_t)t.unit * a.unit_part_floats;
+  } else {
+    const int tok = -1 - t.unit;
+    fr = a.hfrag_sh + (size_t)tok * a.shared_frag_words;
+    pt = a.hpart_sh + (size_t)tok * a.shared_part_floats;
+  }
+  if (lane < 8) fr[t.ti * 8 + lane] = word;  // block (G*4 + tig) = ti
+  if (lane == 0) pt[t.ti] = hsum;
+}
+
+template <int BITS>
+__global__ void __launch_bounds__(kThreads, 2)
+    k_qgemv(const __grid_constant__ GemvArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int nG = tile_ng(a.in), RB = tile_rb(a.in, BITS);
+  const bool swz = tile_swizzled(a.in, BITS);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* redfull = full + kMaxStages;
+  uint64_t* redempty = redfull + kMaxStages;
+  uint32_t* frag = reinterpret_cast<uint32_t*>(smem + 3 * kMaxStages * 8);
+  float* xsum = reinterpret_cast<float*>(frag + nG * 32);
+  float* part = xsum + nG;     // [nG][4]
+  float* red = part + 4 * nG;  // [NS][kNW][32]
+  const int NS = a.n_stages;
+  uint8_t* stages = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(red + NS * kNW * 32) + 127) & ~uintptr_t(127));
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q_begin = (int)((long long)a.n_tiles * blockIdx.x / gridDim.x);
+  const int q_end = (int)((long long)a.n_tiles * (blockIdx.x + 1) / gridDim.x);
+  const int n = q_end - q_begin;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&redfull[i], kNW);
+      mbar_init(&redempty[i], 1);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  SLX_TRACE_POINT(0, 0);
+  SLX_TRACE_SMID(0);
+  if (a.wait_primary) pdl_wait_primary();
+  // Let the dependent (down-projection) grid start its weight stream now.
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    // ------------------------------------------- producer + epilogue ---
+    // The first NS tiles go out in one instruction (lane i -> tile i): the
+    // copy engine serves the requests of one instruction together.
+    const uint64_t pol = l2_evict_first_policy();
+    const int first = n < NS ? n : NS;
+    SlotCache issue_cache, epi_cache;
+    if (lane < first)
+      gemv_issue<BITS>(a, gemv_tile(a, q_begin + lane, issue_cache),
+                       stages + (size_t)lane * a.stage_bytes, &full[lane], pol);
+    for (int i = 0; i < n; ++i) {
+      const int st = i % NS;
+      if (!mbar_wait(&redfull[st], (i / NS) & 1, a.status)) break;
+      // every consumer is done with stage st: refill it
+      if (lane == 0 && i + NS < n)
+        gemv_issue<BITS>(a, gemv_tile(a, q_begin + i + NS, issue_cache),
+                         stages + (size_t)st * a.stage_bytes, &full[st], pol);
+      gemv_epilogue<BITS>(a, gemv_tile(a, q_begin + i, epi_cache),
+                          red + st * kNW * 32, lane);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&redempty[st]);
+      if (i < 6) SLX_TRACE_AT(2, 8 + i, globaltimer_ns());
+    }
+    return;
+  }
+
+  // ------------------------------------------------------- consumers ---
+  const int cw = warp - 1;  // consumer warp 0..kNW-1
+  const int ct = threadIdx.x - 32;
+  const int g = lane >> 2, tig = lane & 3;
+  const int mat = tig >> 1;
+  const int sbl = mat * 16 + g + 8 * (tig & 1);  // this lane's SB word slot
+  int cached_token = -1;
+  SlotCache scache;
+  for (int q = q_begin, i = 0; q < q_end; ++q, ++i) {
+    const int st = i % NS;
+    const TileInfo t = gemv_tile(a, q, scache);
+    if (t.token != cached_token) {
+      named_bar_consumers();
+      const uint16_t* xr = a.x + (size_t)t.token * a.in;
+      for (int p = ct; p < 4 * nG; p += kNW * 32)
+        frag_task<BITS>(xr, p >> 2, p & 3, frag, part);
+      named_bar_consumers();
+      frag_sums(part, xsum, nG, ct, kNW * 32);
+      named_bar_consumers();
+      cached_token = t.token;
+      SLX_TRACE_POINT(0, 1);
+    }
+    if (!t.valid && ct == 0) set_status(a.status, SLX_ERR_UNMAPPED_EXPERT);
+    const bool ok = mbar_wait(&full[st], (i / NS) & 1, a.status);
+    if (i < 6) SLX_TRACE_POINT(0, 2 + 2 * i);
+    const uint8_t* S = stages + (size_t)st * a.stage_bytes;
+    float acc = 0.f;
+    if (ok && t.valid) {
+      const uint8_t* P = S;
+      const uint8_t* Q = S + 16 * RB;
+      const uint32_t* SB = reinterpret_cast<const uint32_t*>(S + 32 * RB);
+      // two groups in flight per warp (independent MMA chains)
+      for (int G = cw; G < nG; G += 2 * kNW) {
+        const int G2 = G + kNW;
+        const bool two = G2 < nG;
+        uint32_t b[8], b2[8];
+        load_frag(frag, G, tig, b);
+        if (two) load_frag(frag, G2, tig, b2);
+        float d0[4], d1[4];
+        float e0[4] = {0.f, 0.f, 0.f, 0.f}, e1[4] = {0.f, 0.f, 0.f, 0.f};
+        group_mma<BITS>(P, RB, swz, G, g, tig, b, d0);
+        group_mma<BITS>(Q, RB, swz, G, g, tig, b, d1);
+        if (two) {
+          group_mma<BITS>(P, RB, swz, G2, g, tig, b2, e0);
+          group_mma<BITS>(Q, RB, swz, G2, g, tig, b2, e1);
+        }
+        const float v = mat == 0 ? ((tig & 1) ? d0[2] : d0[0])
+                                 : ((tig & 1) ? d1[2] : d1[0]);
+        acc = fold(acc, v, SB[G * 32 + sbl], xsum[G]);
+        if (two) {
+          const float v2 = mat == 0 ? ((tig & 1) ? e0[2] : e0[0])
+                                    : ((tig & 1) ? e1[2] : e1[0]);
+          acc = fold(acc, v2, SB[G2 * 32 + sbl], xsum[G2]);
+        }
+      }
+    }
+    // hand the partial to the epilogue warp (red[st] free once it has
+    // consumed the previous tile that used this buffer)
+    if (i >= NS) mbar_wait(&redempty[st], ((i / NS) - 1) & 1, a.status);
+    red[(st * kNW + cw) * 32 + lane] = acc;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&redfull[st]);
+    if (i < 6) SLX_TRACE_POINT(0, 3 + 2 * i);
+  }
+}
+
+// ------------------------------------------------------- phase B kernel ---
+//
+// Work item = (token, 16 output rows).  Each consumer warp takes two units
+// (routed picks j, j+1, or the shared expert) at a time and the 64-column
+// groups G = cw, cw+8, ... of both -- independent MMA chains in flight --
+// leaving per-warp partial dots in red[item parity].  Warp 0 (which also
+// issued the weight copies) then rounds each unit's dot to bf16, weights it
+// by its router score and sums over units in unit order: deterministic, and
+// off the consumers' critical path.
+
+template <int BITS>
+SLX_DEV float down_unit_groups(const uint8_t* S, int in, int cw, int g,
+                               int tig, int rrow, const uint32_t* fr,
+                               const float* xs) {
+  const int nG = tile_ng(in), RB = tile_rb(in, BITS);
+  const bool swz = tile_swizzled(in, BITS);
+  const uint32_t* SB = reinterpret_cast<const uint32_t*>(S + 16 * RB);
+  float acc = 0.f;
+  for (int G = cw; G < nG; G += 2 * kNW) {
+    const int G2 = G + kNW;
+    const bool two = G2 < nG;
+    uint32_t b[8], b2[8];
+    load_frag(fr, G, tig, b);
+    if (two) load_frag(fr, G2, tig, b2);
+    float d[4], e[4] = {0.f, 0.f, 0.f, 0.f};
+    group_mma<BITS>(S, RB, swz, G, g, tig, b, d);
+    if (two) group_mma<BITS>(S, RB, swz, G2, g, tig, b2, e);
+    acc = fold(acc, (tig & 1) ? d[2] : d[0], SB[G * 16 + rrow], xs[G]);
+    if (two)
+      acc = fold(acc, (tig & 1) ? e[2] : e[0], SB[G2 * 16 + rrow], xs[G2]);
+  }
+  return acc;
+}
+
+template <int BITS>
+__global__ void __launch_bounds__(kThreads, 2)
+    k_down(const __grid_constant__ DownArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int U = a.n_units;
+  const int nGr = tile_ng(a.I), nGs = a.Is ? tile_ng(a.Is) : 0;
+  const int nGmax = nGr > nGs ? nGr : nGs;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* itemfull = full + kMaxStages;  // [2], count kNW
+  uint64_t* itemempty = itemfull + 2;      // [2], count 1
+  uint32_t* frag = reinterpret_cast<uint32_t*>(smem + (kMaxStages + 4) * 8);
+  float* part = reinterpret_cast<float*>(frag + (size_t)U * nGmax * 32);
+  //            ^ [U][nGmax][4], 16-byte aligned (float4 copies)
+  float* xsum = part + (size_t)4 * U * nGmax;      // [U][nGmax]
+  float* red = xsum + (size_t)U * nGmax;           // [2][kNW][U][16]
+  float* ysm = red + (size_t)2 * kNW * U * kRows;  // [U][16]
+  uint8_t* stages = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(ysm + (size_t)U * kRows) + 127) &
+      ~uintptr_t(127));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int NS = a.n_stages;
+  const int tph = a.H / kRows;
+  const int q_begin = (int)((long long)a.n_items * blockIdx.x / gridDim.x);
+  const int q_end = (int)((long long)a.n_items * (blockIdx.x + 1) / gridDim.x);
+  const int n_it = q_end - q_begin;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NS; ++i) mbar_init(&full[i], 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&itemfull[i], kNW);
+      mbar_init(&itemempty[i], 1);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    // ------------------------------------------- producer + reduction ---
+    // Weights do not depend on phase A, so stream them before it finishes.
+    // Request seq = item * U + unit goes to stage seq % NS (NS >= U); lane l
+    // of a round issues seq base + l, so one instruction carries up to 32.
+    const uint64_t pol = l2_evict_first_policy();
+    const int total = n_it * U;
+    auto issue = [&](int seq) {
+      const int st = seq % NS;
+      const int q = q_begin + seq / U, j = seq % U;
+      const int token = q / tph, rb = q % tph;
+      const bool shared = j >= a.k;
+      const int bytes = shared ? a.tile_bytes_sh : a.tile_bytes;
+      const uint8_t* src;
+      bool valid = true;
+      if (!shared) {
+        const int slot = lookup_slot(a.ids, token * a.k + j, a.slot_table,
+                                     a.n_table, a.n_slots);
+        valid = slot >= 0;
+        src = a.bank + (size_t)(valid ? slot : 0) * a.slot_stride +
+              a.a_bytes + (size_t)rb * a.tile_bytes;
+      } else {
+        src = a.shared + a.a_bytes_sh + (size_t)rb * a.tile_bytes_sh;
+      }
+      if (valid) {
+        mbar_arrive_expect_tx(&full[st], bytes);
+        bulk_g2s(stages + (size_t)st * a.stage_bytes, src, bytes, &full[st], pol);
+      } else {
+        mbar_arrive(&full[st]);
+      }
+    };
+    const int first = total < NS ? total : NS;
+    for (int base = 0; base < first; base += 32)
+      if (base + lane < first) issue(base + lane);
+    for (int it = 0; it < n_it; ++it) {
+      const int b = it & 1;
+      if (!mbar_wait(&itemfull[b], (it >> 1) & 1, a.status)) break;
+      // the item's stages are free: issue the requests that reuse them
+      const int lo = it * U + NS, hi = (it + 1) * U + NS;
+      for (int s0 = lo; s0 < hi && s0 < total; s0 += 32)
+        if (s0 + lane < hi && s0 + lane < total) issue(s0 + lane);
+      // rounding, score weighting and the combine of item it
+      const int q = q_begin + it;
+      const int token = q / tph, row0 = (q % tph) * kRows;
+      const float* rd = red + (size_t)b * kNW * U * kRows;
+      for (int p = lane; p < U * kRows; p += 32) {
+        const int j = p / kRows, r = p % kRows;
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < kNW; ++w) v += rd[((size_t)w * U + j) * kRows + r];
+        const bool valid = j >= a.k || lookup_slot(a.ids, token * a.k + j,
+                                                   a.slot_table, a.n_table,
+                                                   a.n_slots) >= 0;
+        const float y = valid ? round_bf16(v) : 0.f;  // gather_qmm: bf16
+        if (!a.scores)
+          a.out[((size_t)token * a.k + j) * a.H + row0 + r] = f32_to_bf16(y);
+        else
+          ysm[j * kRows + r] = (j < a.k) ? a.scores[token * a.k + j] * y : y;
+      }
+      __syncwarp();
+      if (a.scores && lane < kRows) {
+        float v = 0.f;
+        for (int j = 0; j < U; ++j) v += ysm[j * kRows + lane];
+        a.out[(size_t)token * a.H + row0 + lane] = f32_to_bf16(v);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&itemempty[b]);
+    }
+    SLX_TRACE_POINT(1, 14);
+    return;
+  }
+
+  const int cw = warp - 1, ct = threadIdx.x - 32;
+  const int g = lane >> 2, tig = lane & 3;
+  const int rrow = g + 8 * (tig & 1);
+  SLX_TRACE_POINT(1, 0);
+  SLX_TRACE_SMID(1);
+  if (a.pdl) pdl_wait_primary();  // the activation fragments come from phase A
+  SLX_TRACE_POINT(1, 1);
+  int cached_token = -1;
+  for (int q = q_begin, it = 0; q < q_end; ++q, ++it) {
+    const int token = q / tph;
+    if (token != cached_token) {
+      // Fragments of every unit's activation were written by phase A; copy
+      // them (all loads in flight before any store) and sum the partials.
+      named_bar_consumers();
+      const int pu = nGmax * 8;  // uint4 per unit in shared memory
+      for (int base = ct; base < U * pu; base += 4 * kNW * 32) {
+        uint4 v[4];
+        int dst[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const int p = base + r * kNW * 32;
+          const int j = p / pu, o = p % pu;
+          dst[r] = -1;
+          if (j < U) {
+            const bool shared = j >= a.k;
+            if (o < (shared ? nGs : nGr) * 8) {
+              const uint32_t* src =
+                  shared ? a.hfrag_sh + (size_t)token * a.shared_frag_words
+                         : a.hfrag + (size_t)(token * a.k + j) * a.unit_frag_words;
+              v[r] = reinterpret_cast<const uint4*>(src)[o];
+              dst[r] = p;
+            }
+          }
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+          if (dst[r] >= 0) reinterpret_cast<uint4*>(frag)[dst[r]] = v[r];
+      }
+      for (int p = ct; p < U * nGmax; p += kNW * 32) {
+        const int j = p / nGmax, G = p % nGmax;
+        const bool shared = j >= a.k;
+        if (G < (shared ? nGs : nGr)) {
+          const float* src = shared
+              ? a.hpart_sh + (size_t)token * a.shared_part_floats
+              : a.hpart + (size_t)(token * a.k + j) * a.unit_part_floats;
+          reinterpret_cast<float4*>(part)[p] =
+              reinterpret_cast<const float4*>(src)[G];
+        }
+      }
+      named_bar_consumers();
+      frag_sums(part, xsum, U * nGmax, ct, kNW * 32);
+      named_bar_consumers();
+      cached_token = token;
+      SLX_TRACE_POINT(1, 2);
+    }
+    const int b = it & 1;
+    if (it >= 2) mbar_wait(&itemempty[b], ((it >> 1) - 1) & 1, a.status);
+    float* rd = red + (size_t)b * kNW * U * kRows;
+    for (int j = 0; j < U; j += 2) {
+      const bool pair = j + 1 < U;
+      const int s0 = (it * U + j) % NS, s1 = (it * U + j + 1) % NS;
+      const bool ok0 = mbar_wait(&full[s0], ((it * U + j) / NS) & 1, a.status);
+      const bool ok1 = pair ? mbar_wait(&full[s1], ((it * U + j + 1) / NS) & 1,
+                                        a.status)
+                            : false;
+      float acc0 = 0.f, acc1 = 0.f;
+      if (ok0)
+        acc0 = down_unit_groups<BITS>(stages + (size_t)s0 * a.stage_bytes,
+                                      j >= a.k ? a.Is : a.I, cw, g, tig, rrow,
+                                      frag + (size_t)j * nGmax * 32,
+                                      xsum + (size_t)j * nGmax);
+      if (ok1)
+        acc1 = down_unit_groups<BITS>(stages + (size_t)s1 * a.stage_bytes,
+                                      j + 1 >= a.k ? a.Is : a.I, cw, g, tig,
+                                      rrow, frag + (size_t)(j + 1) * nGmax * 32,
+                                      xsum + (size_t)(j + 1) * nGmax);
+      if (tig < 2) {
+        rd[((size_t)cw * U + j) * kRows + rrow] = acc0;
+        if (pair) rd[((size_t)cw * U + j + 1) * kRows + rrow] = acc1;
+      }
+      if (it == 0 && j < 20) SLX_TRACE_POINT(1, 3 + j / 2);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&itemfull[b]);
+  }
+}
+
+// ------------------------------------------------------------ launchers ---
+
+static int g_num_sms = 0;
+static int num_sms() {
+  if (!g_num_sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (g_num_sms <= 0) g_num_sms = 148;
+  }
+  return g_num_sms;
+}
+
+// Phase A and phase B each request exactly kSmemTarget bytes: one CTA of
+// each fits on an SM (2 x 113 KB + 2 x 1 KB reserved = the full 228 KB), and
+// -- because two CTAs of either kernel alone also need the full carve-out --
+// both kernels run with the same shared-memory configuration.  An SM must
+// drain to change configuration, so matching them is what lets the PDL
+// secondary start beside a running primary.
+constexpr int kSmemTarget = 113 * 1024;
+constexpr int kSmemBudget = kSmemTarget;
+constexpr int kSmemMax = 227 * 1024;
+
+// Raise the kernel's dynamic shared-memory limit once per instantiation
+// (one process drives one GPU).
+template <typename K, int TAG>
+static cudaError_t set_smem(K kern, int bytes) {
+  static int configured = 0;
+  if (bytes <= configured) return cudaSuccess;
+  const cudaError_t e =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+  if (e == cudaSuccess) configured = kSmemMax;
+  return e;
+}
+
+template <int BITS>
+static int launch_gemv_t(GemvArgs a, cudaStream_t stream, bool pdl_secondary) {
+  const int nG = tile_ng(a.in);
+  a.tile_bytes = (int)pair_tile_bytes(a.in, BITS);
+  a.stage_bytes = (a.tile_bytes + 127) & ~127;
+  // fixed part + per stage (tile + its kNW x 32 partials)
+  const int fixed = 3 * kMaxStages * 8 + nG * 32 * 4 + nG * 4 * 5 + 128;
+  const int per_stage = a.stage_bytes + kNW * 32 * 4;
+  int ns = (kSmemBudget - fixed) / per_stage;
+  if (ns < 2) ns = (kSmemMax - fixed) / per_stage;
+  if (ns > kMaxStages) ns = kMaxStages;
+  if (ns < 2) return SLX_ERR_UNSUPPORTED;
+  a.n_stages = ns;
+  int smem = fixed + ns * per_stage;
+  if (smem < kSmemTarget) smem = kSmemTarget;
+  a.wait_primary = pdl_secondary ? 1 : 0;
+  if (a.n_tiles <= 0) return SLX_OK;
+  int grid = num_sms();
+  if (grid > a.n_tiles) grid = a.n_tiles;
+  cudaError_t e = set_smem<decltype(&k_qgemv<BITS>), BITS>(k_qgemv<BITS>, smem);
+  if (e != cudaSuccess) return SLX_ERR_CUDA;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_secondary ? 1 : 0;
+  e = cudaLaunchKernelEx(&cfg, k_qgemv<BITS>, a);
+  return e == cudaSuccess ? SLX_OK : SLX_ERR_CUDA;
+}
+
+int launch_gemv(GemvArgs a, int bits, cudaStream_t stream, bool pdl_secondary) {
+  switch (bits) {
+    case 2: return launch_gemv_t<2>(a, stream, pdl_secondary);
+    case 4: return launch_gemv_t<4>(a, stream, pdl_secondary);
+    case 8: return launch_gemv_t<8>(a, stream, pdl_secondary);
+    default: return SLX_ERR_UNSUPPORTED;
+  }
+}
+
+template <int BITS>
+static int launch_down_t(DownArgs a, cudaStream_t stream) {
+  const int nGr = tile_ng(a.I), nGs = a.Is ? tile_ng(a.Is) : 0;
+  const int nGmax = nGr > nGs ? nGr : nGs;
+  a.tile_bytes = (int)single_tile_bytes(a.I, BITS);
+  a.tile_bytes_sh = a.Is ? (int)single_tile_bytes(a.Is, BITS) : 0;
+  a.a_bytes = (long long)expert_a_bytes(a.H, a.I, BITS);
+  a.a_bytes_sh = a.Is ? (long long)expert_a_bytes(a.H, a.Is, BITS) : 0;
+  const int tb = a.tile_bytes > a.tile_bytes_sh ? a.tile_bytes : a.tile_bytes_sh;
+  a.stage_bytes = (tb + 127) & ~127;
+  const int fixed = (kMaxStages + 4) * 8 + a.n_units * nGmax * (32 * 4 + 4 * 5) +
+                    (2 * kNW + 1) * a.n_units * kRows * 4 + 128;
+  // Stages of a work item are released together at its end, so the ring
+  // must hold every unit of one item (else the producer could never issue
+  // the item's last units).
+  int ns = (kSmemBudget - fixed) / a.stage_bytes;
+  if (ns < a.n_units) ns = (kSmemMax - fixed) / a.stage_bytes;
+  if (ns > kMaxStages) ns = kMaxStages;
+  if (ns < a.n_units || ns < 2) return SLX_ERR_UNSUPPORTED;
+  a.n_stages = ns;
+  int smem = fixed + ns * a.stage_bytes;
+  if (smem < kSmemTarget) smem = kSmemTarget;
+  if (a.n_items <= 0) return SLX_OK;
+  int grid = num_sms();
+  if (grid > a.n_items) grid = a.n_items;
+  cudaError_t e = set_smem<decltype(&k_down<BITS>), 100 + BITS>(k_down<BITS>, smem);
+  if (e != cudaSuccess) return SLX_ERR_CUDA;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = a.pdl ? 1 : 0;
+  e = cudaLaunchKernelEx(&cfg, k_down<BITS>, a);
+  return e == cudaSuccess ? SLX_OK : SLX_ERR_CUDA;
+}
+
+int launch_down(DownArgs a, int bits, cudaStream_t stream) {
+  switch (bits) {
+    case 2: return launch_down_t<2>(a, stream);
+    case 4: return launch_down_t<4>(a, stream);
+    case 8: return launch_down_t<8>(a, stream);
+    default: return SLX_ERR_UNSUPPORTED;
+  }
+}
+
+// ---------------------------------------------------- dequant (bit-exact) --
+
+// out[r, c] = scale * q + bias for rows listed in `rows`; fp32 or bf16
+// output.  MLX layout input.  One rounding (fmaf of an exact product).
+__global__ void k_dequant_rows(const uint32_t* __restrict__ w,
+                               const uint16_t* __restrict__ s,
+                               const uint16_t* __restrict__ b, int in, int bits,
+                               int gs, const int32_t* __restrict__ rows,
+                               int nrows, int n_src_rows, void* out,
+                               int out_bf16, int32_t* status) {
+  const int r = blockIdx.y;
+  if (r >= nrows) return;
+  const int src = rows ? rows[r] : r;
+  if (src < 0 || src >= n_src_rows) {
+    if (threadIdx.x == 0 && blockIdx.x == 0)
+      set_status(status, SLX_ERR_OUT_OF_RANGE);
+    return;
+  }
+  const int per = 32 / bits;
+  const int wpr = in / per;
+  const int ng = in / gs;
+  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < in;
+       c += gridDim.x * blockDim.x) {
+    const uint32_t word = w[(size_t)src * wpr + c / per];
+    const uint32_t q = (word >> ((c % per) * bits)) & ((1u << bits) - 1u);
+    const float sc = bf16_to_f32(s[(size_t)src * ng + c / gs]);
+    const float bi = bf16_to_f32(b[(size_t)src * ng + c / gs]);
+    const float v = fmaf(sc, (float)q, bi);
+    if (out_bf16)
+      reinterpret_cast<uint16_t*>(out)[(size_t)r * in + c] = f32_to_bf16(v);
+    else
+      reinterpret_cast<float*>(out)[(size_t)r * in + c] = v;
+  }
+}
+
+int launch_dequant_rows(const uint32_t* w, const uint16_t* s, const uint16_t* b,
+                        int in, int bits, int gs, const int32_t* rows,
+                        int nrows, int n_src_rows, void* out, int out_bf16,
+                        int32_t* status, cudaStream_t stream) {
+  if (nrows <= 0) return SLX_OK;
+  if (nrows > 65535) return SLX_ERR_INVALID;
+  dim3 grid((in + 255) / 256, nrows);
+  k_dequant_rows<<<grid, 256, 0, stream>>>(w, s, b, in, bits, gs, rows, nrows,
+                                           n_src_rows, out, out_bf16, status);
+  return cudaGetLastError() == cudaSuccess ? SLX_OK : SLX_ERR_CUDA;
+}
+
+}  // namespace slx
