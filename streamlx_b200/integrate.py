@@ -1,0 +1,472 @@
+"""Model integration: a pool-backed SwitchGLU replacement and the loader.
+
+Mirrors ``streamlx/integrate.py``:
+
+* ``StreamingSwitchGLU(pool)`` is call-compatible with
+  ``SwitchGLU.__call__(x, indices) -> [B, T, k, H]`` (per-expert outputs
+  before score weighting, integrate.py:234-298).  ``fused(x, scores,
+  indices)`` additionally returns the score-weighted combine ``[B, T, H]``
+  (+ shared expert) from the same fused kernel -- the path the decoder uses.
+* Per call, the pool bookkeeping follows the reference exactly (it decides
+  the hit/miss/eviction trace): decode = ``B*T == 1``; one host sync on the
+  routed ids; ``prefetch_absorb`` first; then the hits of the call are
+  touched before the misses are ensured when both exist
+  (``_overlapped``, integrate.py:97-139), else ``ensure(uniq)``; then the
+  next layer's prefetch is started with the predicted ids ordered by score
+  (integrate.py:255-260).  Prediction gates itself off once 512 routed ids
+  were tallied at < 55% agreement (integrate.py:76-77).
+* Prefill whose expert union exceeds the pool runs the expert-major sweep
+  (``STREAMLX_PREFILL=sweep``, default; integrate.py:141-232): pairs grouped
+  by expert, ``STREAMLX_SWEEP_BATCH`` experts per batch in ascending id,
+  read one batch ahead on a worker thread, the ``n_slots`` most-routed
+  experts adopted into the pool (``STREAMLX_SWEEP_WARM``) and retouched so
+  the most frequent ends most-recently-used.  ``STREAMLX_PREFILL=slice`` is
+  the legacy token-slice path (integrate.py:269-298).
+* ``load_streaming_model`` returns ``(model, tokenizer, pools, reader)``
+  with the per-layer budget split ``max(k, budget_left / n_streamed /
+  bytes_per_expert)`` (integrate.py:397-473); ``STREAMLX_PREFETCH=0``
+  disables the next-layer prediction links.
+
+The B200 difference is below the bookkeeping: every resident expert of a
+call is computed by ONE fused kernel launch that maps expert ids to slots on
+the device, after the misses of the call have landed in their slots.
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+import time
+from concurrent.futures import ThreadPoolExecutor
+
+import numpy as np
+
+from .pool import StreamingSwitchMLP
+from .reader import ExpertReader
+from .stindex import PARTS, PROJS, SafetensorsIndex
+
+_PF_EX = None
+
+
+def _pf_ex():
+    global _PF_EX
+    if _PF_EX is None:
+        _PF_EX = ThreadPoolExecutor(max_workers=1,
+                                    thread_name_prefix="streamlx-pf")
+    return _PF_EX
+
+
+class StreamingSwitchGLU:
+    """Pool-backed replacement for one MoE layer's SwitchGLU."""
+
+    def __init__(self, pool: StreamingSwitchMLP, shared=None):
+        self.pool = pool
+        self.shared = shared          # (slx_shared_expert, buffer, inter) or None
+        self.record_sink = None
+        self.prefill_mode = os.environ.get("STREAMLX_PREFILL", "sweep")
+        self.sweep_batch = int(os.environ.get("STREAMLX_SWEEP_BATCH", "16"))
+        self.sweep_warm = os.environ.get("STREAMLX_SWEEP_WARM", "1") != "0"
+        self._sweep_ex = None
+        # (next pool, predict(x) -> (ids, scores) numpy or None)
+        self._pf_next = None
+        self._mini = None
+
+    # -------------------------------------------------------- bookkeeping --
+
+    def _pf_pred(self, x, k):
+        nxt = self._pf_next
+        if nxt is None:
+            return None
+        pool_j, predict = nxt
+        if pool_j.pf_agree_tot >= 512 and pool_j.prefetch_agreement() < 0.55:
+            return None
+        try:
+            return predict(x)
+        except Exception:   # noqa: BLE001 - arch surprise: disable the link
+            self._pf_next = None
+            return None
+
+    def route(self, idx: np.ndarray, pred=None) -> str:
+        """Pool bookkeeping of one call (no device work except slot fills).
+        idx: [B, T, k] routed expert ids (host).  pred: next-layer
+        prediction (ids, scores) for decode, or None.  Returns "pool" when the
+        call's experts are resident, else the prefill mode to run."""
+        pool = self.pool
+        decode = idx.shape[0] * idx.shape[1] == 1
+        if self.record_sink is not None:
+            self.record_sink.append((pool.layer, idx.copy()))
+        flat = [int(e) for e in idx.reshape(-1).tolist()]
+        uniq = list(dict.fromkeys(flat))
+        pool.begin_call()
+        if decode:
+            pool.prefetch_absorb(uniq)
+        if len(uniq) <= pool.n_slots:
+            if decode:
+                hits = [e for e in uniq if pool.resident(e)]
+                miss = [e for e in uniq if not pool.resident(e)]
+                if hits and miss:
+                    pool.touch(hits)
+                    pool.ensure(miss)
+                else:
+                    pool.ensure(uniq)
+                if pred is not None and self._pf_next is not None:
+                    pi = np.asarray(pred[0]).reshape(-1)
+                    ps = np.asarray(pred[1]).reshape(-1)
+                    ordered = list(dict.fromkeys(
+                        int(pi[j]) for j in np.argsort(-ps, kind="stable")))
+                    self._pf_next[0].prefetch_start(ordered, _pf_ex())
+            else:
+                pool.ensure(uniq)
+            return "pool"
+        return self.prefill_mode
+
+    # ------------------------------------------------------------ compute --
+
+    def _host_ids(self, indices):
+        import torch
+        if isinstance(indices, torch.Tensor):
+            return indices.detach().to("cpu").numpy()
+        return np.asarray(indices)
+
+    def __call__(self, x, indices):
+        """Drop-in: per-expert outputs [B, T, k, H] (unweighted)."""
+        return self._run(x, None, indices)
+
+    def fused(self, x, scores, indices):
+        """Score-weighted combine [B, T, H] (+ shared expert)."""
+        return self._run(x, scores, indices)
+
+    def _run(self, x, scores, indices):
+        from . import ops
+        B, T, k = indices.shape
+        pred = self._pf_pred(x, k) if B * T == 1 else None
+        idx = self._host_ids(indices)          # the per-layer host sync
+        mode = self.route(idx, pred)
+        if mode == "pool":
+            return self._pool_compute(x, scores, indices, idx)
+        if mode == "sweep":
+            y = self._expert_sweep(x, idx)
+        else:
+            y = self._slice_prefill(x, idx)
+        if scores is None:
+            return y
+        return self._combine(x, y, scores)
+
+    def _pool_compute(self, x, scores, indices, idx):
+        from . import ops
+        pool = self.pool
+        B, T, k = idx.shape
+        x2d = ops.as_bf16_2d(x)
+        pool.sync_device()
+        ids = ops.as_ids_2d(indices, k, x2d.device)
+        sh = self.shared
+        y = ops.switchglu(pool.store.bank, x2d, ids, k,
+                          scores=None if scores is None else
+                          scores.reshape(-1, k).float().contiguous(),
+                          table=pool.store.table_dev,
+                          shared=sh[0] if sh else None, inter=pool.inter,
+                          shared_inter=sh[2] if sh else 0)
+        if scores is None:
+            return y.reshape(B, T, k, -1)
+        return y.reshape(B, T, -1)
+
+    def _combine(self, x, y, scores):
+        """Score-weighted sum of per-expert outputs (+ shared expert) for the
+        prefill paths."""
+        import torch
+
+        from . import ops
+        B, T, k, H = y.shape
+        acc = (y.float() * scores.reshape(B, T, k, 1).float()).sum(-2)
+        if self.shared is not None:
+            _, sh_buf, sh_inter = self.shared
+            x2d = ops.as_bf16_2d(x)
+            zero_ids = torch.zeros(x2d.shape[0], 1, dtype=torch.int32,
+                                   device=x2d.device)
+            ys = ops.switchglu(shared_bank(sh_buf, self.pool, sh_inter), x2d,
+                               zero_ids, 1, inter=sh_inter)
+            acc = acc + ys.reshape(B, T, H).float()
+        return acc.to(torch.bfloat16)
+
+    # ------------------------------------------------------ prefill paths --
+
+    def _mini_pool(self, n: int):
+        import torch
+
+        from . import _lib as L
+        pool = self.pool
+        stride = L.slot_stride(pool.hidden, pool.inter, pool.bits)
+        if self._mini is None or self._mini[0] < n:
+            buf = torch.empty(n * stride, dtype=torch.uint8,
+                              device=pool.store.pool.device)
+            self._mini = (n, buf, stride)
+        return self._mini
+
+    def _expert_sweep(self, x, idx):
+        """Expert-major prefill (streamlx/integrate.py:141-232)."""
+        import torch
+
+        from . import _lib as L
+        from . import ops
+        pool = self.pool
+        b, t, k = idx.shape
+        P = b * t
+        on_gpu = pool.store.__class__.__name__ == "HbmSlotStore"
+        x_rows = ops.as_bf16_2d(x) if on_gpu else None
+        flat = idx.reshape(-1).astype(np.int64)
+        row_of_pair = np.repeat(np.arange(P, dtype=np.int64), k)
+        order = np.argsort(flat, kind="stable")
+        sorted_e = flat[order]
+        uniq, starts = np.unique(sorted_e, return_index=True)
+        bounds = np.append(starts, sorted_e.size)
+        counts = bounds[1:] - bounds[:-1]
+        warm_ids: set = set()
+        if self.sweep_warm:
+            top = np.argsort(counts, kind="stable")[::-1][:pool.n_slots]
+            warm_ids = {int(uniq[i]) for i in top}
+        if self._sweep_ex is None:
+            self._sweep_ex = ThreadPoolExecutor(max_workers=1)
+        batches = [[int(e) for e in uniq[i0:i0 + self.sweep_batch]]
+                   for i0 in range(0, len(uniq), self.sweep_batch)]
+        fut = self._sweep_ex.submit(pool.reader.read_experts_raw,
+                                    pool.triples_loc, batches[0])
+        y_sorted = None
+        if on_gpu:
+            H = x_rows.shape[1]
+            y_sorted = torch.empty(sorted_e.size, H, dtype=torch.bfloat16,
+                                   device=x_rows.device)
+            nb, mini, stride = self._mini_pool(self.sweep_batch)
+        for bi, ids in enumerate(batches):
+            t0 = time.perf_counter()
+            raw = fut.result()
+            pool.sweep_fetch_s += time.perf_counter() - t0
+            if bi + 1 < len(batches):
+                fut = self._sweep_ex.submit(pool.reader.read_experts_raw,
+                                            pool.triples_loc, batches[bi + 1])
+            pool.sweep_experts += len(ids)
+            i0 = bi * self.sweep_batch
+            i1 = min(i0 + self.sweep_batch, len(uniq))
+            lo, hi = int(bounds[i0]), int(bounds[i1])
+            adopt_items = []
+            for e in ids:
+                if e in warm_ids:
+                    adopt_items.append((pool.adopt(e, None), e))
+            if y_sorted is not None:
+                store = pool.store
+                store.write_to(pool.reader, raw,
+                               [(mini.data_ptr() + j * stride, e)
+                                for j, e in enumerate(ids)], release=False)
+                sel = order[lo:hi]
+                slot = np.searchsorted(uniq[i0:i1], sorted_e[lo:hi])
+                xb = x_rows[torch.as_tensor(row_of_pair[sel],
+                                            device=x_rows.device)]
+                sid = torch.as_tensor(slot.astype(np.int32),
+                                      device=x_rows.device).reshape(-1, 1)
+                bank = L.bank_struct(mini, len(ids), pool.hidden, pool.inter,
+                                     pool.bits, stride)
+                y_sorted[lo:hi] = ops.switchglu(
+                    bank, xb.contiguous(), sid, 1,
+                    inter=pool.inter).reshape(hi - lo, H)
+            pool.store.write(pool.reader, raw, adopt_items)
+        if warm_ids:
+            for i in np.argsort(counts, kind="stable"):
+                e = int(uniq[i])
+                if e in warm_ids and e in pool.id2slot:
+                    pool.id2slot.move_to_end(e)
+        if y_sorted is None:
+            return None
+        inv = np.empty_like(order)
+        inv[order] = np.arange(order.size)
+        y = y_sorted[torch.as_tensor(inv, device=y_sorted.device)]
+        return y.reshape(b, t, k, H)
+
+    def _slice_prefill(self, x, idx):
+        """Legacy token-slice prefill (streamlx/integrate.py:269-298)."""
+        import torch
+
+        from . import ops
+        pool = self.pool
+        b, t, k = idx.shape
+        flat = idx.reshape(-1, k)
+        on_gpu = pool.store.__class__.__name__ == "HbmSlotStore"
+        x_flat = ops.as_bf16_2d(x) if on_gpu else None
+        outs = []
+        s, P = 0, flat.shape[0]
+        while s < P:
+            union: set = set()
+            e = s
+            while e < P:
+                nxt = union | set(flat[e].tolist())
+                if len(nxt) > pool.n_slots:
+                    break
+                union = nxt
+                e += 1
+            if e == s:
+                raise RuntimeError(f"k > n_slots (layer {pool.layer})")
+            ids = list(dict.fromkeys(flat[s:e].reshape(-1).tolist()))
+            pool.ensure(ids)
+            if on_gpu:
+                pool.sync_device()
+                sl = ops.as_ids_2d(flat[s:e], k, x_flat.device)
+                y = ops.switchglu(pool.store.bank, x_flat[s:e].contiguous(), sl,
+                                  k, table=pool.store.table_dev,
+                                  inter=pool.inter)
+                torch.cuda.current_stream().synchronize()
+                outs.append(y)
+            s = e
+        if not outs:
+            return None
+        return torch.cat(outs, 0).reshape(b, t, k, -1)
+
+
+def shared_bank(sh_buf, pool, sh_inter):
+    """Bank view of a shared expert buffer (one slot)."""
+    from . import _lib as L
+    return L.bank_struct(sh_buf, 1, pool.hidden, sh_inter, pool.bits,
+                         L.slot_stride(pool.hidden, sh_inter, pool.bits))
+
+
+def install_streaming(model, model_dir: str, n_slots: int):
+    """Swap every MoE layer's switch_mlp for a streaming wrapper; returns
+    (pools, reader), the reader shared by all pools (integrate.py:301-319)."""
+    index = SafetensorsIndex(model_dir)
+    reader = ExpertReader(index)
+    pools: dict = {}
+    for i, layer in enumerate(model.layers):
+        mlp = getattr(layer, "mlp", None)
+        if mlp is None or not hasattr(mlp, "switch_mlp"):
+            continue
+        pool = StreamingSwitchMLP(model_dir, i, n_slots, index=index,
+                                  reader=reader)
+        layer.mlp.switch_mlp = StreamingSwitchGLU(pool, mlp.shared_struct())
+        pools[i] = pool
+    if not pools:
+        raise RuntimeError("no MoE layers found to wrap")
+    model.link_prefetch(pools)
+    return pools, reader
+
+
+def plan_residency(layers: list, bpe: dict, n_exp: dict, budget_bytes: int,
+                   k: int) -> tuple[set, float]:
+    """Greedy water-fill of fully resident layers (integrate.py:322-346)."""
+    resident: set = set()
+    streamed = list(layers)
+    left = float(budget_bytes)
+    for i in sorted(layers, key=lambda j: n_exp[j] * bpe[j]):
+        full = n_exp[i] * bpe[i]
+        min_rest = sum(k * bpe[j] for j in streamed if j != i)
+        if left / len(streamed) >= full and left - full >= min_rest:
+            resident.add(i)
+            streamed.remove(i)
+            left -= full
+    return resident, left
+
+
+class IdTokenizer:
+    """Tokenizer of the synthetic checkpoints: ids are the text."""
+
+    eos_token_ids: set = set()
+
+    def encode(self, ids):
+        return [int(i) for i in ids]
+
+    def decode(self, ids):
+        return " ".join(str(int(i)) for i in ids)
+
+
+def load_streaming_model(model_dir: str, budget_bytes: int, k: int = 8,
+                         trust_remote_code: bool = False,
+                         tokenizer_config: dict | None = None,
+                         resident: str | None = None, device=None):
+    """Build the decoder with every MoE layer pool-backed.  Returns
+    ``(model, tokenizer, pools, reader)`` (integrate.py:397-473)."""
+    from .model import SynthDecoder
+    index = SafetensorsIndex(model_dir)
+    reader = ExpertReader(index)
+    model = SynthDecoder.from_checkpoint(model_dir, index, device=device)
+    moe_layers = list(range(model.cfg.layers))
+    bpe = {i: index.layer_expert_bytes(i) for i in moe_layers}
+    n_exp = {i: index.switch_triples(i)["gate_proj"]["weight"].shape[0]
+             for i in moe_layers}
+    mode = resident if resident is not None else os.environ.get(
+        "STREAMLX_RESIDENT", "off")
+    res_layers: set = set()
+    budget_left = float(budget_bytes)
+    if mode not in ("off", "0"):
+        res_layers, budget_left = plan_residency(moe_layers, bpe, n_exp,
+                                                 budget_bytes, k)
+    streamed = [i for i in moe_layers if i not in res_layers]
+    pools: dict = {}
+    for i in moe_layers:
+        if i in res_layers:
+            slots = n_exp[i]
+        else:
+            slots = max(k, int(budget_left / len(streamed) / bpe[i]))
+        pool = StreamingSwitchMLP(model_dir, i, slots, index=index,
+                                  reader=reader, device=model.device)
+        if i in res_layers:   # fully resident: fill every slot once
+            pool.begin_call()
+            pool.ensure(list(range(n_exp[i])))
+        model.layers[i].mlp.switch_mlp = StreamingSwitchGLU(
+            pool, model.layers[i].mlp.shared_struct())
+        pools[i] = pool
+    if os.environ.get("STREAMLX_PREFETCH", "1") != "0":
+        linked = model.link_prefetch({i: pools[i] for i in streamed})
+        if linked:
+            print(f"[streamlx] attention-window prefetch: {linked} layer "
+                  f"links", file=sys.stderr)
+    if res_layers:
+        rb = sum(n_exp[i] * bpe[i] for i in res_layers) / 2**30
+        print(f"[streamlx] {len(res_layers)} fully-resident MoE layers "
+              f"({rb:.1f} GiB); {len(streamed)} streamed", file=sys.stderr)
+    return model, IdTokenizer(), pools, reader
+
+
+def preload_popular(pools: dict, trace_npz: str) -> int:
+    """Warm-start each pool with its layer's most-routed experts from a
+    routing trace (integrate.py:476-506)."""
+    import json
+    from pathlib import Path
+    d = np.load(trace_npz)
+    e = d["experts"]
+    p = Path(trace_npz)
+    side = p.parent / (p.stem + ".meta.json")
+    if side.exists():
+        layer_ids = json.loads(side.read_text())["layer_ids"]
+    else:
+        layer_ids = list(range(e.shape[1]))
+    axis_of = {int(lid): i for i, lid in enumerate(layer_ids)}
+    total = 0
+    for lid, pool in pools.items():
+        ax = axis_of.get(lid)
+        if ax is None:
+            continue
+        col = e[:, ax, :].ravel()
+        col = col[col != 0xFFFF]
+        hist = np.bincount(col, minlength=pool.n_experts)
+        top = np.argsort(hist)[::-1][: pool.n_slots]
+        pool.begin_call()
+        pool.ensure(sorted(int(x) for x in top))
+        total += len(top)
+    return total
+
+
+def aggregate_stats(pools: dict) -> dict:
+    """Sum of the pool counters (integrate.py:509-526)."""
+    tot = {"hits": 0, "misses": 0, "evictions": 0, "fetch_s": 0.0,
+           "sweep_experts": 0, "sweep_fetch_s": 0.0, "adopted": 0,
+           "pf_calls": 0, "pf_launched": 0, "pf_used": 0,
+           "pf_agree_hit": 0, "pf_agree_tot": 0}
+    for p in pools.values():
+        s = p.stats
+        for key in ("hits", "misses", "evictions", "sweep_experts", "adopted",
+                    "pf_calls", "pf_launched", "pf_used", "pf_agree_hit",
+                    "pf_agree_tot"):
+            tot[key] += s.get(key, 0)
+        tot["fetch_s"] += s["fetch_s"]
+        tot["sweep_fetch_s"] += s.get("sweep_fetch_s", 0.0)
+    acc = tot["hits"] + tot["misses"]
+    tot["miss_rate"] = tot["misses"] / acc if acc else 0.0
+    tot["fetch_s"] = round(tot["fetch_s"], 3)
+    tot["sweep_fetch_s"] = round(tot["sweep_fetch_s"], 3)
+    return tot

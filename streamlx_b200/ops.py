@@ -1,0 +1,82 @@
+"""Kernel-calling helpers around the pools (device side of the wrapper)."""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib as L
+
+_scratch: dict = {}
+
+
+def _status(device) -> torch.Tensor:
+    key = ("status", device)
+    t = _scratch.get(key)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=device)
+        _scratch[key] = t
+    return t
+
+
+def scratch(nbytes: int, device, tag: str = "glu") -> torch.Tensor:
+    """Grow-only device scratch shared by calls on one device."""
+    key = (tag, device)
+    t = _scratch.get(key)
+    if t is None or t.numel() < nbytes:
+        t = torch.empty(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
+        _scratch[key] = t
+    return t
+
+
+def check_status(device) -> None:
+    """Raise if a kernel recorded a device-side error (synchronises)."""
+    st = _status(device)
+    v = int(st.item())
+    if v != 0:
+        st.zero_()
+        raise L.SlxError("device", v, "device-side error status")
+
+
+def as_bf16_2d(x: torch.Tensor) -> torch.Tensor:
+    x = x.reshape(-1, x.shape[-1])
+    if x.dtype != torch.bfloat16:
+        x = x.to(torch.bfloat16)
+    return x.contiguous()
+
+
+def as_ids_2d(ids, k: int, device) -> torch.Tensor:
+    if not isinstance(ids, torch.Tensor):
+        ids = torch.as_tensor(ids)
+    ids = ids.reshape(-1, k)
+    if ids.dtype != torch.int32 or ids.device != device:
+        ids = ids.to(device=device, dtype=torch.int32)
+    return ids.contiguous()
+
+
+def switchglu(bank, x2d: torch.Tensor, ids2d: torch.Tensor, k: int, *,
+              scores: torch.Tensor | None = None, table: torch.Tensor | None = None,
+              shared=None, out: torch.Tensor | None = None,
+              inter: int, shared_inter: int = 0) -> torch.Tensor:
+    """One fused SwitchGLU launch pair.  scores None -> [T, k, H] per-expert
+    unweighted outputs; else [T, H] combined (+ shared expert)."""
+    T, H = x2d.shape
+    dev = x2d.device
+    if out is None:
+        shape = (T, H) if scores is not None else (T, k, H)
+        out = torch.empty(shape, dtype=torch.bfloat16, device=dev)
+    sI = shared_inter if (scores is not None and shared is not None) else 0
+    sc = scratch(L.switchglu_scratch_bytes(T, k, inter, sI), dev)
+    L.switchglu(bank, x2d, ids2d, out, sc, _status(dev), scores=scores,
+                slot_table=table, shared=shared if sI else None)
+    return out
+
+
+def switch_forward_ids(pool, x, expert_ids) -> torch.Tensor:
+    """streamlx/pool.py:299-304 on the pool: per-expert outputs [1,1,k,H]."""
+    k = len(expert_ids)
+    x2d = as_bf16_2d(x)
+    pool.sync_device()
+    ids = as_ids_2d(list(expert_ids), k, x2d.device)
+    y = switchglu(pool.store.bank, x2d, ids, k, table=pool.store.table_dev,
+                  inter=pool.inter)
+    return y.reshape(1, 1, k, -1)

@@ -189,7 +189,9 @@ class _ShardWriter:
             off += n
         hdr["__metadata__"] = {"format": "mlx"}
         raw = json.dumps(hdr, separators=(",", ":")).encode()
-        raw += b" " * ((-len(raw)) % 8)
+        # pad so tensor data starts 256-byte aligned in the file (safetensors
+        # allows trailing spaces in the header)
+        raw += b" " * ((-(len(raw) + 8)) % 256)
         self.f = open(path, "wb")
         self.f.write(struct.pack("<Q", len(raw)))
         self.f.write(raw)

@@ -1,0 +1,139 @@
+"""End-to-end GPU parity: pool-backed decoder vs the CPU oracle decoder, the
+pool's drop-in SwitchGLU call, and the expert-major prefill sweep vs the
+reference-composed outputs in tests/golden."""
+
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import affine as A
+from oracle.model import OracleDecoder
+from streamlx_b200 import synth
+from streamlx_b200.integrate import (StreamingSwitchGLU, aggregate_stats,
+                                     load_streaming_model)
+from streamlx_b200.pool import StreamingSwitchMLP
+from streamlx_b200.reader import ExpertReader
+from streamlx_b200.stindex import SafetensorsIndex
+
+from .kernel_cases import bf16_np, bf16_tensor, check_close
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+@pytest.fixture(scope="module")
+def tiny(tmp_path_factory):
+    root = tmp_path_factory.mktemp("models")
+    return {name: synth.write_model(str(root / name), synth.PRESETS[name],
+                                    seed=5)
+            for name in ("tiny_dec", "tiny_dec2")}
+
+
+def _margin_ok(logits: np.ndarray, ids: np.ndarray, k: int) -> bool:
+    """Routing is well conditioned when the k-th and (k+1)-th logits differ
+    by more than the bf16 noise of the router input."""
+    s = np.sort(logits)[::-1]
+    return (s[k - 1] - s[k]) > 2e-3
+
+
+@pytest.mark.parametrize("name,slots", [("tiny_dec", 6), ("tiny_dec2", 5)])
+def test_decoder_matches_oracle(tiny, name, slots, monkeypatch):
+    monkeypatch.setenv("STREAMLX_EVICT", "lru")
+    d = tiny[name]
+    cfg = synth.load_config(d)
+    bpe = synth.expert_bytes(cfg.hidden, cfg.inter, cfg.expert_bits, 64)
+    model, tok, pools, reader = load_streaming_model(
+        d, budget_bytes=slots * bpe * cfg.layers, k=cfg.top_k)
+    assert all(p.n_slots == slots for p in pools.values())
+    sinks = []
+    for i in range(cfg.layers):
+        s = []
+        model.layers[i].mlp.switch_mlp.record_sink = s
+        sinks.append(s)
+    oracle = OracleDecoder(d)
+    rng = np.random.default_rng(0)
+    seq = rng.integers(0, cfg.vocab, 24)
+    worst_rel, agree, total = 0.0, 0, 0
+    prev = {}
+    for t, tk in enumerate(seq):
+        model.step(torch.tensor([int(tk)], dtype=torch.int32,
+                                device=model.device))
+        got_logits = bf16_np(model.logits)[0]
+        ids_gpu = [sinks[i][-1][1].reshape(-1) for i in range(cfg.layers)]
+        # the same temporal-reuse decisions as the GPU run
+        forced = {i: prev[i] for i in range(cfg.layers)
+                  if t > 0 and cfg.repeat_p and np.array_equal(ids_gpu[i],
+                                                                prev.get(i))}
+        want_logits, ids_cpu = oracle.step(int(tk), forced=forced)
+        for i in range(cfg.layers):
+            total += 1
+            agree += int(np.array_equal(np.sort(ids_gpu[i]),
+                                        np.sort(ids_cpu[i])))
+        prev = {i: ids_gpu[i] for i in range(cfg.layers)}
+        rel = A.rel_l2(got_logits, want_logits)
+        worst_rel = max(worst_rel, rel)
+        assert np.max(np.abs(got_logits - want_logits)) <= 2e-2 * max(
+            1.0, float(np.max(np.abs(want_logits)))), t
+    assert worst_rel <= 1e-2, worst_rel
+    assert agree >= total - 2, (agree, total)
+    st = aggregate_stats(pools)
+    assert st["misses"] > 0 and st["evictions"] > 0      # the pool streamed
+    assert st["hits"] + st["misses"] == 24 * cfg.layers * cfg.top_k
+    reader.close()
+
+
+def test_pool_dropin_call_matches_oracle(tiny):
+    d = tiny["tiny_dec"]
+    cfg = synth.load_config(d)
+    pool = StreamingSwitchMLP(d, 1, 6)
+    oracle = OracleDecoder(d)
+    rng = np.random.default_rng(3)
+    for step in range(6):
+        ids = [int(e) for e in rng.choice(cfg.n_experts, cfg.top_k,
+                                          replace=False)]
+        x = A.bf16_round(rng.standard_normal((1, cfg.hidden))
+                         .astype(np.float32))
+        y = pool(bf16_tensor(x)[None], ids)             # [1,1,k,H]
+        torch.cuda.synchronize()
+        want = np.stack([A.expert_forward(x, oracle.expert(1, e))[0]
+                         for e in ids])
+        check_close(bf16_np(y)[0, 0], want)
+    assert pool.misses > 0
+    pool.reader.close()
+
+
+@pytest.mark.parametrize("tag", ["sweep_lru_warm1", "sweep_lru_warm0",
+                                 "slice_lru_warm1"])
+def test_prefill_outputs_match_reference_composition(tmp_path, tag,
+                                                     monkeypatch):
+    """The reference's own _expert_sweep / slice path, run under the numpy
+    mlx stand-in, produced y_small / y_big (tests/golden); the GPU sweep
+    must give the same per-expert outputs."""
+    g = np.load(os.path.join(GOLD, "trace_prefill.npz"))
+    mode, pol, warm = tag.split("_")
+    monkeypatch.setenv("STREAMLX_EVICT", pol)
+    monkeypatch.setenv("STREAMLX_PREFILL", mode)
+    monkeypatch.setenv("STREAMLX_SWEEP_BATCH", "16")
+    monkeypatch.setenv("STREAMLX_SWEEP_WARM", warm[-1])
+    cfg = synth.SynthConfig(name="golden_e256", hidden=64, layers=3,
+                            n_experts=256, top_k=10, inter=64, expert_bits=2,
+                            zipf_s=1.1)
+    d = synth.write_model(str(tmp_path / "e256"), cfg, seed=3)
+    index = SafetensorsIndex(d)
+    pool = StreamingSwitchMLP(d, 1, 24, index=index,
+                              reader=ExpertReader(index))
+    w = StreamingSwitchGLU(pool)
+    xs = A.bf16_from_bits(g["xs"])
+    small = w(bf16_tensor(xs[:3])[None],
+              torch.as_tensor(g["small_ids"][None].astype(np.int32)).cuda())
+    big = w(bf16_tensor(xs)[None],
+            torch.as_tensor(g["pre_ids"][None].astype(np.int32)).cuda())
+    torch.cuda.synchronize()
+    check_close(bf16_np(small), g[f"{tag}__y_small"])
+    check_close(bf16_np(big), g[f"{tag}__y_big"])
+    assert pool.sweep_experts > 0 if mode == "sweep" else True
+    pool.reader.close()
