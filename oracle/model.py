@@ -21,8 +21,8 @@ from . import trunk as TR
 
 
 def read_checkpoint(model_dir: str) -> dict:
-    """All tensors of model-*.safetensors as numpy arrays (uint32 codes,
-    uint16 bf16 bits, float32)."""
+    """All tensors of model-*.safetensors as read-only memory-mapped numpy
+    arrays (uint32 codes, uint16 bf16 bits, float32)."""
     out = {}
     dt = {"U32": np.uint32, "BF16": np.uint16, "F32": np.float32}
     for shard in sorted(glob.glob(os.path.join(model_dir,
@@ -30,20 +30,24 @@ def read_checkpoint(model_dir: str) -> dict:
         with open(shard, "rb") as f:
             (hlen,) = struct.unpack("<Q", f.read(8))
             hdr = json.loads(f.read(hlen))
-            base = 8 + hlen
-            for name, info in hdr.items():
-                if name == "__metadata__":
-                    continue
-                a, b = info["data_offsets"]
-                f.seek(base + a)
-                out[name] = np.frombuffer(f.read(b - a),
-                                          dtype=dt[info["dtype"]]).reshape(
-                                              info["shape"])
+        base = 8 + hlen
+        mm = np.memmap(shard, dtype=np.uint8, mode="r")
+        for name, info in hdr.items():
+            if name == "__metadata__":
+                continue
+            a, b = info["data_offsets"]
+            out[name] = mm[base + a:base + b].view(
+                dt[info["dtype"]]).reshape(info["shape"])
     return out
 
 
 class OracleDecoder:
-    def __init__(self, model_dir: str, max_len: int = 256):
+    """exact=True: fp64 accumulation (the parity reference); exact=False:
+    fp32 BLAS accumulation like an fp32 CPU implementation would use (the
+    timed CPU baseline)."""
+
+    def __init__(self, model_dir: str, max_len: int = 256, exact: bool = True):
+        self.exact = exact
         with open(os.path.join(model_dir, "config.json")) as f:
             self.cfg = json.load(f)["streamlx_synthetic"]
         c = self.cfg
@@ -69,15 +73,46 @@ class OracleDecoder:
         return A.bf16_from_bits(self.t[name])
 
     def expert(self, layer: int, e: int) -> dict:
+        """Dequantised expert (cached for small models only)."""
         key = (layer, e)
+        hit = self._deq.get(key)
+        if hit is not None:
+            return hit
+        p = f"model.layers.{layer}.mlp.switch_mlp"
+        t = self.t
+        d = {proj: A.dequant(t[f"{p}.{proj}.weight"][e],
+                             t[f"{p}.{proj}.scales"][e],
+                             t[f"{p}.{proj}.biases"][e], self.ebits, 64)
+             for proj in ("gate_proj", "up_proj", "down_proj")}
+        if self.cfg["n_experts"] * self.L <= 4096:
+            self._deq[key] = d
+        return d
+
+    def embed_row(self, token: int) -> np.ndarray:
+        t = self.t
+        return A.dequant(t["model.embed_tokens.weight"][token],
+                         t["model.embed_tokens.scales"][token],
+                         t["model.embed_tokens.biases"][token], self.tbits,
+                         64)[None]
+
+    def mv(self, x: np.ndarray, w: np.ndarray) -> np.ndarray:
+        if self.exact:
+            return A.qmv(x, w)
+        return A.bf16_round(x.astype(np.float32) @ w.T)
+
+    def expert_fwd(self, x: np.ndarray, d: dict) -> np.ndarray:
+        if self.exact:
+            return A.expert_forward(x, d)
+        up = self.mv(x, d["up_proj"])
+        gate = self.mv(x, d["gate_proj"])
+        return self.mv(A.swiglu(gate, up), d["down_proj"])
+
+    def qkv_weight(self, p: str) -> np.ndarray:
+        key = p + ".qkv"
         if key not in self._deq:
-            p = f"model.layers.{layer}.mlp.switch_mlp"
-            t = self.t
-            self._deq[key] = {
-                proj: A.dequant(t[f"{p}.{proj}.weight"][e],
-                                t[f"{p}.{proj}.scales"][e],
-                                t[f"{p}.{proj}.biases"][e], self.ebits, 64)
-                for proj in ("gate_proj", "up_proj", "down_proj")}
+            self._deq[key] = np.concatenate(
+                [self.deq(f"{p}.self_attn.{n}_proj", self.tbits)
+                 for n in ("q", "k", "v")], 0)
         return self._deq[key]
 
     def moe(self, layer: int, m: np.ndarray, forced_ids=None):
@@ -87,13 +122,13 @@ class OracleDecoder:
         ids, sc, _ = A.router(m, self.t[f"{p}.gate.weight"],
                               self.t[f"{p}.gate.bias"], c["top_k"],
                               c["norm_topk_prob"], forced_ids=forced_ids)
-        y = np.stack([A.expert_forward(m, self.expert(layer, int(e)))[0]
+        y = np.stack([self.expert_fwd(m, self.expert(layer, int(e)))[0]
                       for e in ids[0]])[None]
         sh = None
         if c["shared_inter"]:
             d = {proj: self.deq(f"{p}.shared_expert.{proj}", self.tbits)
                  for proj in ("gate_proj", "up_proj", "down_proj")}
-            sh = A.expert_forward(m, d)
+            sh = self.expert_fwd(m, d)
         return A.moe_combine(y, sc, sh), ids[0], sc[0]
 
     def step(self, token: int, forced: dict | None = None):
@@ -102,16 +137,14 @@ class OracleDecoder:
         c = self.cfg
         H, hd, nq, nkv = c["hidden"], c["head_dim"], c["heads"], c["kv_heads"]
         eps = c["rms_eps"]
-        h = A.bf16_round(self.deq("model.embed_tokens", self.tbits)[token][None])
+        h = A.bf16_round(self.embed_row(token))
         delta = None
         routed = []
         for i in range(self.L):
             p = f"model.layers.{i}"
             h, x = TR.add_rmsnorm(h, delta, self.bf(f"{p}.input_layernorm.weight"),
                                   eps)
-            wq = np.concatenate([self.deq(f"{p}.self_attn.{n}_proj", self.tbits)
-                                 for n in ("q", "k", "v")], 0)
-            qkv = A.qmv(x, wq)[0]
+            qkv = self.mv(x, self.qkv_weight(p))[0]
             q = qkv[:nq * hd].reshape(nq, hd)
             k = qkv[nq * hd:(nq + nkv) * hd].reshape(nkv, hd)
             v = qkv[(nq + nkv) * hd:].reshape(nkv, hd)
@@ -125,7 +158,7 @@ class OracleDecoder:
             self.vc[i][self.pos] = v
             att = TR.attn_decode(qr, self.kc[i], self.vc[i], self.pos + 1, nq,
                                  nkv).reshape(1, -1)
-            o = A.qmv(att, self.deq(f"{p}.self_attn.o_proj", self.tbits))
+            o = self.mv(att, self.deq(f"{p}.self_attn.o_proj", self.tbits))
             h, m = TR.add_rmsnorm(h, o,
                                   self.bf(f"{p}.post_attention_layernorm.weight"),
                                   eps)
@@ -133,6 +166,6 @@ class OracleDecoder:
             delta, ids, _ = self.moe(i, m, None if fi is None else fi[None])
             routed.append(ids)
         h, x = TR.add_rmsnorm(h, delta, self.bf("model.norm.weight"), eps)
-        logits = A.qmv(x, self.deq("lm_head", self.tbits))[0]
+        logits = self.mv(x, self.deq("lm_head", self.tbits))[0]
         self.pos += 1
         return logits, routed

@@ -58,6 +58,14 @@ class SlxError(RuntimeError):
 
 _lib = None
 
+# Number of kernel launches issued through this binding (the bench reports
+# the launches inside its timed region).  slx_switchglu launches two kernels.
+LAUNCHES = [0]
+
+
+def _count(n: int = 1) -> None:
+    LAUNCHES[0] += n
+
 
 def lib() -> C.CDLL:
     """Load the shared object (raises if it is not built)."""
@@ -163,6 +171,7 @@ def pack_experts(experts: list, hidden: int, inter: int, bits: int,
     rc = lib().slx_pack_experts(G, U, D, n, hidden, inter, bits, P,
                                 stream_ptr(stream))
     _check("slx_pack_experts", rc)
+    _count(1)
 
 
 def pack_dense(w3, out_features: int, in_features: int, bits: int,
@@ -172,6 +181,7 @@ def pack_dense(w3, out_features: int, in_features: int, bits: int,
     rc = lib().slx_pack_dense(C.byref(m), out_features, in_features, bits,
                               dst.data_ptr(), stream_ptr(stream))
     _check("slx_pack_dense", rc)
+    _count(1)
 
 
 def bank_struct(pool: torch.Tensor, n_slots: int, hidden: int, inter: int,
@@ -204,6 +214,7 @@ def switchglu(bank: slx_expert_bank, x: torch.Tensor, ids: torch.Tensor,
         out.data_ptr(), scratch.data_ptr(), scratch.numel() * scratch.element_size(),
         status.data_ptr(), stream_ptr(stream))
     _check("slx_switchglu", rc)
+    _count(2)
 
 
 def qlinear(w_tiled: torch.Tensor, out_features: int, in_features: int,
@@ -214,6 +225,7 @@ def qlinear(w_tiled: torch.Tensor, out_features: int, in_features: int,
                            x.data_ptr(), T if T is not None else x.shape[0],
                            y.data_ptr(), status.data_ptr(), stream_ptr(stream))
     _check("slx_qlinear", rc)
+    _count(1)
 
 
 def dequant_rows(w3, in_features: int, bits: int, rows: torch.Tensor | None,
@@ -226,6 +238,7 @@ def dequant_rows(w3, in_features: int, bits: int, rows: torch.Tensor | None,
                                 1 if out.dtype == torch.bfloat16 else 0,
                                 status.data_ptr(), stream_ptr(stream))
     _check("slx_dequant_rows", rc)
+    _count(1)
 
 
 def router_scratch_bytes(T: int, E: int) -> int:
@@ -248,6 +261,7 @@ def router_topk(x: torch.Tensor, w_gate: torch.Tensor, bias, k: int,
         scratch.numel() * scratch.element_size(), status.data_ptr(),
         stream_ptr(stream))
     _check("slx_router_topk", rc)
+    _count(1)
 
 
 def add_rmsnorm(h, delta, weight, eps: float, y, stream=None) -> None:
@@ -255,6 +269,7 @@ def add_rmsnorm(h, delta, weight, eps: float, y, stream=None) -> None:
     rc = lib().slx_add_rmsnorm(h.data_ptr(), ptr(delta), weight.data_ptr(), T,
                                H, eps, y.data_ptr(), stream_ptr(stream))
     _check("slx_add_rmsnorm", rc)
+    _count(1)
 
 
 def qk_norm_rope_cache(qkv, n_q, n_kv, hd, q_norm, k_norm, eps, inv_freq,
@@ -265,6 +280,7 @@ def qk_norm_rope_cache(qkv, n_q, n_kv, hd, q_norm, k_norm, eps, inv_freq,
         k_cache.shape[0], k_cache.data_ptr(), v_cache.data_ptr(),
         status.data_ptr(), stream_ptr(stream))
     _check("slx_qk_norm_rope_cache", rc)
+    _count(1)
 
 
 def attn_decode(qkv, n_q, n_kv, hd, k_cache, v_cache, pos, out,
@@ -274,6 +290,7 @@ def attn_decode(qkv, n_q, n_kv, hd, k_cache, v_cache, pos, out,
                                pos.data_ptr(), k_cache.shape[0], out.data_ptr(),
                                stream_ptr(stream))
     _check("slx_attn_decode", rc)
+    _count(1)
 
 
 def argmax(logits, out, stream=None) -> None:
@@ -281,6 +298,7 @@ def argmax(logits, out, stream=None) -> None:
     rc = lib().slx_argmax(logits.data_ptr(), T, V, out.data_ptr(),
                           stream_ptr(stream))
     _check("slx_argmax", rc)
+    _count(1)
 
 
 def copy_many(dsts: list[int], srcs: list[int], sizes: list[int],

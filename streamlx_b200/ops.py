@@ -8,6 +8,10 @@ from . import _lib as L
 
 _scratch: dict = {}
 
+# When a list, every switchglu launch pair appends (start, end) CUDA events
+# recorded around it on the current stream (the bench's roofline timing).
+TIMING: list | None = None
+
 
 def _status(device) -> torch.Tensor:
     key = ("status", device)
@@ -66,8 +70,16 @@ def switchglu(bank, x2d: torch.Tensor, ids2d: torch.Tensor, k: int, *,
         out = torch.empty(shape, dtype=torch.bfloat16, device=dev)
     sI = shared_inter if (scores is not None and shared is not None) else 0
     sc = scratch(L.switchglu_scratch_bytes(T, k, inter, sI), dev)
+    ev = None
+    if TIMING is not None:
+        ev = (torch.cuda.Event(enable_timing=True),
+              torch.cuda.Event(enable_timing=True))
+        ev[0].record()
     L.switchglu(bank, x2d, ids2d, out, sc, _status(dev), scores=scores,
                 slot_table=table, shared=shared if sI else None)
+    if ev is not None:
+        ev[1].record()
+        TIMING.append((ev[0], ev[1], T, k, inter, sI))
     return out
 
 
