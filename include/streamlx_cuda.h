@@ -159,6 +159,25 @@ int slx_router_topk(const void* x, const void* ratio, const void* w_gate,
                     float* out_scores, void* scratch, size_t scratch_bytes,
                     int32_t* status, void* stream);
 
+/* Router GEMV + softmax + top-k exactly as slx_router_topk, for callers
+ * that hold no device allocator: a host binding that reaches the library
+ * only through this C ABI (ctypes, cgo, JNI) and would otherwise have to
+ * call cudaMalloc itself and track the buffer per device, or a serving loop
+ * that must not allocate device memory once it is warm.  No counterpart in
+ * the reference.  Scratch is a static device array inside the library:
+ * T <= 1024 and T * E <= 32768 (e.g. 128 tokens at 256 experts); larger
+ * calls return SLX_ERR_SCRATCH.  Nothing needs zeroing by the caller.  All
+ * calls on one device share that array, so calls that overlap (two streams,
+ * or two host threads) race: order them on one stream.  The first call on
+ * each device looks up the array's address (loading the module) and should
+ * come before any stream capture. */
+int slx_router_topk_noalloc(const void* x, const void* ratio,
+                            const void* w_gate, const float* bias, int T,
+                            int H, int E, int k, int norm_topk,
+                            const int32_t* force, const int32_t* forced_ids,
+                            int32_t* out_ids, float* out_scores,
+                            int32_t* status, void* stream);
+
 /* Trunk helpers (no reference counterpart; mlx-lm's model code). */
 int slx_add_rmsnorm(void* h, const void* delta, const void* weight, int T,
                     int H, float eps, void* y, void* stream);

@@ -31,7 +31,7 @@ EXPORTS = (
     "slx_switchglu", "slx_qlinear", "slx_dequant_rows",
     "slx_router_scratch_bytes", "slx_router_topk", "slx_add_rmsnorm",
     "slx_qk_norm_rope_cache", "slx_attn_decode", "slx_argmax",
-    "slx_copy_many",
+    "slx_copy_many", "slx_router_topk_noalloc",
 )
 
 
@@ -105,6 +105,9 @@ def lib() -> C.CDLL:
         L.slx_router_topk.restype = i32
         L.slx_router_topk.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, i32,
                                       vp, vp, vp, vp, vp, sz, vp, vp]
+        L.slx_router_topk_noalloc.restype = i32
+        L.slx_router_topk_noalloc.argtypes = [vp, vp, vp, vp, i32, i32, i32,
+                                              i32, i32, vp, vp, vp, vp, vp, vp]
         L.slx_add_rmsnorm.restype = i32
         L.slx_add_rmsnorm.argtypes = [vp, vp, vp, i32, i32, C.c_float, vp, vp]
         L.slx_qk_norm_rope_cache.restype = i32

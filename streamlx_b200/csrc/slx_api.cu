@@ -3,6 +3,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include <vector>
@@ -385,3 +386,62 @@ int slx_copy_many(void* const* dst, const void* const* src,
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Router without caller scratch.  The logits and the per-token tickets live
+// in this file's own static device array; the tickets start at zero (module
+// load) and every router launch leaves them zero.
+namespace {
+
+constexpr int kNoAllocLogits = 32768;   // max T * n_experts
+constexpr int kNoAllocTokens = 1024;    // max T
+constexpr size_t kNoAllocTicketOff = (size_t)kNoAllocLogits * 4;
+constexpr size_t kNoAllocBytes = kNoAllocTicketOff + (size_t)kNoAllocTokens * 4;
+constexpr int kNoAllocDevices = 64;
+
+static __device__ __align__(256) unsigned char g_router_scratch[kNoAllocBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kNoAllocDevices] = {};
+
+}  // namespace
+
+extern "C" int slx_router_topk_noalloc(
+    const void* x, const void* ratio, const void* w_gate, const float* bias,
+    int T, int H, int E, int k, int norm_topk, const int32_t* force,
+    const int32_t* forced_ids, int32_t* out_ids, float* out_scores,
+    int32_t* status, void* stream) {
+  g_err.clear();
+  if (T < 0 || E < 1) return fail(SLX_ERR_INVALID, "router_noalloc: T %d E %d", T, E);
+  if (T > kNoAllocTokens || (long long)T * E > kNoAllocLogits)
+    return fail(SLX_ERR_SCRATCH,
+                "router_noalloc: T %d x E %d exceeds the static scratch "
+                "(%d logits, %d tokens); use slx_router_topk with caller "
+                "scratch", T, E, kNoAllocLogits, kNoAllocTokens);
+  int dev = -1;
+  cudaError_t ce = cudaGetDevice(&dev);
+  if (ce != cudaSuccess)
+    return fail(SLX_ERR_CUDA, "router_noalloc: %s", cudaGetErrorString(ce));
+  if (dev < 0 || dev >= kNoAllocDevices)
+    return fail(SLX_ERR_UNSUPPORTED, "router_noalloc: device %d", dev);
+  void* base;
+  {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+      void* p = nullptr;
+      ce = cudaGetSymbolAddress(&p, g_router_scratch);
+      if (ce != cudaSuccess || !p)
+        return fail(SLX_ERR_CUDA, "router_noalloc: symbol address: %s",
+                    cudaGetErrorString(ce));
+      g_noalloc_addr[dev] = p;
+    }
+    base = g_noalloc_addr[dev];
+  }
+  // slx_router_topk puts the tickets right after the 256-aligned logits;
+  // start the logits so that the tickets land on the fixed ticket words.
+  const size_t logit_bytes = align256((size_t)T * E * 4);
+  unsigned char* scr = (unsigned char*)base + kNoAllocTicketOff - logit_bytes;
+  return slx_router_topk(x, ratio, w_gate, bias, T, H, E, k, norm_topk, force,
+                         forced_ids, out_ids, out_scores, scr,
+                         slx_router_scratch_bytes(T, E), status, stream);
+}
