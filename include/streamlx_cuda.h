@@ -181,6 +181,11 @@ int slx_router_topk_noalloc(const void* x, const void* ratio,
 /* Trunk helpers (no reference counterpart; mlx-lm's model code). */
 int slx_add_rmsnorm(void* h, const void* delta, const void* weight, int T,
                     int H, float eps, void* y, void* stream);
+/* h_out = h_in + delta (delta nullable), y = RMSNorm(h_out) * weight; all
+ * operands 16-byte aligned, H % 8 == 0, H <= 8192; h_out may alias h_in. */
+int slx_add_rmsnorm_out(const void* h_in, const void* delta,
+                        const void* weight, int T, int H, float eps,
+                        void* h_out, void* y, void* stream);
 int slx_qk_norm_rope_cache(void* qkv, int T, int n_q, int n_kv, int head_dim,
                            const void* q_norm, const void* k_norm, float eps,
                            const float* inv_freq, const int32_t* pos,
@@ -197,6 +202,14 @@ int slx_argmax(const void* logits, int T, int V, int32_t* out, void* stream);
  * pinned staging -> HBM). */
 int slx_copy_many(void* const* dst, const void* const* src,
                   const size_t* bytes, int n, void* stream);
+
+/* Timing helpers for graph-launched steps: record a CUDA event on a
+ * stream -- as a timestamp node (cudaEventRecordExternal) while the stream
+ * is being captured, as a plain record otherwise; read n start/end event
+ * pairs in one call. */
+int slx_event_record_external(void* event, void* stream);
+int slx_event_elapsed_many(void* const* start, void* const* end, int n,
+                           float* out_ms);
 
 #ifdef __cplusplus
 }

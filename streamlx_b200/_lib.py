@@ -10,6 +10,7 @@ from __future__ import annotations
 import ctypes as C
 import os
 
+import numpy as np
 import torch
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
@@ -31,7 +32,8 @@ EXPORTS = (
     "slx_switchglu", "slx_qlinear", "slx_dequant_rows",
     "slx_router_scratch_bytes", "slx_router_topk", "slx_add_rmsnorm",
     "slx_qk_norm_rope_cache", "slx_attn_decode", "slx_argmax",
-    "slx_copy_many", "slx_router_topk_noalloc",
+    "slx_copy_many", "slx_router_topk_noalloc", "slx_add_rmsnorm_out",
+    "slx_event_record_external", "slx_event_elapsed_many",
 )
 
 
@@ -110,6 +112,14 @@ def lib() -> C.CDLL:
                                               i32, i32, vp, vp, vp, vp, vp, vp]
         L.slx_add_rmsnorm.restype = i32
         L.slx_add_rmsnorm.argtypes = [vp, vp, vp, i32, i32, C.c_float, vp, vp]
+        L.slx_add_rmsnorm_out.restype = i32
+        L.slx_add_rmsnorm_out.argtypes = [vp, vp, vp, i32, i32, C.c_float, vp,
+                                          vp, vp]
+        L.slx_event_record_external.restype = i32
+        L.slx_event_record_external.argtypes = [vp, vp]
+        L.slx_event_elapsed_many.restype = i32
+        L.slx_event_elapsed_many.argtypes = [C.POINTER(vp), C.POINTER(vp), i32,
+                                             C.POINTER(C.c_float)]
         L.slx_qk_norm_rope_cache.restype = i32
         L.slx_qk_norm_rope_cache.argtypes = [vp, i32, i32, i32, i32, vp, vp,
                                              C.c_float, vp, vp, i32, vp, vp,
@@ -273,6 +283,34 @@ def add_rmsnorm(h, delta, weight, eps: float, y, stream=None) -> None:
                                H, eps, y.data_ptr(), stream_ptr(stream))
     _check("slx_add_rmsnorm", rc)
     _count(1)
+
+
+def add_rmsnorm_out(h_in, delta, weight, eps: float, h_out, y,
+                    stream=None) -> None:
+    T, H = h_in.shape[-2], h_in.shape[-1]
+    rc = lib().slx_add_rmsnorm_out(h_in.data_ptr(), ptr(delta),
+                                   weight.data_ptr(), T, H, eps,
+                                   h_out.data_ptr(), y.data_ptr(),
+                                   stream_ptr(stream))
+    _check("slx_add_rmsnorm_out", rc)
+    _count(1)
+
+
+def event_record_external(event: torch.cuda.Event, stream=None) -> None:
+    """Record `event` as a timestamp node (usable inside stream capture)."""
+    rc = lib().slx_event_record_external(event.cuda_event, stream_ptr(stream))
+    _check("slx_event_record_external", rc)
+
+
+def event_elapsed_many(starts, ends) -> np.ndarray:
+    """Elapsed ms of n (start, end) event pairs (both already completed)."""
+    n = len(starts)
+    a = (C.c_void_p * n)(*[e.cuda_event for e in starts])
+    b = (C.c_void_p * n)(*[e.cuda_event for e in ends])
+    out = (C.c_float * n)()
+    rc = lib().slx_event_elapsed_many(a, b, n, out)
+    _check("slx_event_elapsed_many", rc)
+    return np.frombuffer(out, dtype=np.float32).copy()
 
 
 def qk_norm_rope_cache(qkv, n_q, n_kv, hd, q_norm, k_norm, eps, inv_freq,

@@ -320,14 +320,54 @@ int slx_router_topk(const void* x, const void* ratio, const void* w_gate,
   return rc ? cuda_check(rc, "slx_router_topk") : SLX_OK;
 }
 
+int slx_add_rmsnorm_out(const void* h_in, const void* delta,
+                        const void* weight, int T, int H, float eps,
+                        void* h_out, void* y, void* stream) {
+  g_err.clear();
+  if (!h_in || !weight || !y || !h_out) return fail(SLX_ERR_INVALID, "rmsnorm: NULL");
+  if (!aligned16(h_in) || !aligned16(h_out) || !aligned16(weight) ||
+      !aligned16(y) || (delta && !aligned16(delta)))
+    return fail(SLX_ERR_INVALID, "rmsnorm: operands must be 16-byte aligned");
+  const int rc = slx::launch_add_rmsnorm(
+      (const uint16_t*)h_in, (const uint16_t*)delta, (const uint16_t*)weight,
+      T, H, eps, (uint16_t*)h_out, (uint16_t*)y,
+      reinterpret_cast<cudaStream_t>(stream));
+  return rc ? cuda_check(rc, "slx_add_rmsnorm") : SLX_OK;
+}
+
 int slx_add_rmsnorm(void* h, const void* delta, const void* weight, int T,
                     int H, float eps, void* y, void* stream) {
+  return slx_add_rmsnorm_out(h, delta, weight, T, H, eps, h, y, stream);
+}
+
+int slx_event_record_external(void* event, void* stream) {
   g_err.clear();
-  if (!h || !weight || !y) return fail(SLX_ERR_INVALID, "rmsnorm: NULL");
-  const int rc = slx::launch_add_rmsnorm(
-      (uint16_t*)h, (const uint16_t*)delta, (const uint16_t*)weight, T, H, eps,
-      (uint16_t*)y, reinterpret_cast<cudaStream_t>(stream));
-  return rc ? cuda_check(rc, "slx_add_rmsnorm") : SLX_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaError_t e = cudaStreamIsCapturing(s, &cs);
+  if (e != cudaSuccess)
+    return fail(SLX_ERR_CUDA, "event record: %s", cudaGetErrorString(e));
+  // outside a capture the flag is not accepted; a plain record is the same
+  e = cs == cudaStreamCaptureStatusActive
+          ? cudaEventRecordWithFlags(reinterpret_cast<cudaEvent_t>(event), s,
+                                     cudaEventRecordExternal)
+          : cudaEventRecord(reinterpret_cast<cudaEvent_t>(event), s);
+  return e == cudaSuccess ? SLX_OK
+                          : fail(SLX_ERR_CUDA, "event record: %s",
+                                 cudaGetErrorString(e));
+}
+
+int slx_event_elapsed_many(void* const* start, void* const* end, int n,
+                           float* out_ms) {
+  g_err.clear();
+  for (int i = 0; i < n; ++i) {
+    const cudaError_t e =
+        cudaEventElapsedTime(&out_ms[i], reinterpret_cast<cudaEvent_t>(start[i]),
+                             reinterpret_cast<cudaEvent_t>(end[i]));
+    if (e != cudaSuccess)
+      return fail(SLX_ERR_CUDA, "elapsed[%d]: %s", i, cudaGetErrorString(e));
+  }
+  return SLX_OK;
 }
 
 int slx_qk_norm_rope_cache(void* qkv, int T, int n_q, int n_kv, int head_dim,

@@ -95,8 +95,9 @@ int launch_pack_experts(const void* const* gw, const void* const* gs,
                         int I, int bits, cudaStream_t stream);
 int launch_pack_dense(const void* w, const void* s, const void* b, int out,
                       int in, int bits, void* dst, cudaStream_t stream);
-int launch_add_rmsnorm(uint16_t* h, const uint16_t* d, const uint16_t* w,
-                       int T, int H, float eps, uint16_t* y, cudaStream_t s);
+int launch_add_rmsnorm(const uint16_t* h_in, const uint16_t* d,
+                       const uint16_t* w, int T, int H, float eps,
+                       uint16_t* h_out, uint16_t* y, cudaStream_t s);
 int launch_qk_rope_cache(uint16_t* qkv, int T, int nq, int nkv, int hd,
                          const uint16_t* qn, const uint16_t* kn, float eps,
                          const float* inv_freq, const int32_t* pos,

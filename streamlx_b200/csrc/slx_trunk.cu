@@ -22,29 +22,66 @@ SLX_DEV T breduce(T v, T* red, Op op) {
   return r;
 }
 
-// h = bf16(h + d) (if d), y = bf16(h * rsqrt(mean(h^2) + eps) * w)
-__global__ void __launch_bounds__(256) k_add_rmsnorm(uint16_t* h,
-                                                     const uint16_t* d,
-                                                     const uint16_t* w, int H,
-                                                     float eps, uint16_t* y) {
+// h_out = bf16(h_in + d) (if d, else h_in), y = bf16(h_out * rsqrt(mean(
+// h_out^2) + eps) * w).  One CTA per token, 8 bf16 per thread per chunk (one
+// 16-byte load each), the row kept in registers between the two passes.
+// h_out may alias h_in.
+constexpr int kNormThreads = 256;
+constexpr int kNormMaxChunks = 4;   // H <= 8 * 256 * 4
+
+__global__ void __launch_bounds__(kNormThreads) k_add_rmsnorm(
+    const uint16_t* h_in, const uint16_t* d, const uint16_t* w, int H,
+    float eps, uint16_t* h_out, uint16_t* y) {
   __shared__ float red[32];
   const int t = blockIdx.x;
-  uint16_t* hr = h + (size_t)t * H;
+  const uint16_t* hr = h_in + (size_t)t * H;
   const uint16_t* dr = d ? d + (size_t)t * H : nullptr;
+  uint4 v[kNormMaxChunks];
   float ss = 0.f;
-  for (int c = threadIdx.x; c < H; c += blockDim.x) {
-    float v = bf16_to_f32(hr[c]);
+#pragma unroll
+  for (int j = 0; j < kNormMaxChunks; ++j) {
+    const int c = (j * kNormThreads + threadIdx.x) * 8;
+    if (c >= H) break;
+    uint4 a = *reinterpret_cast<const uint4*>(hr + c);
     if (dr) {
-      v = round_bf16(v + bf16_to_f32(dr[c]));
-      hr[c] = f32_to_bf16(v);
+      const uint4 b = *reinterpret_cast<const uint4*>(dr + c);
+      uint32_t* pa = reinterpret_cast<uint32_t*>(&a);
+      const uint32_t* pb = reinterpret_cast<const uint32_t*>(&b);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float lo = round_bf16(bf16_lo(pa[q]) + bf16_lo(pb[q]));
+        const float hi = round_bf16(bf16_hi(pa[q]) + bf16_hi(pb[q]));
+        pa[q] = (uint32_t)f32_to_bf16(lo) | ((uint32_t)f32_to_bf16(hi) << 16);
+      }
     }
-    ss += v * v;
+    if (dr || h_out != h_in)
+      *reinterpret_cast<uint4*>(h_out + (size_t)t * H + c) = a;
+    const uint32_t* pa = reinterpret_cast<const uint32_t*>(&a);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float lo = bf16_lo(pa[q]), hi = bf16_hi(pa[q]);
+      ss += lo * lo + hi * hi;
+    }
+    v[j] = a;
   }
   ss = breduce(ss, red, [](float a, float b) { return a + b; });
   const float inv = rsqrtf(ss / (float)H + eps);
-  for (int c = threadIdx.x; c < H; c += blockDim.x) {
-    const float v = bf16_to_f32(hr[c]);
-    y[(size_t)t * H + c] = f32_to_bf16(v * inv * bf16_to_f32(w[c]));
+#pragma unroll
+  for (int j = 0; j < kNormMaxChunks; ++j) {
+    const int c = (j * kNormThreads + threadIdx.x) * 8;
+    if (c >= H) break;
+    const uint4 wv = *reinterpret_cast<const uint4*>(w + c);
+    const uint32_t* pa = reinterpret_cast<const uint32_t*>(&v[j]);
+    const uint32_t* pw = reinterpret_cast<const uint32_t*>(&wv);
+    uint4 o;
+    uint32_t* po = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint16_t lo = f32_to_bf16(bf16_lo(pa[q]) * inv * bf16_lo(pw[q]));
+      const uint16_t hi = f32_to_bf16(bf16_hi(pa[q]) * inv * bf16_hi(pw[q]));
+      po[q] = (uint32_t)lo | ((uint32_t)hi << 16);
+    }
+    *reinterpret_cast<uint4*>(y + (size_t)t * H + c) = o;
   }
 }
 
@@ -174,11 +211,12 @@ __global__ void __launch_bounds__(1024) k_argmax(const uint16_t* logits,
   }
 }
 
-int launch_add_rmsnorm(uint16_t* h, const uint16_t* d, const uint16_t* w,
-                       int T, int H, float eps, uint16_t* y,
-                       cudaStream_t s) {
+int launch_add_rmsnorm(const uint16_t* h_in, const uint16_t* d,
+                       const uint16_t* w, int T, int H, float eps,
+                       uint16_t* h_out, uint16_t* y, cudaStream_t s) {
+  if (H % 8 || H > 8 * kNormThreads * kNormMaxChunks) return SLX_ERR_UNSUPPORTED;
   if (T <= 0) return SLX_OK;
-  k_add_rmsnorm<<<T, 256, 0, s>>>(h, d, w, H, eps, y);
+  k_add_rmsnorm<<<T, kNormThreads, 0, s>>>(h_in, d, w, H, eps, h_out, y);
   return cudaGetLastError() == cudaSuccess ? SLX_OK : SLX_ERR_CUDA;
 }
 

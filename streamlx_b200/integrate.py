@@ -73,13 +73,21 @@ class StreamingSwitchGLU:
 
     # -------------------------------------------------------- bookkeeping --
 
-    def _pf_pred(self, x, k):
+    def pred_gate(self) -> bool:
+        """Whether this call makes a next-layer prediction: a link exists
+        and the next pool's agreement has not fallen below 55% over 512+
+        routed ids (integrate.py:67-77)."""
         nxt = self._pf_next
         if nxt is None:
+            return False
+        pool_j = nxt[0]
+        return not (pool_j.pf_agree_tot >= 512 and
+                    pool_j.prefetch_agreement() < 0.55)
+
+    def _pf_pred(self, x, k):
+        if not self.pred_gate():
             return None
-        pool_j, predict = nxt
-        if pool_j.pf_agree_tot >= 512 and pool_j.prefetch_agreement() < 0.55:
-            return None
+        predict = self._pf_next[1]
         try:
             return predict(x)
         except Exception:   # noqa: BLE001 - arch surprise: disable the link
@@ -342,6 +350,9 @@ def install_streaming(model, model_dir: str, n_slots: int):
         pools[i] = pool
     if not pools:
         raise RuntimeError("no MoE layers found to wrap")
+    if hasattr(model, "flush"):
+        for pool in pools.values():
+            pool.flush_hook = model.flush
     model.link_prefetch(pools)
     return pools, reader
 
@@ -410,6 +421,8 @@ def load_streaming_model(model_dir: str, budget_bytes: int, k: int = 8,
         model.layers[i].mlp.switch_mlp = StreamingSwitchGLU(
             pool, model.layers[i].mlp.shared_struct())
         pools[i] = pool
+    for pool in pools.values():     # stats first finish deferred steps
+        pool.flush_hook = model.flush
     if os.environ.get("STREAMLX_PREFETCH", "1") != "0":
         linked = model.link_prefetch({i: pools[i] for i in streamed})
         if linked:

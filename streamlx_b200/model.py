@@ -79,6 +79,7 @@ class MoEBlock:
         self.pf_scores = torch.zeros(1, k, dtype=torch.float32, device=device)
         self.pf_scratch = torch.zeros(L.router_scratch_bytes(1, E),
                                       dtype=torch.uint8, device=device)
+        self.pf_link = None         # (ratio, next layer's MoEBlock)
 
     def shared_struct(self):
         return self.shared
@@ -153,6 +154,11 @@ class SynthDecoder:
             self.logits = torch.zeros(1, cfg.vocab, dtype=torch.bfloat16,
                                       device=dev)
         self.n_pos = 0
+        self.use_graphs = cfg.has_trunk
+        self.pipeline = True
+        self._graphs = None
+        self._pending = None
+        self.glu_times: list | None = None
         # temporal-reuse routing override of the workloads: per (token,
         # layer) a seeded coin decides whether the previous token's expert
         # set is kept (applied identically to the CPU oracle)
@@ -193,12 +199,15 @@ class SynthDecoder:
                         blk.pf_scores.cpu().numpy()[0])
 
             la.mlp.switch_mlp._pf_next = (pools[b], predict)
+            la.mlp.pf_link = (ratio.contiguous(), lb.mlp)
             linked += 1
+        self._graphs = None          # links changed: capture again
         return linked
 
     # -------------------------------------------------------------- decode --
 
     def reset(self) -> None:
+        self.flush()
         self.n_pos = 0
         self._rng = np.random.default_rng(12345)
 
@@ -214,7 +223,22 @@ class SynthDecoder:
     @torch.no_grad()
     def step(self, token: torch.Tensor) -> torch.Tensor:
         """One decode step for the token id in `token` (device int32 [1]);
-        returns the greedy next token (device int32 [1])."""
+        returns the greedy next token (device int32 [1]).
+
+        With ``use_graphs`` the step runs as captured CUDA graphs and the
+        pool bookkeeping follows from the device log (_step_graph); with
+        ``pipeline`` the bookkeeping of a step that needed no slot fill is
+        deferred to the next call (or flush()), where it overlaps that
+        call's device work."""
+        if self.use_graphs and all(
+                hasattr(la.mlp.switch_mlp, "route") for la in self.layers):
+            return self._step_graph(token)
+        self.flush()
+        return self._step_eager(token)
+
+    @torch.no_grad()
+    def _step_eager(self, token: torch.Tensor) -> torch.Tensor:
+        """Layer by layer, one host sync on the routed ids per layer."""
         cfg = self.cfg
         if self.n_pos >= self.max_len:
             raise RuntimeError("KV cache full")
@@ -247,6 +271,281 @@ class SynthDecoder:
         self.n_pos += 1
         return nxt
 
+    # ----------------------------------------------------- graph decode --
+    #
+    # A decode step runs as one CUDA graph per layer plus a tail graph, with
+    # no host sync between layers.  The host then replays every layer's pool
+    # bookkeeping from a device log (routed ids, next-layer prediction), in
+    # layer order, through the wrapper's route() -- the same calls, in the
+    # same order, as the eager path, so the hit/miss/eviction trace is the
+    # same.  A layer computed correctly iff every routed expert had a slot
+    # when its SwitchGLU ran (the kernel reads only routed experts, and a
+    # resident expert never changes slot); otherwise the kernel reported
+    # SLX_ERR_UNMAPPED_EXPERT for that layer, and after its replay has
+    # filled the slots that layer and every later one run again.  Each
+    # layer reads the previous layer's residual and MoE output from
+    # per-layer buffers, so a rerun from layer l sees exactly its inputs.
+
+    _UNMAPPED = -5
+
+    def _graph_buffers(self) -> None:
+        cfg, dev = self.cfg, self.device
+        n, k, H = cfg.layers, cfg.top_k, cfg.hidden
+        bf = torch.bfloat16
+        self.g_s = torch.zeros(n, 1, H, dtype=bf, device=dev)
+        self.g_m = torch.zeros(n, 1, H, dtype=bf, device=dev)
+        self.g_d = torch.zeros(n, 1, H, dtype=bf, device=dev)
+        self.g_emb = torch.zeros(1, H, dtype=bf, device=dev)
+        self.g_fin = torch.zeros(1, H, dtype=bf, device=dev)
+        # device log, read back with one copy per launch cycle:
+        # ids [n,k] | pred ids [n,k] | pred scores [n,k] f32 | layer status
+        # [n] | status | next token
+        words = 3 * n * k + n + 2
+        self.g_log = torch.zeros(words, dtype=torch.int32, device=dev)
+        self.g_log_host = torch.zeros(words, dtype=torch.int32).pin_memory()
+        o = 0
+        self.g_ids = self.g_log[o:o + n * k].view(n, 1, k)
+        o += n * k
+        self.g_pf_ids = self.g_log[o:o + n * k].view(n, 1, k)
+        o += n * k
+        self.g_pf_scores = self.g_log[o:o + n * k].view(torch.float32) \
+            .view(n, 1, k)
+        o += n * k
+        self._lst_off = o
+        self.g_lstatus = self.g_log[o:o + n]
+        o += n
+        self.g_status = self.g_log[o:o + 1]
+        self.g_tok_out = self.g_log[o + 1:o + 2]
+        self.g_scores = torch.zeros(n, 1, k, dtype=torch.float32, device=dev)
+        self.g_prev_ids = torch.zeros(n, 1, k, dtype=torch.int32, device=dev)
+        # control, written with one copy per step: pos | force[n] | token
+        self.g_ctrl = torch.zeros(n + 2, dtype=torch.int32, device=dev)
+        self.g_ctrl_host = torch.zeros(n + 2, dtype=torch.int32).pin_memory()
+        sh = [la.mlp.switch_mlp.shared for la in self.layers]
+        s_inter = max([x[2] for x in sh if x] or [0])
+        self.g_glu_scratch = torch.zeros(
+            L.switchglu_scratch_bytes(1, k, cfg.inter, s_inter),
+            dtype=torch.uint8, device=dev)
+        self.g_ev = [(torch.cuda.Event(enable_timing=True),
+                      torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+        for pair in self.g_ev:      # torch creates the CUDA event on first use
+            for e in pair:
+                e.record()
+
+    def _record_layer(self, i: int) -> None:
+        cfg = self.cfg
+        n, k, H, bits = cfg.layers, cfg.top_k, cfg.hidden, cfg.trunk_bits
+        la = self.layers[i]
+        blk = la.mlp
+        w = blk.switch_mlp
+        eps = cfg.rms_eps
+        if i == 0:
+            L.dequant_rows(self.embed, H, bits, self.g_ctrl[n + 1:n + 2], 1,
+                           cfg.vocab, self.g_emb, self.g_status)
+            h_in, d_in = self.g_emb, None
+        else:
+            h_in, d_in = self.g_m[i - 1], self.g_d[i - 1]
+        self.g_lstatus[i:i + 1].zero_()
+        L.add_rmsnorm_out(h_in, d_in, la.w_in, eps, self.g_s[i], self.x)
+        L.qlinear(la.w_qkv, la.n_qkv, H, bits, self.x, self.qkv,
+                  self.g_status)
+        L.qk_norm_rope_cache(self.qkv, cfg.heads, cfg.kv_heads, cfg.head_dim,
+                             la.q_norm, la.k_norm, eps, self.inv_freq,
+                             self.g_ctrl[0:1], self.k_cache[i],
+                             self.v_cache[i], self.g_status)
+        L.attn_decode(self.qkv, cfg.heads, cfg.kv_heads, cfg.head_dim,
+                      self.k_cache[i], self.v_cache[i], self.g_ctrl[0:1],
+                      self.att)
+        L.qlinear(la.w_o, H, cfg.heads * cfg.head_dim, bits, self.att,
+                  self.o, self.g_status)
+        L.add_rmsnorm_out(self.g_s[i], self.o, la.post_attention_layernorm,
+                          eps, self.g_m[i], self.x)
+        L.router_topk(self.x, blk.w_gate, blk.bias, k, cfg.norm_topk_prob,
+                      self.g_ids[i], self.g_scores[i], blk.scratch,
+                      self.g_status, force=self.g_ctrl[1 + i:2 + i],
+                      forced_ids=self.g_prev_ids[i])
+        if blk.pf_link is not None:
+            ratio, nxt = blk.pf_link
+            L.router_topk(self.x, nxt.w_gate, nxt.bias, k, cfg.norm_topk_prob,
+                          self.g_pf_ids[i], self.g_pf_scores[i],
+                          blk.pf_scratch, self.g_status, ratio=ratio)
+        pool = w.pool
+        sh = w.shared
+        ev = self.g_ev[i]
+        L.event_record_external(ev[0])
+        ops.switchglu(pool.store.bank, self.x, self.g_ids[i], k,
+                      scores=self.g_scores[i], table=pool.store.table_dev,
+                      shared=sh[0] if sh else None, out=self.g_d[i],
+                      inter=pool.inter, shared_inter=sh[2] if sh else 0,
+                      scratch_buf=self.g_glu_scratch,
+                      status=self.g_lstatus[i:i + 1])
+        L.event_record_external(ev[1])
+
+    def _record_tail(self) -> None:
+        cfg = self.cfg
+        n = cfg.layers
+        L.add_rmsnorm_out(self.g_m[n - 1], self.g_d[n - 1], self.norm,
+                          cfg.rms_eps, self.g_fin, self.x)
+        L.qlinear(self.w_lm, cfg.vocab, cfg.hidden, cfg.trunk_bits, self.x,
+                  self.logits, self.g_status)
+        L.argmax(self.logits, self.g_tok_out)
+        # a plain async copy (no allocator event) so it captures as a node
+        L.copy_many([self.g_log_host.data_ptr()], [self.g_log.data_ptr()],
+                    [self.g_log.numel() * 4])
+
+    def _capture(self) -> None:
+        """Capture the per-layer graphs, the tail graph and one graph of the
+        whole step (used when a step starts at layer 0)."""
+        if not hasattr(self, "g_log"):
+            self._graph_buffers()
+        n = self.cfg.layers
+        # the initialising pass below really runs: point it at the position
+        # the next step overwrites anyway, not forced, token 0
+        ch = self.g_ctrl_host.numpy()
+        ch[:] = 0
+        ch[0] = min(self.n_pos, self.max_len - 1)
+        L.copy_many([self.g_ctrl.data_ptr()], [self.g_ctrl_host.data_ptr()],
+                    [self.g_ctrl.numel() * 4])
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        # one eager pass on the side stream initialises every launcher
+        # (function attributes, lazy module loads) outside the capture
+        with torch.cuda.stream(s):
+            for i in range(n):
+                self._record_layer(i)
+            self._record_tail()
+        s.synchronize()
+        mode = "thread_local"
+        graphs = []
+        for i in range(n):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s, capture_error_mode=mode):
+                self._record_layer(i)
+            graphs.append(g)
+        tail = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(tail, stream=s, capture_error_mode=mode):
+            self._record_tail()
+        full = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(full, stream=s, capture_error_mode=mode):
+            for i in range(n):
+                self._record_layer(i)
+            self._record_tail()
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        self._graphs = (graphs, tail, full)
+        self.g_status.zero_()
+        self.g_lstatus.zero_()
+
+    def _graph_kernels(self, start: int) -> int:
+        """Library kernels one launch from layer `start` runs."""
+        per = 0
+        for i in range(start, self.cfg.layers):
+            per += 9 + (1 if self.layers[i].mlp.pf_link is not None else 0)
+        return per + (1 if start == 0 else 0) + 3
+
+    def _launch(self, start: int) -> None:
+        graphs, tail, full = self._graphs
+        if start == 0:
+            full.replay()
+        else:
+            for i in range(start, self.cfg.layers):
+                graphs[i].replay()
+            tail.replay()
+        L._count(self._graph_kernels(start))
+
+    def _read_log(self) -> np.ndarray:
+        torch.cuda.current_stream(self.device).synchronize()
+        log = self.g_log_host.numpy().copy()
+        st = int(log[self._lst_off + self.cfg.layers])
+        if st != 0:
+            self.g_status.zero_()
+            raise L.SlxError("device", st, "decode step device error")
+        return log
+
+    def _glu_timing(self, start: int) -> None:
+        if self.glu_times is None:
+            return
+        ev = self.g_ev[start:]
+        self.glu_times.extend(
+            L.event_elapsed_many([e[0] for e in ev], [e[1] for e in ev])
+            .tolist())
+
+    def _replay(self, log: np.ndarray, start: int) -> int | None:
+        """Pool bookkeeping of layers start.. from a log; returns the first
+        layer that must run again (its slots are now filled) or None."""
+        n, k = self.cfg.layers, self.cfg.top_k
+        ids = log[:n * k].reshape(n, 1, 1, k)
+        pf_ids = log[n * k:2 * n * k].reshape(n, k)
+        pf_sc = log[2 * n * k:3 * n * k].view(np.float32).reshape(n, k)
+        lst = log[self._lst_off:self._lst_off + n]
+        for i in range(start, n):
+            code = int(lst[i])
+            if code not in (0, self._UNMAPPED):
+                raise L.SlxError("device", code, f"layer {i} SwitchGLU")
+            w = self.layers[i].mlp.switch_mlp
+            pred = None
+            if self.layers[i].mlp.pf_link is not None and w.pred_gate():
+                pred = (pf_ids[i].copy(), pf_sc[i].copy())
+            if w.route(ids[i].copy(), pred) != "pool":
+                raise RuntimeError("decode call routed more experts than "
+                                   "the pool has slots")
+            w.pool.sync_device()
+            if code == self._UNMAPPED:
+                return i
+        return None
+
+    def flush(self) -> None:
+        """Finish the deferred bookkeeping of the last step, if any."""
+        pend, self._pending = self._pending, None
+        if pend is not None and self._replay(pend, 0) is not None:
+            raise RuntimeError("deferred step had an unmapped expert")
+
+    def _step_graph(self, token: torch.Tensor) -> torch.Tensor:
+        n = self.cfg.layers
+        if self.n_pos >= self.max_len:
+            raise RuntimeError("KV cache full")
+        if self._graphs is None:
+            self.flush()
+            self._capture()
+        ch = self.g_ctrl_host.numpy()
+        ch[0] = self.n_pos
+        for i in range(n):
+            ch[1 + i] = int(bool(self.repeat_p) and self.n_pos > 0 and
+                            self._rng.random() < self.repeat_p)
+        tok = token.reshape(1)
+        if tok.dtype != torch.int32 or tok.device != self.device:
+            tok = tok.to(device=self.device, dtype=torch.int32)
+        L.copy_many([self.g_ctrl.data_ptr(), self.g_ctrl.data_ptr() + 4 * (n + 1)],
+                    [self.g_ctrl_host.data_ptr(), tok.data_ptr()],
+                    [4 * (n + 1), 4])
+        # this step's device work is queued before the host replays the
+        # previous step: that replay's slot fills and table pushes run after
+        # it on the stream, and this step is judged by its own log
+        self._launch(0)
+        self.flush()
+        log = self._read_log()
+        self._glu_timing(0)
+        lst = log[self._lst_off:self._lst_off + n]
+        if self.pipeline and not (lst == self._UNMAPPED).any():
+            self._pending = log
+        else:
+            start = 0
+            while True:
+                redo = self._replay(log, start)
+                if redo is None:
+                    break
+                self._launch(redo)
+                log = self._read_log()
+                self._glu_timing(redo)
+                if int(log[self._lst_off + redo]) != 0:
+                    raise RuntimeError(f"layer {redo} still unmapped after "
+                                       "its slots were filled")
+                start = redo + 1
+        self.g_prev_ids.copy_(self.g_ids)
+        self.n_pos += 1
+        nxt = torch.empty(1, dtype=torch.int32, device=self.device)
+        nxt.copy_(self.g_tok_out)
+        return nxt
+
     @torch.no_grad()
     def generate(self, prompt_ids, max_new: int) -> list[int]:
         """Token-by-token prompt feed, then greedy decode
@@ -259,6 +558,7 @@ class SynthDecoder:
         for _ in range(max_new):
             out.append(int(tok.item()))
             tok = self.step(tok)
+        self.flush()
         return out
 
     @torch.no_grad()

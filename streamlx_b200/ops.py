@@ -60,22 +60,33 @@ def as_ids_2d(ids, k: int, device) -> torch.Tensor:
 def switchglu(bank, x2d: torch.Tensor, ids2d: torch.Tensor, k: int, *,
               scores: torch.Tensor | None = None, table: torch.Tensor | None = None,
               shared=None, out: torch.Tensor | None = None,
-              inter: int, shared_inter: int = 0) -> torch.Tensor:
+              inter: int, shared_inter: int = 0,
+              scratch_buf: torch.Tensor | None = None,
+              status: torch.Tensor | None = None) -> torch.Tensor:
     """One fused SwitchGLU launch pair.  scores None -> [T, k, H] per-expert
-    unweighted outputs; else [T, H] combined (+ shared expert)."""
+    unweighted outputs; else [T, H] combined (+ shared expert).
+    ``scratch_buf`` / ``status`` override the per-device shared ones (a
+    captured graph needs buffers that never move)."""
     T, H = x2d.shape
     dev = x2d.device
     if out is None:
         shape = (T, H) if scores is not None else (T, k, H)
         out = torch.empty(shape, dtype=torch.bfloat16, device=dev)
     sI = shared_inter if (scores is not None and shared is not None) else 0
-    sc = scratch(L.switchglu_scratch_bytes(T, k, inter, sI), dev)
+    need = L.switchglu_scratch_bytes(T, k, inter, sI)
+    if scratch_buf is not None:
+        if scratch_buf.numel() * scratch_buf.element_size() < need:
+            raise ValueError("switchglu: scratch_buf too small")
+        sc = scratch_buf
+    else:
+        sc = scratch(need, dev)
     ev = None
     if TIMING is not None:
         ev = (torch.cuda.Event(enable_timing=True),
               torch.cuda.Event(enable_timing=True))
         ev[0].record()
-    L.switchglu(bank, x2d, ids2d, out, sc, _status(dev), scores=scores,
+    L.switchglu(bank, x2d, ids2d, out, sc,
+                _status(dev) if status is None else status, scores=scores,
                 slot_table=table, shared=shared if sI else None)
     if ev is not None:
         ev[1].record()

@@ -422,6 +422,9 @@ class StreamingSwitchMLP:
 
     @property
     def stats(self) -> dict:
+        hook = getattr(self, "flush_hook", None)
+        if hook is not None:        # a decoder with deferred bookkeeping
+            hook()
         total = self.hits + self.misses
         return {"hits": self.hits, "misses": self.misses,
                 "evictions": self.evictions,

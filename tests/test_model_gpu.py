@@ -40,14 +40,17 @@ def _margin_ok(logits: np.ndarray, ids: np.ndarray, k: int) -> bool:
     return (s[k - 1] - s[k]) > 2e-3
 
 
+@pytest.mark.parametrize("path", ["graph", "eager"])
 @pytest.mark.parametrize("name,slots", [("tiny_dec", 6), ("tiny_dec2", 5)])
-def test_decoder_matches_oracle(tiny, name, slots, monkeypatch):
+def test_decoder_matches_oracle(tiny, name, slots, path, monkeypatch):
     monkeypatch.setenv("STREAMLX_EVICT", "lru")
     d = tiny[name]
     cfg = synth.load_config(d)
     bpe = synth.expert_bytes(cfg.hidden, cfg.inter, cfg.expert_bits, 64)
     model, tok, pools, reader = load_streaming_model(
         d, budget_bytes=slots * bpe * cfg.layers, k=cfg.top_k)
+    model.use_graphs = path == "graph"
+    model.pipeline = False          # routed ids recorded within each step
     assert all(p.n_slots == slots for p in pools.values())
     sinks = []
     for i in range(cfg.layers):
@@ -84,6 +87,55 @@ def test_decoder_matches_oracle(tiny, name, slots, monkeypatch):
     assert st["misses"] > 0 and st["evictions"] > 0      # the pool streamed
     assert st["hits"] + st["misses"] == 24 * cfg.layers * cfg.top_k
     reader.close()
+
+
+def _pool_state(p):
+    return (p.stats, list(p.id2slot.items()), list(p.free),
+            {str(k): v for k, v in p.pf_rank.items()})
+
+
+@pytest.mark.parametrize("policy", ["lru", "s3fifo"])
+@pytest.mark.parametrize("name,slots", [("tiny_dec", 6), ("tiny_dec2", 5)])
+def test_graph_step_trace_equals_eager(tiny, name, slots, policy, monkeypatch):
+    """The graph step (pipelined, with reruns after misses) gives the eager
+    step's tokens, logits and pool bookkeeping, call for call."""
+    monkeypatch.setenv("STREAMLX_EVICT", policy)
+    d = tiny[name]
+    cfg = synth.load_config(d)
+    bpe = synth.expert_bytes(cfg.hidden, cfg.inter, cfg.expert_bits, 64)
+    runs = []
+    for path in ("eager", "graph"):
+        model, _, pools, reader = load_streaming_model(
+            d, budget_bytes=slots * bpe * cfg.layers, k=cfg.top_k)
+        model.use_graphs = path == "graph"
+        sinks = []
+        for i in range(cfg.layers):
+            sinks.append([])
+            model.layers[i].mlp.switch_mlp.record_sink = sinks[-1]
+        rng = np.random.default_rng(7)
+        toks, logits = [], []
+        tok = None
+        for t in range(40):
+            if t < 8 or tok is None:    # prompt, then greedy decode
+                tok = torch.tensor([int(rng.integers(cfg.vocab))],
+                                   dtype=torch.int32, device=model.device)
+            tok = model.step(tok)
+            toks.append(int(tok.item()))
+            logits.append(model.logits.clone())
+        model.flush()
+        state = [_pool_state(pools[i]) for i in sorted(pools)]
+        seq = [[x[1].tolist() for x in s] for s in sinks]
+        runs.append((toks, torch.cat(logits), state, seq))
+        reader.close()
+    (t0, l0, s0, q0), (t1, l1, s1, q1) = runs
+    assert t0 == t1
+    assert torch.equal(l0, l1)
+    assert q0 == q1
+    for a, b in zip(s0, s1):
+        sa = {k: v for k, v in a[0].items() if not k.endswith("_s")}
+        sb = {k: v for k, v in b[0].items() if not k.endswith("_s")}
+        assert sa == sb and a[1:] == b[1:]
+    assert sum(x[0]["misses"] for x in s1) > 0
 
 
 def test_pool_dropin_call_matches_oracle(tiny):
