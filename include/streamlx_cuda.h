@@ -71,6 +71,14 @@ typedef struct slx_shared_expert {
 
 int slx_version(void);
 
+/* Programmatic dependent launch for the calling host thread's subsequent
+ * launches (0 = off, the default).  With it on, each kernel may start while
+ * the previous one on the stream drains: it streams its fixed weights early
+ * and waits (griddepcontrol.wait) before touching anything the previous
+ * kernel wrote, so results are the same either way.  Returns the previous
+ * setting. */
+int slx_set_pdl(int on);
+
 /* Last host-side error message of the calling thread ("" if none). */
 const char* slx_last_error_string(void);
 
@@ -159,6 +167,30 @@ int slx_router_topk(const void* x, const void* ratio, const void* w_gate,
                     float* out_scores, void* scratch, size_t scratch_bytes,
                     int32_t* status, void* stream);
 
+/* One router "head": a gate [E, H] bf16 (+ bias [E] fp32, nullable), an
+ * optional ratio [H] bf16 applied to x first (next-layer predictor), the
+ * optional forced-ids override, outputs, and this head's own scratch of
+ * slx_router_scratch_bytes(T, E) bytes. */
+typedef struct slx_router_head {
+  const void* w_gate;
+  const float* bias;
+  const void* ratio;
+  const int32_t* force;
+  const int32_t* forced_ids;
+  int32_t* out_ids;
+  float* out_scores;
+  void* scratch;
+  size_t scratch_bytes;
+} slx_router_head;
+
+/* slx_router_topk for 1 or 2 heads over the same x [T, H] in one launch:
+ * the decode layer's router and its next-layer predictor
+ * (streamlx/integrate.py:60-88 runs the predictor's gate on the same
+ * MoE input).  Each head's results equal a slx_router_topk call. */
+int slx_router_topk_multi(const slx_router_head* heads, int n_heads,
+                          const void* x, int T, int H, int E, int k,
+                          int norm_topk, int32_t* status, void* stream);
+
 /* Router GEMV + softmax + top-k exactly as slx_router_topk, for callers
  * that hold no device allocator: a host binding that reaches the library
  * only through this C ABI (ctypes, cgo, JNI) and would otherwise have to
@@ -191,6 +223,9 @@ int slx_qk_norm_rope_cache(void* qkv, int T, int n_q, int n_kv, int head_dim,
                            const float* inv_freq, const int32_t* pos,
                            int max_len, void* k_cache, void* v_cache,
                            int32_t* status, void* stream);
+/* Batch-1 decode attention (GQA, head_dim 128, n_q / n_kv <= 8) over
+ * positions 0..pos[t] of the caches; one 8-CTA cluster per (token, kv
+ * head) splits the positions and merges in distributed shared memory. */
 int slx_attn_decode(const void* qkv, int T, int n_q, int n_kv, int head_dim,
                     const void* k_cache, const void* v_cache,
                     const int32_t* pos, int max_len, void* out, void* stream);

@@ -34,6 +34,7 @@ EXPORTS = (
     "slx_qk_norm_rope_cache", "slx_attn_decode", "slx_argmax",
     "slx_copy_many", "slx_router_topk_noalloc", "slx_add_rmsnorm_out",
     "slx_event_record_external", "slx_event_elapsed_many",
+    "slx_router_topk_multi", "slx_set_pdl",
 )
 
 
@@ -69,6 +70,14 @@ def _count(n: int = 1) -> None:
     LAUNCHES[0] += n
 
 
+class slx_router_head(C.Structure):
+    _fields_ = [("w_gate", C.c_void_p), ("bias", C.c_void_p),
+                ("ratio", C.c_void_p), ("force", C.c_void_p),
+                ("forced_ids", C.c_void_p), ("out_ids", C.c_void_p),
+                ("out_scores", C.c_void_p), ("scratch", C.c_void_p),
+                ("scratch_bytes", C.c_size_t)]
+
+
 def lib() -> C.CDLL:
     """Load the shared object (raises if it is not built)."""
     global _lib
@@ -80,6 +89,8 @@ def lib() -> C.CDLL:
         L = C.CDLL(LIB_PATH)
         vp, i32, sz = C.c_void_p, C.c_int, C.c_size_t
         L.slx_version.restype = i32
+        L.slx_set_pdl.restype = i32
+        L.slx_set_pdl.argtypes = [i32]
         L.slx_last_error_string.restype = C.c_char_p
         L.slx_expert_tiled_bytes.restype = sz
         L.slx_expert_tiled_bytes.argtypes = [i32, i32, i32]
@@ -107,6 +118,10 @@ def lib() -> C.CDLL:
         L.slx_router_topk.restype = i32
         L.slx_router_topk.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, i32,
                                       vp, vp, vp, vp, vp, sz, vp, vp]
+        L.slx_router_topk_multi.restype = i32
+        L.slx_router_topk_multi.argtypes = [C.POINTER(slx_router_head), i32,
+                                            vp, i32, i32, i32, i32, i32, vp,
+                                            vp]
         L.slx_router_topk_noalloc.restype = i32
         L.slx_router_topk_noalloc.argtypes = [vp, vp, vp, vp, i32, i32, i32,
                                               i32, i32, vp, vp, vp, vp, vp, vp]
@@ -133,6 +148,12 @@ def lib() -> C.CDLL:
         L.slx_copy_many.argtypes = [vp, vp, vp, i32, vp]
         _lib = L
     return _lib
+
+
+def set_pdl(on: bool) -> bool:
+    """Programmatic dependent launch for this thread's next launches;
+    returns the previous setting."""
+    return bool(lib().slx_set_pdl(1 if on else 0))
 
 
 def _check(fn: str, rc: int) -> None:
@@ -274,6 +295,27 @@ def router_topk(x: torch.Tensor, w_gate: torch.Tensor, bias, k: int,
         scratch.numel() * scratch.element_size(), status.data_ptr(),
         stream_ptr(stream))
     _check("slx_router_topk", rc)
+    _count(1)
+
+
+def router_head(w_gate, bias, out_ids, out_scores, scratch, ratio=None,
+                force=None, forced_ids=None) -> slx_router_head:
+    return slx_router_head(w_gate.data_ptr(), ptr(bias), ptr(ratio),
+                           ptr(force), ptr(forced_ids), out_ids.data_ptr(),
+                           out_scores.data_ptr(), scratch.data_ptr(),
+                           scratch.numel() * scratch.element_size())
+
+
+def router_topk_multi(x: torch.Tensor, heads: list, E: int, k: int,
+                      norm_topk: bool, status: torch.Tensor,
+                      stream=None) -> None:
+    """One launch of 1-2 router heads (router_head structs) over x [T, H]."""
+    T, H = x.shape[-2], x.shape[-1]
+    arr = (slx_router_head * len(heads))(*heads)
+    rc = lib().slx_router_topk_multi(arr, len(heads), x.data_ptr(), T, H, E,
+                                     k, 1 if norm_topk else 0,
+                                     status.data_ptr(), stream_ptr(stream))
+    _check("slx_router_topk_multi", rc)
     _count(1)
 
 

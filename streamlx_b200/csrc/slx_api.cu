@@ -14,6 +14,7 @@
 namespace {
 
 thread_local std::string g_err;
+thread_local int g_pdl = 0;
 
 int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -48,9 +49,19 @@ size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
 
 }  // namespace
 
+namespace slx {
+bool pdl_enabled() { return g_pdl != 0; }
+}  // namespace slx
+
 extern "C" {
 
 int slx_version(void) { return 1; }
+
+int slx_set_pdl(int on) {
+  const int prev = g_pdl;
+  g_pdl = on ? 1 : 0;
+  return prev;
+}
 
 const char* slx_last_error_string(void) { return g_err.c_str(); }
 
@@ -320,6 +331,56 @@ int slx_router_topk(const void* x, const void* ratio, const void* w_gate,
   return rc ? cuda_check(rc, "slx_router_topk") : SLX_OK;
 }
 
+int slx_router_topk_multi(const slx_router_head* heads, int n_heads,
+                          const void* x, int T, int H, int E, int k,
+                          int norm_topk, int32_t* status, void* stream) {
+  g_err.clear();
+  if (!heads || n_heads < 1 || n_heads > 2)
+    return fail(SLX_ERR_INVALID, "router_multi: 1 or 2 heads");
+  if (!x || !aligned16(x))
+    return fail(SLX_ERR_INVALID, "router_multi: x NULL or not 16-byte aligned");
+  if (T < 0 || H <= 0 || H % 8 || E < 1 || k < 1 || k > E)
+    return fail(SLX_ERR_INVALID, "router shape T %d H %d E %d k %d", T, H, E, k);
+  if (T == 0) return SLX_OK;
+  const size_t need = slx_router_scratch_bytes(T, E);
+  slx::RouterArgs a[2] = {};
+  for (int i = 0; i < n_heads; ++i) {
+    const slx_router_head& h = heads[i];
+    if (!h.w_gate || !h.out_ids || !h.out_scores)
+      return fail(SLX_ERR_INVALID, "router_multi head %d: NULL pointer", i);
+    if (!aligned16(h.w_gate) || (h.ratio && !aligned16(h.ratio)))
+      return fail(SLX_ERR_INVALID, "router_multi head %d: not 16-byte aligned", i);
+    if (h.force && !h.forced_ids)
+      return fail(SLX_ERR_INVALID, "router_multi head %d: force without ids", i);
+    if (!h.scratch || h.scratch_bytes < need)
+      return fail(SLX_ERR_SCRATCH, "router_multi head %d: scratch %zu < %zu",
+                  i, h.scratch_bytes, need);
+    for (int j = 0; j < i; ++j)
+      if (heads[j].scratch == h.scratch)
+        return fail(SLX_ERR_INVALID, "router_multi: heads share scratch");
+    a[i].x = (const uint16_t*)x;
+    a[i].ratio = (const uint16_t*)h.ratio;
+    a[i].w = (const uint16_t*)h.w_gate;
+    a[i].bias = h.bias;
+    a[i].T = T;
+    a[i].H = H;
+    a[i].E = E;
+    a[i].k = k;
+    a[i].norm_topk = norm_topk;
+    a[i].force = h.force;
+    a[i].forced_ids = h.forced_ids;
+    a[i].out_ids = h.out_ids;
+    a[i].out_scores = h.out_scores;
+    a[i].logits = reinterpret_cast<float*>(h.scratch);
+    a[i].tickets = reinterpret_cast<int32_t*>(
+        reinterpret_cast<uint8_t*>(h.scratch) + align256((size_t)T * E * 4));
+    a[i].status = status;
+  }
+  const int rc = slx::launch_router_heads(a, n_heads,
+                                          reinterpret_cast<cudaStream_t>(stream));
+  return rc ? cuda_check(rc, "slx_router_topk_multi") : SLX_OK;
+}
+
 int slx_add_rmsnorm_out(const void* h_in, const void* delta,
                         const void* weight, int T, int H, float eps,
                         void* h_out, void* y, void* stream) {
@@ -394,6 +455,8 @@ int slx_attn_decode(const void* qkv, int T, int n_q, int n_kv, int head_dim,
   if (!qkv || !k_cache || !v_cache || !pos || !out)
     return fail(SLX_ERR_INVALID, "attn: NULL");
   if (n_q < 1 || n_kv < 1 || n_q % n_kv) return fail(SLX_ERR_INVALID, "heads");
+  if (!aligned16(k_cache) || !aligned16(v_cache))
+    return fail(SLX_ERR_INVALID, "attn: caches not 16-byte aligned");
   const int rc = slx::launch_attn_decode(
       (const uint16_t*)qkv, T, n_q, n_kv, head_dim, (const uint16_t*)k_cache,
       (const uint16_t*)v_cache, pos, max_len, (uint16_t*)out,

@@ -121,12 +121,39 @@ SLX_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes,
 }
 
 // ------------------------------------------------------------------ PDL ---
+//
+// Every kernel of the library lets its dependent grid launch at once
+// (launch_dependents at entry) and executes griddepcontrol.wait before it
+// reads anything a preceding kernel wrote or writes any global memory; only
+// reads of immutable weights may come before the wait.  Both instructions
+// are no-ops for a grid launched without the programmatic-serialization
+// attribute, so the same code is correct with and without PDL.
 
 SLX_DEV void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 SLX_DEV void pdl_wait_primary() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// Launch setting of the calling host thread (slx_set_pdl).
+bool pdl_enabled();
+
+// <<<>>> replacement that adds the PDL attribute when pdl_enabled().
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block,
+                     size_t smem, cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
 // ------------------------------------------------------------------ MMA ---
@@ -256,6 +283,18 @@ SLX_DEV float silu_f32(float g) { return g / (1.f + __expf(-g)); }
   do {                        \
   } while (0)
 #endif
+
+// Ticket of a "last CTA finishes the job" pattern: call after a
+// __syncthreads() that follows the CTA's global writes, from one thread.
+// The release half publishes this CTA's writes (ordered before it by the
+// barrier); the acquire half lets the last CTA read every other CTA's
+// writes (through L2: use ld.cg / __ldcg) after its own __syncthreads().
+SLX_DEV int ticket_acq_rel(int32_t* counter) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
+               : "=r"(old) : "l"(counter) : "memory");
+  return old;
+}
 
 SLX_DEV void set_status(int32_t* status, int32_t code) {
   if (status) atomicCAS(status, 0, code);

@@ -87,6 +87,8 @@ int launch_dequant_rows(const uint32_t* w, const uint16_t* s, const uint16_t* b,
                         int nrows, int n_src_rows, void* out, int out_bf16,
                         int32_t* status, cudaStream_t stream);
 int launch_router(const RouterArgs& a, cudaStream_t stream);
+int launch_router_heads(const RouterArgs* heads, int n_heads,
+                        cudaStream_t stream);
 int launch_pack_experts(const void* const* gw, const void* const* gs,
                         const void* const* gb, const void* const* uw,
                         const void* const* us, const void* const* ub,

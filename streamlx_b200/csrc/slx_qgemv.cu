@@ -305,8 +305,13 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   SLX_TRACE_POINT(0, 0);
   SLX_TRACE_SMID(0);
-  if (a.wait_primary) pdl_wait_primary();
-  // Let the dependent (down-projection) grid start its weight stream now.
+  // A dense matrix's tiles are fixed weights: they may be in flight before
+  // the wait; an expert tile's address depends on the routed ids.  The
+  // dependent grid may launch now (dense: it waits for us before reading
+  // anything we write) or, for the expert phase, once the ids are final
+  // (the down projection reads ids and the slot table before its wait).
+  const bool early = a.mode == SLX_GEMV_LINEAR;
+  if (!early) pdl_wait_primary();
   pdl_launch_dependents();
 
   if (warp == 0) {
@@ -319,6 +324,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (lane < first)
       gemv_issue<BITS>(a, gemv_tile(a, q_begin + lane, issue_cache),
                        stages + (size_t)lane * a.stage_bytes, &full[lane], pol);
+    if (early) pdl_wait_primary();  // before the epilogue writes y
     for (int i = 0; i < n; ++i) {
       const int st = i % NS;
       if (!mbar_wait(&redfull[st], (i / NS) & 1, a.status)) break;
@@ -336,6 +342,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 
   // ------------------------------------------------------- consumers ---
+  if (early) pdl_wait_primary();  // x comes from the preceding kernel
   const int cw = warp - 1;  // consumer warp 0..kNW-1
   const int ct = threadIdx.x - 32;
   const int g = lane >> 2, tig = lane & 3;
@@ -470,6 +477,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     fence_mbar_init();
   }
   __syncthreads();
+  pdl_launch_dependents();  // the next op waits for this grid to finish
 
   if (warp == 0) {
     // ------------------------------------------- producer + reduction ---
@@ -680,6 +688,7 @@ static int launch_gemv_t(GemvArgs a, cudaStream_t stream, bool pdl_secondary) {
   a.n_stages = ns;
   int smem = fixed + ns * per_stage;
   if (smem < kSmemTarget) smem = kSmemTarget;
+  if (pdl_enabled()) pdl_secondary = true;
   a.wait_primary = pdl_secondary ? 1 : 0;
   if (a.n_tiles <= 0) return SLX_OK;
   int grid = num_sms();
@@ -745,7 +754,7 @@ static int launch_down_t(DownArgs a, cudaStream_t stream) {
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = a.pdl ? 1 : 0;
+  cfg.numAttrs = (a.pdl || pdl_enabled()) ? 1 : 0;
   e = cudaLaunchKernelEx(&cfg, k_down<BITS>, a);
   return e == cudaSuccess ? SLX_OK : SLX_ERR_CUDA;
 }
@@ -769,6 +778,8 @@ __global__ void k_dequant_rows(const uint32_t* __restrict__ w,
                                int gs, const int32_t* __restrict__ rows,
                                int nrows, int n_src_rows, void* out,
                                int out_bf16, int32_t* status) {
+  pdl_launch_dependents();
+  pdl_wait_primary();
   const int r = blockIdx.y;
   if (r >= nrows) return;
   const int src = rows ? rows[r] : r;
@@ -801,9 +812,9 @@ int launch_dequant_rows(const uint32_t* w, const uint16_t* s, const uint16_t* b,
   if (nrows <= 0) return SLX_OK;
   if (nrows > 65535) return SLX_ERR_INVALID;
   dim3 grid((in + 255) / 256, nrows);
-  k_dequant_rows<<<grid, 256, 0, stream>>>(w, s, b, in, bits, gs, rows, nrows,
-                                           n_src_rows, out, out_bf16, status);
-  return cudaGetLastError() == cudaSuccess ? SLX_OK : SLX_ERR_CUDA;
+  return launch_k(k_dequant_rows, grid, dim3(256), 0, stream, w, s, b, in, bits,
+                  gs, rows, nrows, n_src_rows, out, out_bf16, status) ==
+                 cudaSuccess ? SLX_OK : SLX_ERR_CUDA;
 }
 
 }  // namespace slx

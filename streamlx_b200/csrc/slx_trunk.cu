@@ -4,6 +4,8 @@
 // reference (mlx-lm owns it); these exist so decode tok/s can be measured on
 // the synthetic decoders, and they read their position from device memory so
 // a whole decode step can be captured in a CUDA graph.
+#include <cooperative_groups.h>
+
 #include "slx_kernels.cuh"
 
 namespace slx {
@@ -33,6 +35,8 @@ __global__ void __launch_bounds__(kNormThreads) k_add_rmsnorm(
     const uint16_t* h_in, const uint16_t* d, const uint16_t* w, int H,
     float eps, uint16_t* h_out, uint16_t* y) {
   __shared__ float red[32];
+  pdl_launch_dependents();
+  pdl_wait_primary();
   const int t = blockIdx.x;
   const uint16_t* hr = h_in + (size_t)t * H;
   const uint16_t* dr = d ? d + (size_t)t * H : nullptr;
@@ -95,6 +99,8 @@ __global__ void k_qk_rope_cache(uint16_t* qkv, int nq, int nkv, int hd,
                                 uint16_t* kcache, uint16_t* vcache,
                                 int32_t* status) {
   __shared__ float red[32];
+  pdl_launch_dependents();
+  pdl_wait_primary();
   const int t = blockIdx.x, hidx = blockIdx.y;
   const int half = hd / 2, i = threadIdx.x;  // blockDim.x == half
   const int p = pos[t];
@@ -135,79 +141,241 @@ __global__ void k_qk_rope_cache(uint16_t* qkv, int nq, int nkv, int hd,
   }
 }
 
-// One CTA per (token, q head).  Scores over positions 0..pos[t], softmax in
-// fp32, output bf16.  Dynamic smem: max_len floats.
-__global__ void __launch_bounds__(128) k_attn_decode(
-    const uint16_t* qkv, int nq, int nkv, int hd, const uint16_t* kcache,
-    const uint16_t* vcache, const int32_t* pos, int max_len, float scale,
-    uint16_t* out) {
-  extern __shared__ float sc[];
-  __shared__ float red[32];
-  const int t = blockIdx.x, hq = blockIdx.y;
-  const int hk = hq / (nq / nkv);
-  const int n = pos[t] + 1;
-  if (n <= 0 || n > max_len) return;
-  const uint16_t* q = qkv + (size_t)t * (nq + 2 * nkv) * hd + hq * hd;
+// Split-K decode attention (GQA) on a thread-block cluster.  The 8 CTAs of
+// a cluster serve one (token, kv head) and every q head that shares it; CTA
+// r takes the 64-position chunks r, r+8, ...: it stages a chunk's K and V
+// rows (2 x 16 KB) in shared memory with one round of 16-byte loads, scores
+// every (head, position) pair (4 threads per position), and folds the chunk
+// into a running softmax (max, sum, unnormalised O) per head.  Each CTA then
+// writes its (O, max, sum) into CTA 0's shared memory (distributed shared
+// memory); after one cluster barrier CTA 0 merges them and writes out.
+constexpr int kAttnThreads = 256;
+constexpr int kAttnChunk = 64;
+constexpr int kAttnMaxRep = 8;
+constexpr int kAttnCluster = 8;
+constexpr int kAttnPart = 128 + 2;  // O, max, sum
+// dynamic shared memory: K, V chunk (bf16) | q (fp32) | p | partials
+constexpr int kAttnSmem = 2 * kAttnChunk * 128 * 2 + kAttnMaxRep * 128 * 4 +
+                          kAttnMaxRep * kAttnChunk * 4 +
+                          kAttnCluster * kAttnMaxRep * kAttnPart * 4;
+
+__global__ void __cluster_dims__(kAttnCluster, 1, 1)
+    __launch_bounds__(kAttnThreads) k_attn_decode(
+        const uint16_t* qkv, int nq, int nkv, int hd, const uint16_t* kcache,
+        const uint16_t* vcache, const int32_t* pos, int max_len, float scale,
+        uint16_t* out) {
+  namespace cg = cooperative_groups;
+  extern __shared__ __align__(16) uint8_t attn_smem[];
+  uint16_t* Ks = reinterpret_cast<uint16_t*>(attn_smem);
+  uint16_t* Vs = Ks + kAttnChunk * 128;
+  float* qs = reinterpret_cast<float*>(Vs + kAttnChunk * 128);
+  float* ps = qs + kAttnMaxRep * 128;                 // [rep][64]
+  float* parts = ps + kAttnMaxRep * kAttnChunk;       // [8][rep][130]
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  pdl_launch_dependents();
+  pdl_wait_primary();
+  const int hk = blockIdx.y, t = blockIdx.z;
+  const int rep = nq / nkv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nw = blockDim.x >> 5;
-  // each lane owns hd/32 dims (hd = 128 -> 4)
-  float qv[4];
+  const int n = pos[t] + 1;
+  const bool ok_n = n > 0 && n <= max_len;
+  const size_t kstride = (size_t)nkv * hd;
+  const uint16_t* q = qkv + (size_t)t * (nq + 2 * nkv) * hd +
+                      (size_t)hk * rep * hd;
+  for (int i = threadIdx.x; i < rep * 128; i += kAttnThreads)
+    qs[i] = bf16_to_f32(q[i]);
+  // running state: warp r < rep owns head r's (m, l); thread (d2, rg) owns
+  // O of heads rg*2, rg*2+1 at dims 2*d2, 2*d2+1
+  float m_run = -INFINITY, l_run = 0.f;
+  const int d2 = threadIdx.x & 63, rg = threadIdx.x >> 6;
+  float oa0 = 0.f, oa1 = 0.f, ob0 = 0.f, ob1 = 0.f;
+  const int nchunks = ok_n ? (n + kAttnChunk - 1) / kAttnChunk : 0;
+  for (int c = rank; c < nchunks; c += kAttnCluster) {
+    const int c0 = c * kAttnChunk;
+    const int np = min(kAttnChunk, n - c0);
+    __syncthreads();  // previous chunk's K/V/p reads are done
+    for (int u = threadIdx.x; u < kAttnChunk * 16; u += kAttnThreads) {
+      const int r = u >> 4, cu = u & 15;
+      uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+      if (r < np) {
+        const size_t off = (size_t)(c0 + r) * kstride + (size_t)hk * hd;
+        kv = reinterpret_cast<const uint4*>(kcache + off)[cu];
+        vv = reinterpret_cast<const uint4*>(vcache + off)[cu];
+      }
+      reinterpret_cast<uint4*>(Ks)[u] = kv;
+      reinterpret_cast<uint4*>(Vs)[u] = vv;
+    }
+    __syncthreads();
+    {  // scores: thread = (position, quarter of the 128 dims)
+      const int p = threadIdx.x >> 2, qt = threadIdx.x & 3;
+      uint4 kr[4];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) qv[j] = bf16_to_f32(q[lane * 4 + j]);
-  for (int p = warp; p < n; p += nw) {
-    const uint16_t* kr = kcache + ((size_t)p * nkv + hk) * hd + lane * 4;
-    const uint2 kw = *reinterpret_cast<const uint2*>(kr);
-    float s = qv[0] * bf16_lo(kw.x) + qv[1] * bf16_hi(kw.x) +
-              qv[2] * bf16_lo(kw.y) + qv[3] * bf16_hi(kw.y);
+      for (int u = 0; u < 4; ++u)
+        kr[u] = reinterpret_cast<const uint4*>(Ks + p * 128 + qt * 32)[u];
+      for (int r = 0; r < rep; ++r) {
+        const float* qr = qs + r * 128 + qt * 32;
+        float sacc = 0.f;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if (lane == 0) sc[p] = s * scale;
+        for (int u = 0; u < 4; ++u) {
+          const float4 qa = *reinterpret_cast<const float4*>(qr + u * 8);
+          const float4 qb = *reinterpret_cast<const float4*>(qr + u * 8 + 4);
+          sacc += qa.x * bf16_lo(kr[u].x) + qa.y * bf16_hi(kr[u].x) +
+                  qa.z * bf16_lo(kr[u].y) + qa.w * bf16_hi(kr[u].y) +
+                  qb.x * bf16_lo(kr[u].z) + qb.y * bf16_hi(kr[u].z) +
+                  qb.z * bf16_lo(kr[u].w) + qb.w * bf16_hi(kr[u].w);
+        }
+        sacc += __shfl_xor_sync(0xffffffffu, sacc, 1);
+        sacc += __shfl_xor_sync(0xffffffffu, sacc, 2);
+        if (qt == 0) ps[r * kAttnChunk + p] = p < np ? sacc * scale : -INFINITY;
+      }
+    }
+    __syncthreads();
+    __shared__ float s_scale[kAttnMaxRep];
+    if (warp < rep) {  // chunk softmax folded into head warp's running state
+      const float a0 = ps[warp * kAttnChunk + lane];
+      const float a1 = ps[warp * kAttnChunk + lane + 32];
+      float m = fmaxf(a0, a1);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      const float m_new = fmaxf(m_run, m);
+      const float e0 = lane < np ? expf(a0 - m_new) : 0.f;
+      const float e1 = lane + 32 < np ? expf(a1 - m_new) : 0.f;
+      ps[warp * kAttnChunk + lane] = e0;
+      ps[warp * kAttnChunk + lane + 32] = e1;
+      float l = e0 + e1;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+      const float f = expf(m_run - m_new);  // 0 on the first chunk
+      l_run = l_run * f + l;
+      m_run = m_new;
+      if (lane == 0) s_scale[warp] = f;
+    }
+    __syncthreads();
+    {  // O = O * f + P.V for this thread's heads and dims
+      const int r = rg * 2;
+      if (r < rep) {
+        const bool two = r + 1 < rep;
+        const float fa = s_scale[r], fb = two ? s_scale[r + 1] : 0.f;
+        oa0 *= fa; oa1 *= fa; ob0 *= fb; ob1 *= fb;
+        for (int p = 0; p < np; ++p) {
+          const uint32_t v = reinterpret_cast<const uint32_t*>(Vs + p * 128)[d2];
+          const float vl = bf16_lo(v), vh = bf16_hi(v);
+          const float w0 = ps[r * kAttnChunk + p];
+          oa0 += w0 * vl;
+          oa1 += w0 * vh;
+          if (two) {
+            const float w1 = ps[(r + 1) * kAttnChunk + p];
+            ob0 += w1 * vl;
+            ob1 += w1 * vh;
+          }
+        }
+      }
+    }
   }
-  __syncthreads();
-  float mx = -INFINITY;
-  for (int p = threadIdx.x; p < n; p += blockDim.x) mx = fmaxf(mx, sc[p]);
-  mx = breduce(mx, red, [](float a, float b) { return fmaxf(a, b); });
-  float se = 0.f;
-  for (int p = threadIdx.x; p < n; p += blockDim.x) {
-    const float e = expf(sc[p] - mx);
-    sc[p] = e;
-    se += e;
+  // partials into CTA 0's shared memory
+  float* lp = cluster.map_shared_rank(parts, 0) +
+              (size_t)rank * kAttnMaxRep * kAttnPart;
+  {
+    const int r = rg * 2;
+    if (r < rep) {
+      lp[r * kAttnPart + 2 * d2] = oa0;
+      lp[r * kAttnPart + 2 * d2 + 1] = oa1;
+      if (r + 1 < rep) {
+        lp[(r + 1) * kAttnPart + 2 * d2] = ob0;
+        lp[(r + 1) * kAttnPart + 2 * d2 + 1] = ob1;
+      }
+    }
   }
-  se = breduce(se, red, [](float a, float b) { return a + b; });
-  __syncthreads();
-  const int d = threadIdx.x;  // blockDim.x == hd
-  float acc = 0.f;
-  for (int p = 0; p < n; ++p)
-    acc += sc[p] * bf16_to_f32(vcache[((size_t)p * nkv + hk) * hd + d]);
-  out[((size_t)t * nq + hq) * hd + d] = f32_to_bf16(acc / se);
+  if (warp < rep && lane == 0) {
+    lp[warp * kAttnPart + 128] = m_run;
+    lp[warp * kAttnPart + 129] = l_run;
+  }
+  cluster.sync();
+  if (rank != 0 || !ok_n) return;
+  const int nv = min(nchunks, kAttnCluster);  // CTAs that saw positions
+  for (int r = warp; r < rep; r += kAttnThreads / 32) {
+    float M = -INFINITY;
+    for (int cc = 0; cc < nv; ++cc)
+      M = fmaxf(M, parts[(cc * kAttnMaxRep + r) * kAttnPart + 128]);
+    float Lsum = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int cc = 0; cc < nv; ++cc) {
+      const float* pp = parts + (size_t)(cc * kAttnMaxRep + r) * kAttnPart;
+      const float f = expf(pp[128] - M);
+      Lsum += f * pp[129];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) o[j] += f * pp[lane * 4 + j];
+    }
+    uint16_t* dst = out + ((size_t)t * nq + hk * rep + r) * hd + lane * 4;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) dst[j] = f32_to_bf16(o[j] / Lsum);
+  }
 }
 
-// greedy argmax over bf16 logits, ties -> lowest index
+// greedy argmax over bf16 logits, ties -> lowest index.  One CTA per token;
+// 16-byte loads, four in flight per thread, then a (value, index) reduction.
+SLX_DEV void argmax_take(float v, int i, float& best, int& bi) {
+  if (v > best || (v == best && i < bi)) {
+    best = v;
+    bi = i;
+  }
+}
+
 __global__ void __launch_bounds__(1024) k_argmax(const uint16_t* logits,
                                                   int V, int32_t* out) {
   __shared__ float rv[32];
   __shared__ int ri[32];
+  pdl_launch_dependents();
+  pdl_wait_primary();
   const int t = blockIdx.x;
   const uint16_t* l = logits + (size_t)t * V;
   float best = -INFINITY;
   int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float v = bf16_to_f32(l[i]);
-    if (v > best || (v == best && i < bi)) { best = v; bi = i; }
+  const bool vec = (V % 8 == 0) &&
+                   ((reinterpret_cast<uintptr_t>(l) & 15u) == 0);
+  if (vec) {
+    const uint4* l4 = reinterpret_cast<const uint4*>(l);
+    const int n4 = V / 8;
+    for (int b = threadIdx.x; b < n4; b += 4 * blockDim.x) {
+      uint4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int q = b + u * blockDim.x;
+        v[u] = q < n4 ? __ldcs(l4 + q) : make_uint4(0xff80ff80u, 0xff80ff80u,
+                                                   0xff80ff80u, 0xff80ff80u);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int q = b + u * blockDim.x;
+        const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          argmax_take(bf16_lo(w[j]), q * 8 + 2 * j, best, bi);
+          argmax_take(bf16_hi(w[j]), q * 8 + 2 * j + 1, best, bi);
+        }
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < V; i += blockDim.x)
+      argmax_take(bf16_to_f32(l[i]), i, best, bi);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, best, o);
     const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+    argmax_take(ov, oi, best, bi);
   }
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (lane == 0) { rv[warp] = best; ri[warp] = bi; }
+  if (lane == 0) {
+    rv[warp] = best;
+    ri[warp] = bi;
+  }
   __syncthreads();
   if (threadIdx.x == 0) {
     for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
-      if (rv[w] > best || (rv[w] == best && ri[w] < bi)) { best = rv[w]; bi = ri[w]; }
-    out[t] = bi;
+      argmax_take(rv[w], ri[w], best, bi);
+    out[t] = bi < V ? bi : 0;
   }
 }
 
@@ -216,8 +384,8 @@ int launch_add_rmsnorm(const uint16_t* h_in, const uint16_t* d,
                        uint16_t* h_out, uint16_t* y, cudaStream_t s) {
   if (H % 8 || H > 8 * kNormThreads * kNormMaxChunks) return SLX_ERR_UNSUPPORTED;
   if (T <= 0) return SLX_OK;
-  k_add_rmsnorm<<<T, kNormThreads, 0, s>>>(h_in, d, w, H, eps, h_out, y);
-  return cudaGetLastError() == cudaSuccess ? SLX_OK : SLX_ERR_CUDA;
+  return launch_k(k_add_rmsnorm, dim3(T), dim3(kNormThreads), 0, s, h_in, d, w,
+                  H, eps, h_out, y) == cudaSuccess ? SLX_OK : SLX_ERR_CUDA;
 }
 
 int launch_qk_rope_cache(uint16_t* qkv, int T, int nq, int nkv, int hd,
@@ -228,9 +396,10 @@ int launch_qk_rope_cache(uint16_t* qkv, int T, int nq, int nkv, int hd,
   if (hd != 128) return SLX_ERR_UNSUPPORTED;
   if (T <= 0) return SLX_OK;
   dim3 grid(T, nq + 2 * nkv);
-  k_qk_rope_cache<<<grid, hd / 2, 0, s>>>(qkv, nq, nkv, hd, qn, kn, eps,
-                                          inv_freq, pos, max_len, kc, vc,
-                                          status);
+  const cudaError_t e = launch_k(k_qk_rope_cache, grid, dim3(hd / 2), 0, s,
+                                 qkv, nq, nkv, hd, qn, kn, eps, inv_freq, pos,
+                                 max_len, kc, vc, status);
+  if (e != cudaSuccess) return SLX_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? SLX_OK : SLX_ERR_CUDA;
 }
 
@@ -238,24 +407,29 @@ int launch_attn_decode(const uint16_t* qkv, int T, int nq, int nkv, int hd,
                        const uint16_t* kc, const uint16_t* vc,
                        const int32_t* pos, int max_len, uint16_t* out,
                        cudaStream_t s) {
-  if (hd != 128 || nq % nkv) return SLX_ERR_UNSUPPORTED;
+  if (hd != 128 || nq % nkv || nq / nkv > kAttnMaxRep) return SLX_ERR_UNSUPPORTED;
   if (T <= 0) return SLX_OK;
-  const int smem = max_len * 4;
-  if (smem > 200 * 1024) return SLX_ERR_UNSUPPORTED;
-  if (smem > 48 * 1024)
-    cudaFuncSetAttribute(k_attn_decode,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  dim3 grid(T, nq);
-  k_attn_decode<<<grid, hd, smem, s>>>(qkv, nq, nkv, hd, kc, vc, pos, max_len,
-                                       1.0f / sqrtf((float)hd), out);
-  return cudaGetLastError() == cudaSuccess ? SLX_OK : SLX_ERR_CUDA;
+  if (T > 65535 || nkv > 65535) return SLX_ERR_INVALID;
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(k_attn_decode,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kAttnSmem) != cudaSuccess)
+      return SLX_ERR_CUDA;
+    configured = true;
+  }
+  dim3 grid(kAttnCluster, nkv, T);
+  const cudaError_t e = launch_k(k_attn_decode, grid, dim3(kAttnThreads),
+                                 (size_t)kAttnSmem, s, qkv, nq, nkv, hd, kc, vc,
+                                 pos, max_len, 1.0f / sqrtf((float)hd), out);
+  return e == cudaSuccess ? SLX_OK : SLX_ERR_CUDA;
 }
 
 int launch_argmax(const uint16_t* logits, int T, int V, int32_t* out,
                   cudaStream_t s) {
   if (T <= 0) return SLX_OK;
-  k_argmax<<<T, 1024, 0, s>>>(logits, V, out);
-  return cudaGetLastError() == cudaSuccess ? SLX_OK : SLX_ERR_CUDA;
+  return launch_k(k_argmax, dim3(T), dim3(1024), 0, s, logits, V, out) ==
+                 cudaSuccess ? SLX_OK : SLX_ERR_CUDA;
 }
 
 }  // namespace slx

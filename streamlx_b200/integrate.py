@@ -94,11 +94,26 @@ class StreamingSwitchGLU:
             self._pf_next = None
             return None
 
-    def route(self, idx: np.ndarray, pred=None) -> str:
+    def start_prefetch(self, pred) -> None:
+        """Start the next layer's prefetch from a prediction (ids, scores):
+        ids ordered by score, stable (integrate.py:255-260)."""
+        if pred is None or self._pf_next is None:
+            return
+        pi = np.asarray(pred[0]).reshape(-1)
+        ps = np.asarray(pred[1]).reshape(-1)
+        ordered = list(dict.fromkeys(
+            int(pi[j]) for j in np.argsort(-ps, kind="stable")))
+        self._pf_next[0].prefetch_start(ordered, _pf_ex())
+
+    def route(self, idx: np.ndarray, pred=None,
+              start_prefetch: bool = True) -> str:
         """Pool bookkeeping of one call (no device work except slot fills).
         idx: [B, T, k] routed expert ids (host).  pred: next-layer
         prediction (ids, scores) for decode, or None.  Returns "pool" when the
-        call's experts are resident, else the prefill mode to run."""
+        call's experts are resident, else the prefill mode to run.
+        ``start_prefetch=False``: the caller has already started this call's
+        next-layer prefetch (it touches only the next pool, whose state no
+        call in between changes)."""
         pool = self.pool
         decode = idx.shape[0] * idx.shape[1] == 1
         if self.record_sink is not None:
@@ -117,12 +132,8 @@ class StreamingSwitchGLU:
                     pool.ensure(miss)
                 else:
                     pool.ensure(uniq)
-                if pred is not None and self._pf_next is not None:
-                    pi = np.asarray(pred[0]).reshape(-1)
-                    ps = np.asarray(pred[1]).reshape(-1)
-                    ordered = list(dict.fromkeys(
-                        int(pi[j]) for j in np.argsort(-ps, kind="stable")))
-                    self._pf_next[0].prefetch_start(ordered, _pf_ex())
+                if start_prefetch:
+                    self.start_prefetch(pred)
             else:
                 pool.ensure(uniq)
             return "pool"

@@ -156,8 +156,11 @@ class SynthDecoder:
         self.n_pos = 0
         self.use_graphs = cfg.has_trunk
         self.pipeline = True
+        self.pdl = True             # captured kernels chain with PDL
+        self.glu_events = True      # time every SwitchGLU pair in the graphs
         self._graphs = None
         self._pending = None
+        self._pf_done = 0
         self.glu_times: list | None = None
         # temporal-reuse routing override of the workloads: per (token,
         # layer) a seeded coin decides whether the previous token's expert
@@ -295,6 +298,7 @@ class SynthDecoder:
         self.g_s = torch.zeros(n, 1, H, dtype=bf, device=dev)
         self.g_m = torch.zeros(n, 1, H, dtype=bf, device=dev)
         self.g_d = torch.zeros(n, 1, H, dtype=bf, device=dev)
+        self.g_xm = torch.zeros(n, 1, H, dtype=bf, device=dev)  # MoE input
         self.g_emb = torch.zeros(1, H, dtype=bf, device=dev)
         self.g_fin = torch.zeros(1, H, dtype=bf, device=dev)
         # device log, read back with one copy per launch cycle:
@@ -326,13 +330,14 @@ class SynthDecoder:
         self.g_glu_scratch = torch.zeros(
             L.switchglu_scratch_bytes(1, k, cfg.inter, s_inter),
             dtype=torch.uint8, device=dev)
+        self._side = torch.cuda.Stream(device=dev)   # predictor branch
         self.g_ev = [(torch.cuda.Event(enable_timing=True),
                       torch.cuda.Event(enable_timing=True)) for _ in range(n)]
         for pair in self.g_ev:      # torch creates the CUDA event on first use
             for e in pair:
                 e.record()
 
-    def _record_layer(self, i: int) -> None:
+    def _record_layer(self, i: int, join: bool = True) -> None:
         cfg = self.cfg
         n, k, H, bits = cfg.layers, cfg.top_k, cfg.hidden, cfg.trunk_bits
         la = self.layers[i]
@@ -345,7 +350,6 @@ class SynthDecoder:
             h_in, d_in = self.g_emb, None
         else:
             h_in, d_in = self.g_m[i - 1], self.g_d[i - 1]
-        self.g_lstatus[i:i + 1].zero_()
         L.add_rmsnorm_out(h_in, d_in, la.w_in, eps, self.g_s[i], self.x)
         L.qlinear(la.w_qkv, la.n_qkv, H, bits, self.x, self.qkv,
                   self.g_status)
@@ -358,28 +362,55 @@ class SynthDecoder:
                       self.att)
         L.qlinear(la.w_o, H, cfg.heads * cfg.head_dim, bits, self.att,
                   self.o, self.g_status)
+        xm = self.g_xm[i]
         L.add_rmsnorm_out(self.g_s[i], self.o, la.post_attention_layernorm,
-                          eps, self.g_m[i], self.x)
-        L.router_topk(self.x, blk.w_gate, blk.bias, k, cfg.norm_topk_prob,
-                      self.g_ids[i], self.g_scores[i], blk.scratch,
-                      self.g_status, force=self.g_ctrl[1 + i:2 + i],
-                      forced_ids=self.g_prev_ids[i])
+                          eps, self.g_m[i], xm)
+        L.router_topk_multi(
+            xm, [L.router_head(blk.w_gate, blk.bias, self.g_ids[i],
+                               self.g_scores[i], blk.scratch,
+                               force=self.g_ctrl[1 + i:2 + i],
+                               forced_ids=self.g_prev_ids[i])],
+            cfg.n_experts, k, cfg.norm_topk_prob, self.g_status)
         if blk.pf_link is not None:
+            # the next-layer predictor only feeds the host's prefetch: it
+            # runs on a side branch, off the layer's critical path
             ratio, nxt = blk.pf_link
-            L.router_topk(self.x, nxt.w_gate, nxt.bias, k, cfg.norm_topk_prob,
-                          self.g_pf_ids[i], self.g_pf_scores[i],
-                          blk.pf_scratch, self.g_status, ratio=ratio)
+            cur = torch.cuda.current_stream(self.device)
+            self._side.wait_stream(cur)
+            self._forked = True
+            prev = L.set_pdl(False)
+            try:
+                with torch.cuda.stream(self._side):
+                    L.router_topk_multi(
+                        xm, [L.router_head(nxt.w_gate, nxt.bias,
+                                           self.g_pf_ids[i],
+                                           self.g_pf_scores[i],
+                                           blk.pf_scratch, ratio=ratio)],
+                        cfg.n_experts, k, cfg.norm_topk_prob, self.g_status)
+            finally:
+                L.set_pdl(prev)
         pool = w.pool
         sh = w.shared
         ev = self.g_ev[i]
-        L.event_record_external(ev[0])
-        ops.switchglu(pool.store.bank, self.x, self.g_ids[i], k,
+        if self.glu_events:
+            L.event_record_external(ev[0])
+        ops.switchglu(pool.store.bank, xm, self.g_ids[i], k,
                       scores=self.g_scores[i], table=pool.store.table_dev,
                       shared=sh[0] if sh else None, out=self.g_d[i],
                       inter=pool.inter, shared_inter=sh[2] if sh else 0,
                       scratch_buf=self.g_glu_scratch,
                       status=self.g_lstatus[i:i + 1])
-        L.event_record_external(ev[1])
+        if self.glu_events:
+            L.event_record_external(ev[1])
+        if join:
+            self._join_side()
+
+    def _join_side(self) -> None:
+        """Rejoin the predictor branch (only if this recording forked it:
+        a capture may not wait on work from outside itself)."""
+        if getattr(self, "_forked", False):
+            torch.cuda.current_stream(self.device).wait_stream(self._side)
+            self._forked = False
 
     def _record_tail(self) -> None:
         cfg = self.cfg
@@ -416,6 +447,18 @@ class SynthDecoder:
             self._record_tail()
         s.synchronize()
         mode = "thread_local"
+        prev_pdl = L.set_pdl(self.pdl)
+        try:
+            graphs, tail, full = self._capture_graphs(s, mode)
+        finally:
+            L.set_pdl(prev_pdl)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        self._graphs = (graphs, tail, full)
+        self.g_status.zero_()
+        self.g_lstatus.zero_()
+
+    def _capture_graphs(self, s, mode):
+        n = self.cfg.layers
         graphs = []
         for i in range(n):
             g = torch.cuda.CUDAGraph()
@@ -427,13 +470,12 @@ class SynthDecoder:
             self._record_tail()
         full = torch.cuda.CUDAGraph()
         with torch.cuda.graph(full, stream=s, capture_error_mode=mode):
+            self.g_lstatus.zero_()
             for i in range(n):
-                self._record_layer(i)
+                self._record_layer(i, join=False)
+            self._join_side()
             self._record_tail()
-        torch.cuda.current_stream(self.device).wait_stream(s)
-        self._graphs = (graphs, tail, full)
-        self.g_status.zero_()
-        self.g_lstatus.zero_()
+        return graphs, tail, full
 
     def _graph_kernels(self, start: int) -> int:
         """Library kernels one launch from layer `start` runs."""
@@ -447,6 +489,7 @@ class SynthDecoder:
         if start == 0:
             full.replay()
         else:
+            self.g_lstatus[start:].zero_()
             for i in range(start, self.cfg.layers):
                 graphs[i].replay()
             tail.replay()
@@ -462,30 +505,46 @@ class SynthDecoder:
         return log
 
     def _glu_timing(self, start: int) -> None:
-        if self.glu_times is None:
+        if self.glu_times is None or not self.glu_events:
             return
         ev = self.g_ev[start:]
         self.glu_times.extend(
             L.event_elapsed_many([e[0] for e in ev], [e[1] for e in ev])
             .tolist())
 
-    def _replay(self, log: np.ndarray, start: int) -> int | None:
-        """Pool bookkeeping of layers start.. from a log; returns the first
-        layer that must run again (its slots are now filled) or None."""
+    def _prefetch_upto(self, log: np.ndarray) -> None:
+        """Start the next-layer prefetches of this step's layers whose logged
+        prediction is final (every layer up to and including the first
+        unmapped one), in layer order.  Layer i's prefetch touches only pool
+        i+1, and nothing changes pool i+1 between the previous step's call of
+        layer i+1 (already replayed) and this step's, so starting them here,
+        before this step's bookkeeping, gives the reference's per-pool order
+        while the reads overlap the bookkeeping and the next step."""
         n, k = self.cfg.layers, self.cfg.top_k
-        ids = log[:n * k].reshape(n, 1, 1, k)
+        lst = log[self._lst_off:self._lst_off + n]
+        bad = np.flatnonzero(lst == self._UNMAPPED)
+        upto = n if bad.size == 0 else int(bad[0]) + 1
         pf_ids = log[n * k:2 * n * k].reshape(n, k)
         pf_sc = log[2 * n * k:3 * n * k].view(np.float32).reshape(n, k)
+        for i in range(self._pf_done, upto):
+            w = self.layers[i].mlp.switch_mlp
+            if self.layers[i].mlp.pf_link is not None and w.pred_gate():
+                w.start_prefetch((pf_ids[i].copy(), pf_sc[i].copy()))
+        self._pf_done = max(self._pf_done, upto)
+
+    def _replay(self, log: np.ndarray, start: int) -> int | None:
+        """Pool bookkeeping of layers start.. from a log; returns the first
+        layer that must run again (its slots are now filled) or None.  The
+        layers' prefetches were started by _prefetch_upto."""
+        n, k = self.cfg.layers, self.cfg.top_k
+        ids = log[:n * k].reshape(n, 1, 1, k)
         lst = log[self._lst_off:self._lst_off + n]
         for i in range(start, n):
             code = int(lst[i])
             if code not in (0, self._UNMAPPED):
                 raise L.SlxError("device", code, f"layer {i} SwitchGLU")
             w = self.layers[i].mlp.switch_mlp
-            pred = None
-            if self.layers[i].mlp.pf_link is not None and w.pred_gate():
-                pred = (pf_ids[i].copy(), pf_sc[i].copy())
-            if w.route(ids[i].copy(), pred) != "pool":
+            if w.route(ids[i].copy(), None, start_prefetch=False) != "pool":
                 raise RuntimeError("decode call routed more experts than "
                                    "the pool has slots")
             w.pool.sync_device()
@@ -524,6 +583,8 @@ class SynthDecoder:
         self.flush()
         log = self._read_log()
         self._glu_timing(0)
+        self._pf_done = 0
+        self._prefetch_upto(log)
         lst = log[self._lst_off:self._lst_off + n]
         if self.pipeline and not (lst == self._UNMAPPED).any():
             self._pending = log
@@ -536,6 +597,7 @@ class SynthDecoder:
                 self._launch(redo)
                 log = self._read_log()
                 self._glu_timing(redo)
+                self._prefetch_upto(log)
                 if int(log[self._lst_off + redo]) != 0:
                     raise RuntimeError(f"layer {redo} still unmapped after "
                                        "its slots were filled")

@@ -333,3 +333,66 @@ def test_trunk_kernels(dev):
     L.argmax(bf16_tensor(lg, dev), out)
     torch.cuda.synchronize()
     assert out.cpu().tolist() == [OT.argmax_first(lg[0]), 77]
+
+
+def test_router_two_heads_one_launch(dev):
+    """Router + next-layer predictor in one launch equal two single calls."""
+    T, H, E, k = 3, 2048, 256, 8
+    rng = np.random.default_rng(11)
+    x = bf16_tensor(A.bf16_round(rng.standard_normal((T, H))
+                                 .astype(np.float32)), dev)
+    ws = [bf16_tensor(A.bf16_round((rng.standard_normal((E, H)) / np.sqrt(H))
+                                   .astype(np.float32)), dev) for _ in range(2)]
+    bs = [torch.from_numpy(synth.zipf_bias(E, 1.0, s)).to(dev) for s in (1, 2)]
+    ratio = bf16_tensor(A.bf16_round((1 + 0.05 * rng.standard_normal(H))
+                                     .astype(np.float32)), dev)
+    force = torch.tensor([0, 1, 0], dtype=torch.int32, device=dev)
+    forced = torch.from_numpy(np.stack([rng.choice(E, k, replace=False)
+                                        for _ in range(T)]).astype(np.int32)
+                              ).to(dev)
+    st = _status(dev)
+
+    def outs():
+        return (torch.empty(T, k, dtype=torch.int32, device=dev),
+                torch.empty(T, k, dtype=torch.float32, device=dev),
+                torch.zeros(L.router_scratch_bytes(T, E), dtype=torch.uint8,
+                            device=dev))
+    single = [outs(), outs()]
+    L.router_topk(x, ws[0], bs[0], k, True, *single[0], st, force=force,
+                  forced_ids=forced)
+    L.router_topk(x, ws[1], bs[1], k, True, *single[1], st, ratio=ratio)
+    multi = [outs(), outs()]
+    for _ in range(2):      # tickets left at zero for the next call
+        heads = [L.router_head(ws[0], bs[0], *multi[0], force=force,
+                               forced_ids=forced),
+                 L.router_head(ws[1], bs[1], *multi[1], ratio=ratio)]
+        L.router_topk_multi(x, heads, E, k, True, st)
+        torch.cuda.synchronize()
+        assert st.item() == 0
+        for a, b in zip(single, multi):
+            assert torch.equal(a[0], b[0])
+            assert torch.equal(a[1], b[1])
+
+
+@pytest.mark.parametrize("nq,nkv", [(16, 2), (24, 4), (4, 2)])
+def test_attn_decode_chunks(dev, nq, nkv):
+    """Split-K attention over chunk boundaries (64 positions per chunk)."""
+    hd, maxlen = 128, 300
+    rng = np.random.default_rng(nq)
+    kc_np = A.bf16_round(rng.standard_normal((maxlen, nkv, hd))
+                         .astype(np.float32))
+    vc_np = A.bf16_round(rng.standard_normal((maxlen, nkv, hd))
+                         .astype(np.float32))
+    kc, vc = bf16_tensor(kc_np, dev), bf16_tensor(vc_np, dev)
+    for p in (0, 63, 64, 127, 130, 299):
+        qkv = A.bf16_round(rng.standard_normal((1, (nq + 2 * nkv) * hd))
+                           .astype(np.float32))
+        att = torch.empty(1, nq * hd, dtype=torch.bfloat16, device=dev)
+        pos = torch.tensor([p], dtype=torch.int32, device=dev)
+        for _ in range(2):          # tickets left at zero for the next call
+            L.attn_decode(bf16_tensor(qkv, dev), nq, nkv, hd, kc, vc, pos,
+                          att)
+        torch.cuda.synchronize()
+        want = OT.attn_decode(qkv[0, :nq * hd].reshape(nq, hd), kc_np, vc_np,
+                              p + 1, nq, nkv)
+        check_close(bf16_np(att).reshape(nq, hd), want)
