@@ -12,9 +12,10 @@ token, then W warm-up and K timed decode steps (one step = one token).
 Output: one JSON line (rank 0).  ``value`` is device-timed tokens/s (token
 kept on the GPU between steps); ``e2e`` is the same loop through the public
 step API with the token copied host->device and the sampled token read back
-every step.  ``roofline`` times every SwitchGLU launch pair inside the timed
-region with CUDA events (algorithmic bytes = routed experts + shared expert
-+ activations per launch) against the measured HBM copy peak.
+every step.  ``roofline`` times the SwitchGLU launch pairs of one layer in
+eight inside the timed region with CUDA events recorded as graph nodes
+(algorithmic bytes = routed experts + shared expert + activations per
+launch) against the measured HBM copy peak.
 ``cpu_baseline`` times the CPU oracle decoder on a bounded sample.
 
 ``--impl reference`` times the reference's path restated on the CPU (the
@@ -345,6 +346,7 @@ def run_ours(args) -> None:
                      "traffic": traffic,
                      "algorithmic_bytes_per_launch": per_launch,
                      "launches_timed": len(durs),
+                     "sampling": "layers 3, 11, 19, 27, 35 of every step",
                      "mean_launch_us": round(1000 * mean_ms, 2)},
         "gpu_launches": launches,
         "clocks": clk,

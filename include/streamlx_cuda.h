@@ -38,6 +38,7 @@ extern "C" {
 #define SLX_ERR_UNMAPPED_EXPERT (-5) /* device: expert id has no pool slot */
 #define SLX_ERR_DEVICE_TIMEOUT (-6)  /* device: a bounded wait expired */
 #define SLX_ERR_SCRATCH (-7)         /* scratch buffer too small */
+#define SLX_ERR_IO (-8)              /* host file read failed or was short */
 
 #define SLX_GEMV_GLU 0
 #define SLX_GEMV_LINEAR 1
@@ -127,6 +128,18 @@ int slx_switchglu(const slx_expert_bank* bank, const slx_shared_expert* shared,
                   const float* scores, const int32_t* slot_table, int n_table,
                   void* out, void* scratch, size_t scratch_bytes,
                   int32_t* status, void* stream);
+
+/* Decode calls (T == 1) of slx_switchglu run both phases in one cooperative
+ * launch when the token's tiles fit one CTA per SM; the first 256 bytes of
+ * the scratch hold that launch's grid-barrier words and must be zero before
+ * the first call (every call, of any shape, leaves them reusable).  on = 0 forces the
+ * two-launch path for the calling host thread.  Returns the previous
+ * setting. */
+int slx_set_switchglu_fused(int on);
+
+/* Kernels the calling thread's last successful slx_switchglu launched
+ * (1 fused, 2 two-phase; launch accounting). */
+int slx_switchglu_last_kernels(void);
 
 /* Dense quantized linear y[T, out] = x[T, in] @ dequant(W)^T (bf16 out,
  * fp32 accumulate) over a tile-format matrix (slx_pack_dense).  Trunk
@@ -230,6 +243,16 @@ int slx_attn_decode(const void* qkv, int T, int n_q, int n_kv, int head_dim,
                     const void* k_cache, const void* v_cache,
                     const int32_t* pos, int max_len, void* out, void* stream);
 int slx_argmax(const void* logits, int T, int V, int32_t* out, void* stream);
+
+/* Read n byte ranges of files: fds[i] from offsets[i], sizes[i] bytes,
+ * into dsts[i], on up to `threads` native threads (a pool shared by all
+ * callers; the caller works too).  Replaces the per-span os.pread tasks of
+ * streamlx/reader.py:80-100.  Returns SLX_ERR_IO with *failed_index and
+ * *failed_errno (0 = end of file before the range ended) on the first
+ * failure.  Host code only: usable without a GPU. */
+int slx_pread_many(const int* fds, const int64_t* offsets,
+                   const int64_t* sizes, void* const* dsts, int n, int threads,
+                   int* failed_index, int* failed_errno);
 
 /* Issue n host->device / device->device / device->host copies, one
  * cudaMemcpyAsync each, on `stream` (host arrays of device/host pointers).

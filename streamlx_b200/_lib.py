@@ -20,7 +20,7 @@ SLX_OK = 0
 ERRORS = {
     -1: "SLX_ERR_INVALID", -2: "SLX_ERR_UNSUPPORTED", -3: "SLX_ERR_CUDA",
     -4: "SLX_ERR_OUT_OF_RANGE", -5: "SLX_ERR_UNMAPPED_EXPERT",
-    -6: "SLX_ERR_DEVICE_TIMEOUT", -7: "SLX_ERR_SCRATCH",
+    -6: "SLX_ERR_DEVICE_TIMEOUT", -7: "SLX_ERR_SCRATCH", -8: "SLX_ERR_IO",
 }
 GEMV_GLU, GEMV_LINEAR = 0, 1
 
@@ -34,7 +34,8 @@ EXPORTS = (
     "slx_qk_norm_rope_cache", "slx_attn_decode", "slx_argmax",
     "slx_copy_many", "slx_router_topk_noalloc", "slx_add_rmsnorm_out",
     "slx_event_record_external", "slx_event_elapsed_many",
-    "slx_router_topk_multi", "slx_set_pdl",
+    "slx_router_topk_multi", "slx_set_pdl", "slx_pread_many",
+    "slx_set_switchglu_fused", "slx_switchglu_last_kernels",
 )
 
 
@@ -91,6 +92,9 @@ def lib() -> C.CDLL:
         L.slx_version.restype = i32
         L.slx_set_pdl.restype = i32
         L.slx_set_pdl.argtypes = [i32]
+        L.slx_set_switchglu_fused.restype = i32
+        L.slx_set_switchglu_fused.argtypes = [i32]
+        L.slx_switchglu_last_kernels.restype = i32
         L.slx_last_error_string.restype = C.c_char_p
         L.slx_expert_tiled_bytes.restype = sz
         L.slx_expert_tiled_bytes.argtypes = [i32, i32, i32]
@@ -144,6 +148,9 @@ def lib() -> C.CDLL:
                                       vp, vp]
         L.slx_argmax.restype = i32
         L.slx_argmax.argtypes = [vp, i32, i32, vp, vp]
+        L.slx_pread_many.restype = i32
+        L.slx_pread_many.argtypes = [vp, vp, vp, vp, i32, i32,
+                                     C.POINTER(C.c_int), C.POINTER(C.c_int)]
         L.slx_copy_many.restype = i32
         L.slx_copy_many.argtypes = [vp, vp, vp, i32, vp]
         _lib = L
@@ -154,6 +161,11 @@ def set_pdl(on: bool) -> bool:
     """Programmatic dependent launch for this thread's next launches;
     returns the previous setting."""
     return bool(lib().slx_set_pdl(1 if on else 0))
+
+
+def set_switchglu_fused(on: bool) -> bool:
+    """Decode SwitchGLU as one cooperative launch (default) or two."""
+    return bool(lib().slx_set_switchglu_fused(1 if on else 0))
 
 
 def _check(fn: str, rc: int) -> None:
@@ -248,7 +260,7 @@ def switchglu(bank: slx_expert_bank, x: torch.Tensor, ids: torch.Tensor,
         out.data_ptr(), scratch.data_ptr(), scratch.numel() * scratch.element_size(),
         status.data_ptr(), stream_ptr(stream))
     _check("slx_switchglu", rc)
-    _count(2)
+    _count(lib().slx_switchglu_last_kernels())
 
 
 def qlinear(w_tiled: torch.Tensor, out_features: int, in_features: int,
@@ -382,6 +394,19 @@ def argmax(logits, out, stream=None) -> None:
                           stream_ptr(stream))
     _check("slx_argmax", rc)
     _count(1)
+
+
+def pread_many(fds: np.ndarray, offsets: np.ndarray, sizes: np.ndarray,
+               dsts: np.ndarray, threads: int) -> tuple[int, int, int]:
+    """Native batched pread (host only).  Arrays: int32 fds, int64 offsets
+    and sizes, uint64 destination addresses.  Returns (rc, failed index,
+    errno of the failure, 0 = end of file)."""
+    n = len(fds)
+    fi, fe = C.c_int(-1), C.c_int(0)
+    rc = lib().slx_pread_many(fds.ctypes.data, offsets.ctypes.data,
+                              sizes.ctypes.data, dsts.ctypes.data, n, threads,
+                              C.byref(fi), C.byref(fe))
+    return int(rc), fi.value, fe.value
 
 
 def copy_many(dsts: list[int], srcs: list[int], sizes: list[int],

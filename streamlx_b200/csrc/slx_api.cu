@@ -15,6 +15,8 @@ namespace {
 
 thread_local std::string g_err;
 thread_local int g_pdl = 0;
+thread_local int g_fused = 1;
+thread_local int g_glu_kernels = 0;  // kernels the last slx_switchglu launched
 
 int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -71,7 +73,9 @@ const char* slx_last_error_string(void) { return g_err.c_str(); }
 size_t slx_switchglu_scratch_bytes(int T, int k, int inter, int shared_inter) {
   if (T < 0 || k < 0 || inter < 0 || shared_inter < 0) return 0;
   const size_t u = (size_t)T * k, ng = inter / 64, ngs = shared_inter / 64;
-  return align256(u * ng * 128) + align256(u * ng * 16) +
+  // the first 256 bytes: grid-barrier words of the fused decode kernel (at
+  // a fixed place, so calls of any shape sharing one scratch agree on them)
+  return 256 + align256(u * ng * 128) + align256(u * ng * 16) +
          align256((size_t)T * ngs * 128) + align256((size_t)T * ngs * 16);
 }
 
@@ -168,6 +172,8 @@ int slx_switchglu(const slx_expert_bank* bank, const slx_shared_expert* shared,
     return fail(SLX_ERR_SCRATCH, "scratch %zu < %zu bytes", scratch_bytes, need);
   const size_t nu = (size_t)T * k, ng = I / 64, ngs = Is / 64;
   uint8_t* sp = reinterpret_cast<uint8_t*>(scratch);
+  int* gbar = reinterpret_cast<int*>(sp);
+  sp += 256;
   uint32_t* hfrag = reinterpret_cast<uint32_t*>(sp);
   sp += align256(nu * ng * 128);
   float* hpart = reinterpret_cast<float*>(sp);
@@ -202,8 +208,6 @@ int slx_switchglu(const slx_expert_bank* bank, const slx_shared_expert* shared,
   a.shared_part_floats = (int)ngs * 4;
   a.status = status;
   a.n_tiles = T * k * (I / 16) + T * (Is / 16);
-  int rc = slx::launch_gemv(a, bits, s, /*pdl_secondary=*/true);
-  if (rc) return cuda_check(rc, "slx_switchglu gate/up");
 
   slx::DownArgs d = {};
   d.T = T;
@@ -232,8 +236,33 @@ int slx_switchglu(const slx_expert_bank* bank, const slx_shared_expert* shared,
   d.n_items = T * (H / 16);
   d.n_units = k + (Is > 0 ? 1 : 0);
   d.pdl = 1;
+  int rc = SLX_ERR_UNSUPPORTED;
+  if (g_fused && T == 1) {
+    // one cooperative launch for both phases when the token's tiles fit
+    d.tile_bytes = (int)slx::single_tile_bytes(I, bits);
+    d.tile_bytes_sh = Is ? (int)slx::single_tile_bytes(Is, bits) : 0;
+    d.a_bytes = (long long)slx::expert_a_bytes(H, I, bits);
+    d.a_bytes_sh = Is ? (long long)slx::expert_a_bytes(H, Is, bits) : 0;
+    rc = slx::launch_switchglu_fused(a, d, gbar, bits, s);
+    if (rc != SLX_ERR_UNSUPPORTED) {
+      g_glu_kernels = rc ? 0 : 1;
+      return rc ? cuda_check(rc, "slx_switchglu fused") : SLX_OK;
+    }
+  }
+  g_glu_kernels = 0;
+  rc = slx::launch_gemv(a, bits, s, /*pdl_secondary=*/true);
+  if (rc) return cuda_check(rc, "slx_switchglu gate/up");
   rc = slx::launch_down(d, bits, s);
+  if (!rc) g_glu_kernels = 2;
   return rc ? cuda_check(rc, "slx_switchglu down") : SLX_OK;
+}
+
+int slx_switchglu_last_kernels(void) { return g_glu_kernels; }
+
+int slx_set_switchglu_fused(int on) {
+  const int prev = g_fused;
+  g_fused = on ? 1 : 0;
+  return prev;
 }
 
 int slx_qlinear(const void* w_tiled, int out_features, int in_features,

@@ -36,7 +36,7 @@
 #include "slx_tiles.cuh"
 
 #ifdef SLX_TRACE
-__device__ unsigned long long g_slx_trace[3][160][16];
+static __device__ unsigned long long g_slx_trace[3][160][16];
 extern "C" int slx_trace_read(unsigned long long* host) {
   return cudaMemcpyFromSymbol(host, g_slx_trace, sizeof(g_slx_trace)) ==
                  cudaSuccess ? 0 : -1;
@@ -227,13 +227,13 @@ SLX_DEV void gemv_issue(const GemvArgs& a, const TileInfo& t, uint8_t* dst,
 // Reduce the tile's partials (red[w][lane], w < kNW) and write its output.
 // Lane (g, tig): tig>>1 selects the matrix (gate/up or rows 0-15/16-31),
 // tig&1 the row half.  All 32 lanes must call this.
-template <int BITS>
+template <int BITS, int NWR = kNW>
 SLX_DEV void gemv_epilogue(const GemvArgs& a, const TileInfo& t,
                            const float* red, int lane) {
   const int g = lane >> 2, tig = lane & 3;
   float v = 0.f;
 #pragma unroll
-  for (int w = 0; w < kNW; ++w) v += red[w * 32 + lane];
+  for (int w = 0; w < NWR; ++w) v += red[w * 32 + lane];
   if (a.mode != SLX_GEMV_GLU) {
     const int mat = tig >> 1;
     const int r = 16 * mat + g + 8 * (tig & 1);
@@ -511,8 +511,11 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
     };
     const int first = total < NS ? total : NS;
+    if (lane == 0) SLX_TRACE_AT(1, 12, globaltimer_ns());
     for (int base = 0; base < first; base += 32)
       if (base + lane < first) issue(base + lane);
+    __syncwarp();
+    if (lane == 0) SLX_TRACE_AT(1, 13, globaltimer_ns());  // issued
     for (int it = 0; it < n_it; ++it) {
       const int b = it & 1;
       if (!mbar_wait(&itemfull[b], (it >> 1) & 1, a.status)) break;
@@ -609,30 +612,32 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int b = it & 1;
     if (it >= 2) mbar_wait(&itemempty[b], ((it >> 1) - 1) & 1, a.status);
     float* rd = red + (size_t)b * kNW * U * kRows;
-    for (int j = 0; j < U; j += 2) {
-      const bool pair = j + 1 < U;
-      const int s0 = (it * U + j) % NS, s1 = (it * U + j + 1) % NS;
-      const bool ok0 = mbar_wait(&full[s0], ((it * U + j) / NS) & 1, a.status);
-      const bool ok1 = pair ? mbar_wait(&full[s1], ((it * U + j + 1) / NS) & 1,
-                                        a.status)
-                            : false;
-      float acc0 = 0.f, acc1 = 0.f;
-      if (ok0)
-        acc0 = down_unit_groups<BITS>(stages + (size_t)s0 * a.stage_bytes,
-                                      j >= a.k ? a.Is : a.I, cw, g, tig, rrow,
-                                      frag + (size_t)j * nGmax * 32,
-                                      xsum + (size_t)j * nGmax);
-      if (ok1)
-        acc1 = down_unit_groups<BITS>(stages + (size_t)s1 * a.stage_bytes,
-                                      j + 1 >= a.k ? a.Is : a.I, cw, g, tig,
-                                      rrow, frag + (size_t)(j + 1) * nGmax * 32,
-                                      xsum + (size_t)(j + 1) * nGmax);
-      if (tig < 2) {
-        rd[((size_t)cw * U + j) * kRows + rrow] = acc0;
-        if (pair) rd[((size_t)cw * U + j + 1) * kRows + rrow] = acc1;
+    // every tile of the item was requested long before phase A finished:
+    // wait for all of them, then compute the units back to back (no
+    // barrier between units, so their loads and MMAs overlap)
+    bool ok_all = true;
+    for (int j = 0; j < U; ++j)
+      ok_all &= mbar_wait(&full[(it * U + j) % NS], ((it * U + j) / NS) & 1,
+                          a.status);
+    if (it == 0) SLX_TRACE_POINT(1, 8);
+    for (int j0 = 0; j0 < U; j0 += 3) {
+      float acc[3] = {0.f, 0.f, 0.f};
+#pragma unroll
+      for (int u = 0; u < 3; ++u) {
+        const int j = j0 + u;
+        if (j < U && ok_all)
+          acc[u] = down_unit_groups<BITS>(
+              stages + (size_t)((it * U + j) % NS) * a.stage_bytes,
+              j >= a.k ? a.Is : a.I, cw, g, tig, rrow,
+              frag + (size_t)j * nGmax * 32, xsum + (size_t)j * nGmax);
       }
-      if (it == 0 && j < 20) SLX_TRACE_POINT(1, 3 + j / 2);
+      if (tig < 2) {
+#pragma unroll
+        for (int u = 0; u < 3; ++u)
+          if (j0 + u < U) rd[((size_t)cw * U + j0 + u) * kRows + rrow] = acc[u];
+      }
     }
+    if (it == 0) SLX_TRACE_POINT(1, 9);
     __syncwarp();
     if (lane == 0) mbar_arrive(&itemfull[b]);
   }
@@ -649,6 +654,400 @@ static int num_sms() {
     if (g_num_sms <= 0) g_num_sms = 148;
   }
   return g_num_sms;
+}
+
+// ------------------------------------------------ fused decode SwitchGLU ---
+//
+// One cooperative launch does both phases for a single token (decode):
+//   start   warp 0 requests every gate/up tile and every down tile this CTA
+//           will need (one bulk copy each, all in flight at once); the 16
+//           compute warps build the activation fragments meanwhile;
+//   phase A the compute warps take 64-column groups G = w, w+16, ... of each
+//           of the CTA's gate/up tiles; one warp per tile reduces the
+//           partials and writes SwiGLU(h) as down-projection fragments;
+//   barrier every CTA has written its fragments (grid-wide arrive/wait on a
+//           counter in scratch, bounded);
+//   phase B the fragments of all units are loaded once, the compute warps
+//           take (unit, group) tasks of the CTA's 16-row output items, and
+//           one warp per item rounds each unit's rows to bf16, weights them
+//           by the router scores and sums the units in order (+ shared).
+// Every reduction runs in a fixed order, so results do not depend on timing.
+
+constexpr int kFusedSmemMax = 220 * 1024;
+constexpr int kFW = 16;                   // compute warps
+constexpr int kFThreads = 32 * (kFW + 1);
+constexpr int kFMaxA = 8;                 // gate/up tiles per CTA
+constexpr int kFMaxB = 64;                // down tiles per CTA
+constexpr int kFMaxUnits = 64;
+
+struct FusedArgs {
+  GemvArgs a;
+  DownArgs d;
+  int* bar;     // [0] arrivals, [1] epoch
+  int off_frag, off_part, off_xsum, off_reda, off_stage_a;
+  int off_bfrag, off_bpart, off_bxsum, off_redb, off_stage_b, off_meta;
+  int stage_a, stage_b;  // bytes per A / B tile slot
+  int b_late;            // down tiles share the gate/up slots: request them
+                         // once phase A is done (they load during the barrier)
+};
+
+SLX_DEV int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+SLX_DEV void st_release_gpu(int* p, int v) {
+  asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// All CTAs of a cooperative grid; call from one thread after a CTA barrier.
+SLX_DEV bool grid_barrier(int* bar, int nblocks, int32_t* status) {
+  const int epoch = ld_acquire_gpu(&bar[1]);
+  if (ticket_acq_rel(&bar[0]) == nblocks - 1) {
+    bar[0] = 0;
+    st_release_gpu(&bar[1], epoch + 1);
+    return true;
+  }
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0; ld_acquire_gpu(&bar[1]) == epoch; ++i) {
+    if ((i & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+      set_status(status, SLX_ERR_DEVICE_TIMEOUT);
+      return false;
+    }
+    __nanosleep(20);
+  }
+  return true;
+}
+
+// One 64-column group of a 16-row down tile: per-row partial (lanes with
+// tig < 2 hold rows g and g + 8).
+template <int BITS>
+SLX_DEV float down_group(const uint8_t* S, int in, int G, int g, int tig,
+                         int rrow, const uint32_t* fr, const float* xs) {
+  const int RB = tile_rb(in, BITS);
+  const bool swz = tile_swizzled(in, BITS);
+  const int nG = tile_ng(in);
+  const uint32_t* SB = reinterpret_cast<const uint32_t*>(S + 16 * RB);
+  uint32_t b[8];
+  load_frag(fr, G, tig, b);
+  float dd[4];
+  group_mma<BITS>(S, RB, swz, G, g, tig, b, dd);
+  (void)nG;
+  return fold(0.f, (tig & 1) ? dd[2] : dd[0], SB[G * 16 + rrow], xs[G]);
+}
+
+template <int BITS>
+__global__ void __launch_bounds__(kFThreads, 1)
+    k_switchglu_fused(const __grid_constant__ FusedArgs f) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const GemvArgs& a = f.a;
+  const DownArgs& d = f.d;
+  uint64_t* fullA = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* fullB = fullA + kFMaxA;
+  uint32_t* frag = reinterpret_cast<uint32_t*>(smem + f.off_frag);
+  float* part = reinterpret_cast<float*>(smem + f.off_part);
+  float* xsum = reinterpret_cast<float*>(smem + f.off_xsum);
+  float* redA = reinterpret_cast<float*>(smem + f.off_reda);  // [kFMaxA][kFW][32]
+  uint8_t* stA = smem + f.off_stage_a;
+  uint32_t* bfrag = reinterpret_cast<uint32_t*>(smem + f.off_bfrag);
+  float* bpart = reinterpret_cast<float*>(smem + f.off_bpart);
+  float* bxsum = reinterpret_cast<float*>(smem + f.off_bxsum);
+  float* redB = reinterpret_cast<float*>(smem + f.off_redb);  // [tiles][nGmax][16]
+  uint8_t* stB = smem + f.off_stage_b;
+  int* meta = reinterpret_cast<int*>(smem + f.off_meta);      // A tile valid + B unit valid
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G_ = gridDim.x, bid = blockIdx.x;
+  const int nG = tile_ng(a.in);
+  const int RB = tile_rb(a.in, BITS);
+  const bool swz = tile_swizzled(a.in, BITS);
+  const int qa0 = (int)((long long)a.n_tiles * bid / G_);
+  const int na = (int)((long long)a.n_tiles * (bid + 1) / G_) - qa0;
+  const int U = d.n_units;
+  const int qb0 = (int)((long long)d.n_items * bid / G_);
+  const int nb = (int)((long long)d.n_items * (bid + 1) / G_) - qb0;
+  const int nbt = nb * U;  // down tiles of this CTA
+  const int nGr = tile_ng(d.I), nGs = d.Is ? tile_ng(d.Is) : 0;
+  const int nGmax = nGr > nGs ? nGr : nGs;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kFMaxA; ++i) mbar_init(&fullA[i], 1);
+    for (int i = 0; i < kFMaxB; ++i) mbar_init(&fullB[i], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_wait_primary();
+
+  if (warp == 0) {
+    // ---- every weight request of this CTA, up front ----
+    const uint64_t pol = l2_evict_first_policy();
+    if (lane < na) {
+      SlotCache c;
+      const TileInfo t = gemv_tile(a, qa0 + lane, c);
+      meta[lane] = t.valid;
+      if (!t.valid) set_status(a.status, SLX_ERR_UNMAPPED_EXPERT);
+      gemv_issue<BITS>(a, t, stA + (size_t)lane * f.stage_a, &fullA[lane], pol);
+    }
+  }
+  auto issue_b = [&]() {
+    const uint64_t pol = l2_evict_first_policy();
+    for (int s = lane; s < nbt; s += 32) {
+      const int q = qb0 + s / U, j = s % U;
+      const int rb = q;  // one token: item = 16-row block of H
+      const bool shared = j >= d.k;
+      const int bytes = shared ? d.tile_bytes_sh : d.tile_bytes;
+      const uint8_t* src;
+      bool valid = true;
+      if (!shared) {
+        const int slot = lookup_slot(d.ids, j, d.slot_table, d.n_table, d.n_slots);
+        valid = slot >= 0;
+        src = d.bank + (size_t)(valid ? slot : 0) * d.slot_stride + d.a_bytes +
+              (size_t)rb * d.tile_bytes;
+      } else {
+        src = d.shared + d.a_bytes_sh + (size_t)rb * d.tile_bytes_sh;
+      }
+      if (s < U) meta[kFMaxA + j] = valid;
+      if (!valid) set_status(d.status, SLX_ERR_UNMAPPED_EXPERT);
+      if (valid) {
+        mbar_arrive_expect_tx(&fullB[s], bytes);
+        bulk_g2s(stB + (size_t)s * f.stage_b, src, bytes, &fullB[s], pol);
+      } else {
+        mbar_arrive(&fullB[s]);
+      }
+    }
+  };
+  if (warp == 0) {
+    if (!f.b_late) issue_b();
+  } else {
+    // ---- activation fragments of the token ----
+    const int ct = threadIdx.x - 32;
+    for (int p = ct; p < 4 * nG; p += kFW * 32)
+      frag_task<BITS>(a.x, p >> 2, p & 3, frag, part);
+  }
+  __syncthreads();
+  if (warp > 0) frag_sums(part, xsum, nG, threadIdx.x - 32, kFW * 32);
+  __syncthreads();
+
+  // ---- phase A: gate/up groups ----
+  if (warp > 0) {
+    const int cw = warp - 1;
+    const int g = lane >> 2, tig = lane & 3;
+    const int mat = tig >> 1;
+    const int sbl = mat * 16 + g + 8 * (tig & 1);
+    for (int i = 0; i < na; ++i) {
+      const bool ok = mbar_wait(&fullA[i], 0, a.status);
+      const uint8_t* S = stA + (size_t)i * f.stage_a;
+      float acc = 0.f;
+      if (ok && meta[i]) {
+        const uint8_t* P = S;
+        const uint8_t* Q = S + 16 * RB;
+        const uint32_t* SB = reinterpret_cast<const uint32_t*>(S + 32 * RB);
+        for (int G = cw; G < nG; G += 2 * kFW) {
+          const int G2 = G + kFW;
+          const bool two = G2 < nG;
+          uint32_t b[8], b2[8];
+          load_frag(frag, G, tig, b);
+          if (two) load_frag(frag, G2, tig, b2);
+          float d0[4], d1[4];
+          float e0[4] = {0.f, 0.f, 0.f, 0.f}, e1[4] = {0.f, 0.f, 0.f, 0.f};
+          group_mma<BITS>(P, RB, swz, G, g, tig, b, d0);
+          group_mma<BITS>(Q, RB, swz, G, g, tig, b, d1);
+          if (two) {
+            group_mma<BITS>(P, RB, swz, G2, g, tig, b2, e0);
+            group_mma<BITS>(Q, RB, swz, G2, g, tig, b2, e1);
+          }
+          const float v = mat == 0 ? ((tig & 1) ? d0[2] : d0[0])
+                                   : ((tig & 1) ? d1[2] : d1[0]);
+          acc = fold(acc, v, SB[G * 32 + sbl], xsum[G]);
+          if (two) {
+            const float v2 = mat == 0 ? ((tig & 1) ? e0[2] : e0[0])
+                                      : ((tig & 1) ? e1[2] : e1[0]);
+            acc = fold(acc, v2, SB[G2 * 32 + sbl], xsum[G2]);
+          }
+        }
+      }
+      redA[((size_t)i * kFW + cw) * 32 + lane] = acc;
+    }
+  }
+  __syncthreads();
+  // one warp per tile: reduce the 16 partials, SwiGLU, write fragments
+  if (warp > 0 && warp - 1 < na) {
+    const int i = warp - 1;
+    SlotCache c;
+    TileInfo t = gemv_tile(a, qa0 + i, c);
+    t.valid = t.valid1 = meta[i];
+    gemv_epilogue<BITS, kFW>(a, t, redA + (size_t)i * kFW * 32, lane);
+  }
+  if (warp == 0 && f.b_late) issue_b();  // the A slots are free now
+  __syncthreads();
+  if (threadIdx.x == 0) grid_barrier(f.bar, G_, a.status);
+  __syncthreads();
+  pdl_launch_dependents();
+  if (nb == 0) return;
+
+  // ---- phase B: fragments of every unit, then (unit, group) tasks ----
+  {
+    const int ct = threadIdx.x;
+    const int pu = nGmax * 8;  // uint4 per unit
+    for (int p = ct; p < U * pu; p += kFThreads) {
+      const int j = p / pu, o = p % pu;
+      const bool shared = j >= d.k;
+      if (o < (shared ? nGs : nGr) * 8) {
+        const uint32_t* src = shared ? d.hfrag_sh
+                                     : d.hfrag + (size_t)j * d.unit_frag_words;
+        reinterpret_cast<uint4*>(bfrag)[p] =
+            __ldcg(reinterpret_cast<const uint4*>(src) + o);
+      }
+    }
+    for (int p = ct; p < U * nGmax; p += kFThreads) {
+      const int j = p / nGmax, G = p % nGmax;
+      const bool shared = j >= d.k;
+      if (G < (shared ? nGs : nGr)) {
+        const float* src = shared ? d.hpart_sh
+                                  : d.hpart + (size_t)j * d.unit_part_floats;
+        reinterpret_cast<float4*>(bpart)[p] =
+            __ldcg(reinterpret_cast<const float4*>(src) + G);
+      }
+    }
+  }
+  __syncthreads();
+  frag_sums(bpart, bxsum, U * nGmax, threadIdx.x, kFThreads);
+  __syncthreads();
+  if (warp > 0) {
+    const int cw = warp - 1;
+    const int g = lane >> 2, tig = lane & 3;
+    const int rrow = g + 8 * (tig & 1);
+    const int ntask = nbt * nGmax;
+    for (int task = cw; task < ntask; task += kFW) {
+      const int s = task / nGmax, G = task % nGmax;
+      const int j = s % U;
+      const int in = j >= d.k ? d.Is : d.I;
+      float v = 0.f;
+      if (G < tile_ng(in)) {
+        const bool ok = mbar_wait(&fullB[s], 0, d.status);
+        if (ok && meta[kFMaxA + j])
+          v = down_group<BITS>(stB + (size_t)s * f.stage_b, in, G, g, tig,
+                               rrow, bfrag + (size_t)j * nGmax * 32,
+                               bxsum + (size_t)j * nGmax);
+      }
+      if (tig < 2) redB[((size_t)s * nGmax + G) * kRows + rrow] = v;
+    }
+  }
+  __syncthreads();
+  // one warp per item: bf16 per unit, score weights, combine in unit order
+  if (warp < nb) {
+    const int it = warp;
+    const int q = qb0 + it;
+    const int row0 = q * kRows;
+    float y_out = 0.f;  // lane < 16: row lane
+    for (int j = 0; j < U; ++j) {
+      const int s = it * U + j;
+      const int in = j >= d.k ? d.Is : d.I;
+      const int ng = tile_ng(in);
+      float v = 0.f;
+      if (lane < kRows)
+        for (int G = 0; G < ng; ++G) v += redB[((size_t)s * nGmax + G) * kRows + lane];
+      const float y = meta[kFMaxA + j] ? round_bf16(v) : 0.f;
+      if (!d.scores) {
+        if (lane < kRows)
+          d.out[(size_t)j * d.H + row0 + lane] = f32_to_bf16(y);
+      } else {
+        y_out += (j < d.k) ? d.scores[j] * y : y;
+      }
+    }
+    if (d.scores && lane < kRows) d.out[row0 + lane] = f32_to_bf16(y_out);
+  }
+}
+
+// Shared-memory layout of the fused kernel for one problem, or 0 if it
+// does not fit one CTA per SM.
+template <int BITS>
+static int fused_layout(FusedArgs& f, int grid) {
+  const GemvArgs& a = f.a;
+  const DownArgs& d = f.d;
+  const int nG = tile_ng(a.in);
+  const int na_max = (a.n_tiles + grid - 1) / grid;
+  const int nb_max = (d.n_items + grid - 1) / grid;
+  const int U = d.n_units;
+  if (na_max > kFMaxA || nb_max * U > kFMaxB || U > kFMaxUnits) return 0;
+  const int nGr = tile_ng(d.I), nGs = d.Is ? tile_ng(d.Is) : 0;
+  const int nGmax = nGr > nGs ? nGr : nGs;
+  auto al = [](int v) { return (v + 127) & ~127; };
+  int o = (kFMaxA + kFMaxB) * 8;
+  o = al(o); f.off_frag = o;    o += nG * 32 * 4;
+  o = al(o); f.off_part = o;    o += nG * 4 * 4;
+  o = al(o); f.off_xsum = o;    o += nG * 4;
+  o = al(o); f.off_reda = o;    o += kFMaxA * kFW * 32 * 4;
+  o = al(o); f.off_meta = o;    o += (kFMaxA + kFMaxUnits) * 4;
+  o = al(o); f.off_bfrag = o;   o += U * nGmax * 32 * 4;
+  o = al(o); f.off_bpart = o;   o += U * nGmax * 4 * 4;
+  o = al(o); f.off_bxsum = o;   o += U * nGmax * 4;
+  o = al(o); f.off_redb = o;    o += nb_max * U * nGmax * kRows * 4;
+  f.stage_a = al((int)pair_tile_bytes(a.in, BITS));
+  const int tb = d.tile_bytes > d.tile_bytes_sh ? d.tile_bytes : d.tile_bytes_sh;
+  f.stage_b = al(tb);
+  o = al(o); f.off_stage_a = o;
+  const int bytes_a = na_max * f.stage_a, bytes_b = nb_max * U * f.stage_b;
+  if (o + bytes_a + bytes_b <= kFusedSmemMax) {
+    f.b_late = 0;
+    f.off_stage_b = o + bytes_a;
+    return o + bytes_a + bytes_b;
+  }
+  f.b_late = 1;
+  f.off_stage_b = o;
+  return o + (bytes_a > bytes_b ? bytes_a : bytes_b);
+}
+
+template <int BITS>
+static int launch_fused_t(FusedArgs f, cudaStream_t stream) {
+  static int max_grid = -1;
+  if (max_grid < 0) {
+    int per_sm = 0;
+    if (cudaFuncSetAttribute(k_switchglu_fused<BITS>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kFusedSmemMax) != cudaSuccess)
+      return SLX_ERR_CUDA;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+            &per_sm, k_switchglu_fused<BITS>, kFThreads, kFusedSmemMax) !=
+        cudaSuccess)
+      return SLX_ERR_CUDA;
+    max_grid = per_sm >= 1 ? num_sms() : 0;
+  }
+  if (max_grid <= 0) return SLX_ERR_UNSUPPORTED;
+  const int grid = max_grid;
+  const int bytes = fused_layout<BITS>(f, grid);
+  if (bytes <= 0 || bytes > kFusedSmemMax) return SLX_ERR_UNSUPPORTED;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kFThreads);
+  cfg.dynamicSmemBytes = bytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_switchglu_fused<BITS>, f) == cudaSuccess
+             ? SLX_OK : SLX_ERR_CUDA;
+}
+
+int launch_switchglu_fused(const GemvArgs& a, const DownArgs& d, int* bar,
+                           int bits, cudaStream_t stream) {
+  if (a.T != 1 || d.T != 1) return SLX_ERR_UNSUPPORTED;
+  FusedArgs f = {};
+  f.a = a;
+  f.d = d;
+  f.bar = bar;
+  switch (bits) {
+    case 2: f.a.tile_bytes = (int)pair_tile_bytes(a.in, 2); break;
+    case 4: f.a.tile_bytes = (int)pair_tile_bytes(a.in, 4); break;
+    case 8: f.a.tile_bytes = (int)pair_tile_bytes(a.in, 8); break;
+    default: return SLX_ERR_UNSUPPORTED;
+  }
+  switch (bits) {
+    case 2: return launch_fused_t<2>(f, stream);
+    case 4: return launch_fused_t<4>(f, stream);
+    default: return launch_fused_t<8>(f, stream);
+  }
 }
 
 // Phase A and phase B each request exactly kSmemTarget bytes: one CTA of

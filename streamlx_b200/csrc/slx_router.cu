@@ -34,6 +34,10 @@
 
 #include "slx_kernels.cuh"
 
+#ifdef SLX_TRACE
+static __device__ unsigned long long g_slx_trace[3][160][16];
+#endif
+
 namespace slx {
 
 constexpr int kRouterCluster = 8;  // CTAs per (head, token)

@@ -157,7 +157,7 @@ class SynthDecoder:
         self.use_graphs = cfg.has_trunk
         self.pipeline = True
         self.pdl = True             # captured kernels chain with PDL
-        self.glu_events = True      # time every SwitchGLU pair in the graphs
+        self.glu_events = True      # time sampled SwitchGLU pairs in graphs
         self._graphs = None
         self._pending = None
         self._pf_done = 0
@@ -272,6 +272,11 @@ class SynthDecoder:
         nxt = torch.empty(1, dtype=torch.int32, device=self.device)
         L.argmax(self.logits, nxt)
         self.n_pos += 1
+        ops.check_status(self.device)   # the kernels' device-side errors
+        if int(self.status.item()) != 0:
+            code = int(self.status.item())
+            self.status.zero_()
+            raise L.SlxError("device", code, "decode step device error")
         return nxt
 
     # ----------------------------------------------------- graph decode --
@@ -392,7 +397,8 @@ class SynthDecoder:
         pool = w.pool
         sh = w.shared
         ev = self.g_ev[i]
-        if self.glu_events:
+        timed = self._glu_timed(i)
+        if timed:
             L.event_record_external(ev[0])
         ops.switchglu(pool.store.bank, xm, self.g_ids[i], k,
                       scores=self.g_scores[i], table=pool.store.table_dev,
@@ -400,7 +406,7 @@ class SynthDecoder:
                       inter=pool.inter, shared_inter=sh[2] if sh else 0,
                       scratch_buf=self.g_glu_scratch,
                       status=self.g_lstatus[i:i + 1])
-        if self.glu_events:
+        if timed:
             L.event_record_external(ev[1])
         if join:
             self._join_side()
@@ -458,31 +464,39 @@ class SynthDecoder:
         self.g_lstatus.zero_()
 
     def _capture_graphs(self, s, mode):
+        """Capture the graphs; the library kernels each one launches are
+        counted while it is recorded (launch accounting of replays)."""
         n = self.cfg.layers
         graphs = []
+        self._kernels_layer = []
         for i in range(n):
             g = torch.cuda.CUDAGraph()
+            c0 = L.LAUNCHES[0]
             with torch.cuda.graph(g, stream=s, capture_error_mode=mode):
                 self._record_layer(i)
+            self._kernels_layer.append(L.LAUNCHES[0] - c0)
             graphs.append(g)
         tail = torch.cuda.CUDAGraph()
+        c0 = L.LAUNCHES[0]
         with torch.cuda.graph(tail, stream=s, capture_error_mode=mode):
             self._record_tail()
+        self._kernels_tail = L.LAUNCHES[0] - c0
         full = torch.cuda.CUDAGraph()
+        c0 = L.LAUNCHES[0]
         with torch.cuda.graph(full, stream=s, capture_error_mode=mode):
             self.g_lstatus.zero_()
             for i in range(n):
                 self._record_layer(i, join=False)
             self._join_side()
             self._record_tail()
+        self._kernels_full = L.LAUNCHES[0] - c0
         return graphs, tail, full
 
     def _graph_kernels(self, start: int) -> int:
         """Library kernels one launch from layer `start` runs."""
-        per = 0
-        for i in range(start, self.cfg.layers):
-            per += 9 + (1 if self.layers[i].mlp.pf_link is not None else 0)
-        return per + (1 if start == 0 else 0) + 3
+        if start == 0:
+            return self._kernels_full
+        return sum(self._kernels_layer[start:]) + self._kernels_tail
 
     def _launch(self, start: int) -> None:
         graphs, tail, full = self._graphs
@@ -504,10 +518,18 @@ class SynthDecoder:
             raise L.SlxError("device", st, "decode step device error")
         return log
 
+    def _glu_timed(self, i: int) -> bool:
+        """Layers whose SwitchGLU pair is bracketed by timing events: one in
+        eight (an event node costs a few microseconds of the step)."""
+        return self.glu_events and i % 8 == 3
+
     def _glu_timing(self, start: int) -> None:
         if self.glu_times is None or not self.glu_events:
             return
-        ev = self.g_ev[start:]
+        ev = [self.g_ev[i] for i in range(start, self.cfg.layers)
+              if self._glu_timed(i)]
+        if not ev:
+            return
         self.glu_times.extend(
             L.event_elapsed_many([e[0] for e in ev], [e[1] for e in ev])
             .tolist())

@@ -27,7 +27,8 @@ def scratch(nbytes: int, device, tag: str = "glu") -> torch.Tensor:
     key = (tag, device)
     t = _scratch.get(key)
     if t is None or t.numel() < nbytes:
-        t = torch.empty(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
+        # zeroed: the switchglu scratch ends with grid-barrier words
+        t = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
         _scratch[key] = t
     return t
 

@@ -32,6 +32,16 @@ import numpy as np
 
 from .stindex import PARTS, PROJS, SafetensorsIndex, TensorLoc
 
+def _native():
+    """The library's batched pread, or None when it is not built."""
+    try:
+        from . import _lib
+        _lib.lib()
+        return _lib
+    except (ImportError, OSError):
+        return None
+
+
 _NP_VIEW = {"U32": np.uint32, "BF16": np.uint16, "F16": np.float16,
             "F32": np.float32, "U16": np.uint16, "U8": np.uint8}
 
@@ -103,6 +113,7 @@ class ExpertReader:
                  merge_gap: int = 64 * 1024, max_span: int = 16 * 1024 * 1024,
                  arena_bytes: int = 512 << 20, pinned: bool | None = None):
         self.index = index
+        self.workers = workers
         self.merge_gap = merge_gap
         self.max_span = max_span
         self._fds: dict[str, int] = {}
@@ -165,26 +176,10 @@ class ExpertReader:
         buf = self.arena.buf
         offs = [base + r for r in rel]
 
-        def read_span(i):
-            path, off, n, _ = spans[i]
-            view = memoryview(buf[offs[i]:offs[i] + n])
-            got = os.preadv(self._fd(path), [view], off)
-            if got != n:
-                raise IOError(f"short read {got}/{n} at {off} of {path}")
-            return i
-
         out: dict = {}
-        futs = [self._ex.submit(read_span, i) for i in range(len(spans))]
         try:
-            done = [f.result() for f in futs]
+            done = self._read_spans(spans, offs, buf)
         except BaseException:
-            for f in futs:
-                f.cancel()
-            for f in futs:
-                try:
-                    f.result()
-                except BaseException:   # noqa: BLE001 - first error re-raised
-                    pass
             if total:
                 self.arena.release(base, total)
             raise
@@ -200,6 +195,48 @@ class ExpertReader:
                     self.useful_bytes += m
         out["__arena__"] = (base, total)
         return out
+
+    def _read_spans(self, spans, offs, buf) -> range:
+        """pread every span into the arena: one native call over a pool of
+        threads when the library is built, else one os.preadv per span on
+        the Python pool (host IO either way)."""
+        n_sp = len(spans)
+        if n_sp == 0:
+            return range(0)
+        L = _native()
+        if L is not None:
+            fds = np.array([self._fd(sp[0]) for sp in spans], dtype=np.int32)
+            off = np.array([sp[1] for sp in spans], dtype=np.int64)
+            size = np.array([sp[2] for sp in spans], dtype=np.int64)
+            dst = np.array([buf.ctypes.data + o for o in offs],
+                           dtype=np.uint64)
+            rc, bad, err = L.pread_many(fds, off, size, dst, self.workers)
+            if rc != 0:
+                path, o, n, _ = spans[bad] if bad >= 0 else spans[0]
+                raise IOError(f"short read at {o} (+{n}) of {path}"
+                              + (f": {os.strerror(err)}" if err else ""))
+            return range(n_sp)
+
+        def read_span(i):
+            path, off, n, _ = spans[i]
+            view = memoryview(buf[offs[i]:offs[i] + n])
+            got = os.preadv(self._fd(path), [view], off)
+            if got != n:
+                raise IOError(f"short read {got}/{n} at {off} of {path}")
+            return i
+
+        futs = [self._ex.submit(read_span, i) for i in range(n_sp)]
+        try:
+            return [f.result() for f in futs]
+        except BaseException:
+            for f in futs:
+                f.cancel()
+            for f in futs:
+                try:
+                    f.result()
+                except BaseException:   # noqa: BLE001 - first error re-raised
+                    pass
+            raise
 
     def release_raw(self, raw: dict, event=None) -> None:
         """Return a read's staging region to the arena (after `event`)."""

@@ -116,7 +116,7 @@ def _run_switchglu(dev, E, H, I, bits, k, T, n_slots, combined, seed,
     tab = torch.from_numpy(table).to(dev)
     out = torch.empty((T, H) if combined else (T, k, H), dtype=torch.bfloat16,
                       device=dev)
-    scratch = torch.empty(L.switchglu_scratch_bytes(T, k, I, shared_I),
+    scratch = torch.zeros(L.switchglu_scratch_bytes(T, k, I, shared_I),
                           dtype=torch.uint8, device=dev)
     st = _status(dev)
     L.switchglu(bank, xt, idt, out, scratch, st,
@@ -148,14 +148,36 @@ def _run_switchglu(dev, E, H, I, bits, k, T, n_slots, combined, seed,
     (16, 512, 256, 8, 2, 3, 6, True, 0),        # 8-bit, 3 tokens
     (32, 1024, 512, 4, 4, 5, 12, True, 256),    # 5 tokens + shared
 ])
-def test_switchglu_parity(dev, case):
+@pytest.mark.parametrize("fused", [True, False])
+def test_switchglu_parity(dev, case, fused):
+    """Decode calls (T == 1) run as one cooperative launch by default; the
+    two-launch path serves every T."""
     E, H, I, bits, k, T, ns, comb, shI = case
-    got, want = _run_switchglu(dev, E, H, I, bits, k, T, ns, comb, seed=7,
-                               shared_I=shI)
-    check_close(got, want)
+    if fused and T != 1:
+        pytest.skip("the single-launch path serves decode calls only")
+    prev = L.set_switchglu_fused(fused)
+    try:
+        for seed in (7, 8):     # twice: the grid barrier words are reused
+            got, want = _run_switchglu(dev, E, H, I, bits, k, T, ns, comb,
+                                       seed=seed, shared_I=shI)
+            check_close(got, want)
+            if T == 1:
+                assert L.lib().slx_switchglu_last_kernels() == \
+                    (1 if fused else 2)
+    finally:
+        L.set_switchglu_fused(prev)
 
 
-def test_switchglu_unmapped_expert_sets_status(dev):
+@pytest.mark.parametrize("fused", [True, False])
+def test_switchglu_unmapped_expert_sets_status(dev, fused):
+    prev = L.set_switchglu_fused(fused)
+    try:
+        _unmapped_case(dev)
+    finally:
+        L.set_switchglu_fused(prev)
+
+
+def _unmapped_case(dev):
     E, H, I, bits, k, ns = 16, 512, 256, 4, 2, 4
     tt, _, _ = make_bank(E, H, I, bits, 3, device="cpu")
     pool, stride = pack_pool(tt, list(range(ns)), H, I, bits)
@@ -165,7 +187,7 @@ def test_switchglu_unmapped_expert_sets_status(dev):
     ids = torch.tensor([[1, 9]], dtype=torch.int32, device=dev)  # 9 unmapped
     x = torch.randn(1, H, device=dev).to(torch.bfloat16)
     out = torch.empty(1, k, H, dtype=torch.bfloat16, device=dev)
-    scratch = torch.empty(L.switchglu_scratch_bytes(1, k, I), dtype=torch.uint8,
+    scratch = torch.zeros(L.switchglu_scratch_bytes(1, k, I), dtype=torch.uint8,
                           device=dev)
     st = _status(dev)
     L.switchglu(bank, x, ids, out, scratch, st, slot_table=table)
