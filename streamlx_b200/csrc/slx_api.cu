@@ -172,7 +172,7 @@ int slx_switchglu(const slx_expert_bank* bank, const slx_shared_expert* shared,
     return fail(SLX_ERR_SCRATCH, "scratch %zu < %zu bytes", scratch_bytes, need);
   const size_t nu = (size_t)T * k, ng = I / 64, ngs = Is / 64;
   uint8_t* sp = reinterpret_cast<uint8_t*>(scratch);
-  int* gbar = reinterpret_cast<int*>(sp);
+  void* gbar = sp;  // 64-bit arrival counter of the fused kernel's barrier
   sp += 256;
   uint32_t* hfrag = reinterpret_cast<uint32_t*>(sp);
   sp += align256(nu * ng * 128);

@@ -82,7 +82,7 @@ struct RouterArgs {
 
 int launch_gemv(GemvArgs a, int bits, cudaStream_t stream, bool pdl_secondary);
 int launch_down(DownArgs a, int bits, cudaStream_t stream);
-int launch_switchglu_fused(const GemvArgs& a, const DownArgs& d, int* bar,
+int launch_switchglu_fused(const GemvArgs& a, const DownArgs& d, void* bar,
                            int bits, cudaStream_t stream);
 int launch_dequant_rows(const uint32_t* w, const uint16_t* s, const uint16_t* b,
                         int in, int bits, int gs, const int32_t* rows,

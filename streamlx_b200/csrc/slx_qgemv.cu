@@ -683,7 +683,7 @@ constexpr int kFMaxUnits = 64;
 struct FusedArgs {
   GemvArgs a;
   DownArgs d;
-  int* bar;     // [0] arrivals, [1] epoch
+  unsigned long long* bar;  // arrival counter (only grows)
   int off_frag, off_part, off_xsum, off_reda, off_stage_a;
   int off_bfrag, off_bpart, off_bxsum, off_redb, off_stage_b, off_meta;
   int stage_a, stage_b;  // bytes per A / B tile slot
@@ -691,30 +691,32 @@ struct FusedArgs {
                          // once phase A is done (they load during the barrier)
 };
 
-SLX_DEV int ld_acquire_gpu(const int* p) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+SLX_DEV unsigned long long ld_acquire_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
-SLX_DEV void st_release_gpu(int* p, int v) {
-  asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+SLX_DEV void red_release_add_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
 // All CTAs of a cooperative grid; call from one thread after a CTA barrier.
-SLX_DEV bool grid_barrier(int* bar, int nblocks, int32_t* status) {
-  const int epoch = ld_acquire_gpu(&bar[1]);
-  if (ticket_acq_rel(&bar[0]) == nblocks - 1) {
-    bar[0] = 0;
-    st_release_gpu(&bar[1], epoch + 1);
-    return true;
-  }
+// The counter only grows: a launch's CTAs all read a value inside
+// [n * nblocks, (n + 1) * nblocks) on entry (the earlier launches are
+// complete), add one each with a release reduction (no reply to wait for,
+// unlike a returning atomic), and wait until it reaches (n + 1) * nblocks.
+SLX_DEV bool grid_barrier(unsigned long long* cnt, int nblocks,
+                          int32_t* status) {
+  const unsigned long long nb = (unsigned long long)nblocks;
+  const unsigned long long v = ld_acquire_u64(cnt);
+  const unsigned long long target = v - v % nb + nb;
+  red_release_add_u64(cnt, 1ull);
   const uint64_t t0 = globaltimer_ns();
-  for (uint32_t i = 0; ld_acquire_gpu(&bar[1]) == epoch; ++i) {
+  for (uint32_t i = 0; ld_acquire_u64(cnt) < target; ++i) {
     if ((i & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
       set_status(status, SLX_ERR_DEVICE_TIMEOUT);
       return false;
     }
-    __nanosleep(20);
   }
   return true;
 }
@@ -776,6 +778,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
   }
   __syncthreads();
   pdl_wait_primary();
+  SLX_TRACE_POINT(0, 0);
 
   if (warp == 0) {
     // ---- every weight request of this CTA, up front ----
@@ -826,6 +829,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
   __syncthreads();
   if (warp > 0) frag_sums(part, xsum, nG, threadIdx.x - 32, kFW * 32);
   __syncthreads();
+  SLX_TRACE_POINT(0, 1);
 
   // ---- phase A: gate/up groups ----
   if (warp > 0) {
@@ -835,6 +839,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
     const int sbl = mat * 16 + g + 8 * (tig & 1);
     for (int i = 0; i < na; ++i) {
       const bool ok = mbar_wait(&fullA[i], 0, a.status);
+      if (i < 3) SLX_TRACE_POINT(0, 2 + i);
       const uint8_t* S = stA + (size_t)i * f.stage_a;
       float acc = 0.f;
       if (ok && meta[i]) {
@@ -869,6 +874,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
     }
   }
   __syncthreads();
+  SLX_TRACE_POINT(0, 5);
   // one warp per tile: reduce the 16 partials, SwiGLU, write fragments
   if (warp > 0 && warp - 1 < na) {
     const int i = warp - 1;
@@ -879,8 +885,10 @@ __global__ void __launch_bounds__(kFThreads, 1)
   }
   if (warp == 0 && f.b_late) issue_b();  // the A slots are free now
   __syncthreads();
+  SLX_TRACE_POINT(0, 6);
   if (threadIdx.x == 0) grid_barrier(f.bar, G_, a.status);
   __syncthreads();
+  SLX_TRACE_POINT(0, 7);
   pdl_launch_dependents();
   if (nb == 0) return;
 
@@ -912,27 +920,30 @@ __global__ void __launch_bounds__(kFThreads, 1)
   __syncthreads();
   frag_sums(bpart, bxsum, U * nGmax, threadIdx.x, kFThreads);
   __syncthreads();
+  SLX_TRACE_POINT(0, 8);
   if (warp > 0) {
     const int cw = warp - 1;
     const int g = lane >> 2, tig = lane & 3;
     const int rrow = g + 8 * (tig & 1);
     const int ntask = nbt * nGmax;
+    // the down tiles were requested at the start: wait for them once
+    bool ok = true;
+    for (int s = 0; s < nbt; ++s) ok &= mbar_wait(&fullB[s], 0, d.status);
+    SLX_TRACE_POINT(0, 11);
     for (int task = cw; task < ntask; task += kFW) {
       const int s = task / nGmax, G = task % nGmax;
       const int j = s % U;
       const int in = j >= d.k ? d.Is : d.I;
       float v = 0.f;
-      if (G < tile_ng(in)) {
-        const bool ok = mbar_wait(&fullB[s], 0, d.status);
-        if (ok && meta[kFMaxA + j])
-          v = down_group<BITS>(stB + (size_t)s * f.stage_b, in, G, g, tig,
-                               rrow, bfrag + (size_t)j * nGmax * 32,
-                               bxsum + (size_t)j * nGmax);
-      }
+      if (G < tile_ng(in) && ok && meta[kFMaxA + j])
+        v = down_group<BITS>(stB + (size_t)s * f.stage_b, in, G, g, tig,
+                             rrow, bfrag + (size_t)j * nGmax * 32,
+                             bxsum + (size_t)j * nGmax);
       if (tig < 2) redB[((size_t)s * nGmax + G) * kRows + rrow] = v;
     }
   }
   __syncthreads();
+  SLX_TRACE_POINT(0, 9);
   // one warp per item: bf16 per unit, score weights, combine in unit order
   if (warp < nb) {
     const int it = warp;
@@ -956,6 +967,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
     }
     if (d.scores && lane < kRows) d.out[row0 + lane] = f32_to_bf16(y_out);
   }
+  SLX_TRACE_POINT(0, 10);
 }
 
 // Shared-memory layout of the fused kernel for one problem, or 0 if it
@@ -1030,13 +1042,13 @@ static int launch_fused_t(FusedArgs f, cudaStream_t stream) {
              ? SLX_OK : SLX_ERR_CUDA;
 }
 
-int launch_switchglu_fused(const GemvArgs& a, const DownArgs& d, int* bar,
+int launch_switchglu_fused(const GemvArgs& a, const DownArgs& d, void* bar,
                            int bits, cudaStream_t stream) {
   if (a.T != 1 || d.T != 1) return SLX_ERR_UNSUPPORTED;
   FusedArgs f = {};
   f.a = a;
   f.d = d;
-  f.bar = bar;
+  f.bar = reinterpret_cast<unsigned long long*>(bar);
   switch (bits) {
     case 2: f.a.tile_bytes = (int)pair_tile_bytes(a.in, 2); break;
     case 4: f.a.tile_bytes = (int)pair_tile_bytes(a.in, 4); break;

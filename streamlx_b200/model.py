@@ -575,9 +575,14 @@ class SynthDecoder:
         return None
 
     def flush(self) -> None:
-        """Finish the deferred bookkeeping of the last step, if any."""
+        """Finish the deferred bookkeeping of the last step, if any: start
+        its next-layer prefetches, then replay its pool calls."""
         pend, self._pending = self._pending, None
-        if pend is not None and self._replay(pend, 0) is not None:
+        if pend is None:
+            return
+        self._pf_done = 0
+        self._prefetch_upto(pend)
+        if self._replay(pend, 0) is not None:
             raise RuntimeError("deferred step had an unmapped expert")
 
     def _step_graph(self, token: torch.Tensor) -> torch.Tensor:
@@ -605,12 +610,14 @@ class SynthDecoder:
         self.flush()
         log = self._read_log()
         self._glu_timing(0)
-        self._pf_done = 0
-        self._prefetch_upto(log)
         lst = log[self._lst_off:self._lst_off + n]
         if self.pipeline and not (lst == self._UNMAPPED).any():
+            # bookkeeping (and the prefetch reads it starts) waits for the
+            # next call, where it overlaps that step's device work
             self._pending = log
         else:
+            self._pf_done = 0
+            self._prefetch_upto(log)
             start = 0
             while True:
                 redo = self._replay(log, start)
