@@ -141,6 +141,39 @@ int slx_set_switchglu_fused(int on);
  * (1 fused, 2 two-phase; launch accounting). */
 int slx_switchglu_last_kernels(void);
 
+/* Scratch bytes slx_prefill_grouped needs for n_blocks pair blocks (0 for
+ * an unsupported shape): the fp16 operand images of both phases. */
+size_t slx_prefill_scratch_bytes(int n_blocks, int hidden, int inter,
+                                 int bits);
+
+/* Expert-major prefill (K3) on the tcgen05 tensor cores.  Replaces the
+ * per-batch switch_forward of streamlx/integrate.py:141-232 (_expert_sweep:
+ * pairs grouped by expert, streamlx/pool.py:30-50 gather_qmm gate/up,
+ * swiglu, gather_qmm down) for every pair whose expert has a slot.
+ *   x        [n_rows, hidden] bf16 token rows
+ *   pair_row [n_pairs] int32: x row of each (token, expert) pair, pairs
+ *            grouped by expert
+ *   blocks   [n_blocks][4] int32 {slot, first pair, pairs (1..128), 0}: runs
+ *            of consecutive pairs of one expert (a longer run is split)
+ *   out_row  [n_pairs] int32 output row of each pair, or NULL (= pair index)
+ *   out      [n_out, hidden] bf16 per-pair UNWEIGHTED expert outputs
+ * Rounding as switch_forward: gate/up -> bf16, silu(gate)*up -> bf16,
+ * down -> bf16.  2-bit experts, hidden and inter multiples of 512 (<= 4096).
+ * A block with a bad slot / range, or a pair row out of range, sets
+ * SLX_ERR_OUT_OF_RANGE in *status and is skipped. */
+int slx_prefill_grouped(const slx_expert_bank* bank, const void* x,
+                        int n_rows, const int32_t* pair_row, int n_pairs,
+                        const int32_t* blocks, int n_blocks,
+                        const int32_t* out_row, void* out, int n_out,
+                        void* scratch, size_t scratch_bytes, int32_t* status,
+                        void* stream);
+
+/* Where slx_prefill_grouped's dequantised weight operand lives for the
+ * calling thread: 1 = tensor memory (default; tcgen05.st, no shared-memory
+ * round trip), 0 = a swizzled shared-memory ring.  Same results; returns the
+ * previous setting. */
+int slx_set_prefill_a_tmem(int on);
+
 /* Dense quantized linear y[T, out] = x[T, in] @ dequant(W)^T (bf16 out,
  * fp32 accumulate) over a tile-format matrix (slx_pack_dense).  Trunk
  * projections of the decoder around the expert path (no reference

@@ -36,6 +36,8 @@ EXPORTS = (
     "slx_event_record_external", "slx_event_elapsed_many",
     "slx_router_topk_multi", "slx_set_pdl", "slx_pread_many",
     "slx_set_switchglu_fused", "slx_switchglu_last_kernels",
+    "slx_prefill_scratch_bytes", "slx_prefill_grouped",
+    "slx_set_prefill_a_tmem",
 )
 
 
@@ -153,6 +155,14 @@ def lib() -> C.CDLL:
                                      C.POINTER(C.c_int), C.POINTER(C.c_int)]
         L.slx_copy_many.restype = i32
         L.slx_copy_many.argtypes = [vp, vp, vp, i32, vp]
+        L.slx_prefill_scratch_bytes.restype = sz
+        L.slx_prefill_scratch_bytes.argtypes = [i32, i32, i32, i32]
+        L.slx_prefill_grouped.restype = i32
+        L.slx_prefill_grouped.argtypes = [C.POINTER(slx_expert_bank), vp, i32,
+                                          vp, i32, vp, i32, vp, vp, i32, vp,
+                                          sz, vp, vp]
+        L.slx_set_prefill_a_tmem.restype = i32
+        L.slx_set_prefill_a_tmem.argtypes = [i32]
         _lib = L
     return _lib
 
@@ -419,3 +429,30 @@ def copy_many(dsts: list[int], srcs: list[int], sizes: list[int],
     Z = (C.c_size_t * n)(*sizes)
     rc = lib().slx_copy_many(D, S, Z, n, stream_ptr(stream))
     _check("slx_copy_many", rc)
+
+
+def prefill_scratch_bytes(n_blocks: int, hidden: int, inter: int,
+                          bits: int) -> int:
+    return int(lib().slx_prefill_scratch_bytes(n_blocks, hidden, inter, bits))
+
+
+def set_prefill_a_tmem(on: bool) -> bool:
+    """Prefill weight operand in tensor memory (default) or shared memory."""
+    return bool(lib().slx_set_prefill_a_tmem(1 if on else 0))
+
+
+def prefill_grouped(bank: slx_expert_bank, x: torch.Tensor,
+                    pair_row: torch.Tensor, blocks: torch.Tensor,
+                    out: torch.Tensor, scratch: torch.Tensor,
+                    status: torch.Tensor, out_row: torch.Tensor | None = None,
+                    stream: torch.cuda.Stream | None = None) -> None:
+    """Expert-major prefill over pair blocks (int32 [n_blocks, 4] = slot,
+    first pair, pairs, 0); out [n_out, H] per-pair unweighted outputs."""
+    rc = lib().slx_prefill_grouped(
+        C.byref(bank), x.data_ptr(), x.shape[0], pair_row.data_ptr(),
+        pair_row.numel(), blocks.data_ptr(), blocks.shape[0], ptr(out_row),
+        out.data_ptr(), out.shape[0], scratch.data_ptr(),
+        scratch.numel() * scratch.element_size(), status.data_ptr(),
+        stream_ptr(stream))
+    _check("slx_prefill_grouped", rc)
+    _count(3)

@@ -17,7 +17,7 @@ CSRC = os.path.join(HERE, "csrc")
 ROOT = os.path.dirname(HERE)
 LIB = os.path.join(HERE, "libstreamlx_cuda.so")
 SOURCES = ["slx_api.cu", "slx_qgemv.cu", "slx_router.cu", "slx_trunk.cu",
-           "slx_pack.cu", "slx_io.cu"]
+           "slx_pack.cu", "slx_io.cu", "slx_prefill.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",

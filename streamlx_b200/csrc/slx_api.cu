@@ -17,6 +17,7 @@ thread_local std::string g_err;
 thread_local int g_pdl = 0;
 thread_local int g_fused = 1;
 thread_local int g_glu_kernels = 0;  // kernels the last slx_switchglu launched
+thread_local int g_pf_a_tmem = 1;    // prefill: A operand in TMEM (else smem)
 
 int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -258,6 +259,60 @@ int slx_switchglu(const slx_expert_bank* bank, const slx_shared_expert* shared,
 }
 
 int slx_switchglu_last_kernels(void) { return g_glu_kernels; }
+
+size_t slx_prefill_scratch_bytes(int n_blocks, int hidden, int inter,
+                                 int bits) {
+  if (n_blocks < 0 || bits != 2 || hidden <= 0 || inter <= 0 ||
+      hidden % 512 || inter % 512)
+    return 0;
+  return slx::prefill_scratch_bytes(n_blocks, hidden, inter);
+}
+
+int slx_set_prefill_a_tmem(int on) {
+  const int prev = g_pf_a_tmem;
+  g_pf_a_tmem = on ? 1 : 0;
+  return prev;
+}
+
+int slx_prefill_grouped(const slx_expert_bank* bank, const void* x,
+                        int n_rows, const int32_t* pair_row, int n_pairs,
+                        const int32_t* blocks, int n_blocks,
+                        const int32_t* out_row, void* out, int n_out,
+                        void* scratch, size_t scratch_bytes, int32_t* status,
+                        void* stream) {
+  g_err.clear();
+  if (!bank) return fail(SLX_ERR_INVALID, "slx_prefill_grouped: bank is NULL");
+  const int H = bank->hidden, I = bank->inter;
+  if (bank->bits != 2)
+    return fail(SLX_ERR_UNSUPPORTED, "prefill: bits %d (2-bit experts only)",
+                bank->bits);
+  if (H <= 0 || I <= 0 || H % 512 || I % 512 || H > 4096 || I > 4096)
+    return fail(SLX_ERR_UNSUPPORTED,
+                "prefill: hidden %d / inter %d must be multiples of 512, <= 4096",
+                H, I);
+  if (bank->n_slots < 1 || bank->slot_stride % 16 ||
+      bank->slot_stride < (int64_t)slx::expert_tiled_bytes(H, I, 2))
+    return fail(SLX_ERR_INVALID, "prefill: n_slots %d slot_stride %lld",
+                bank->n_slots, (long long)bank->slot_stride);
+  if (n_blocks < 0 || n_pairs < 0 || n_rows < 0 || n_out < 0)
+    return fail(SLX_ERR_INVALID, "prefill: negative count");
+  if (n_blocks == 0) return SLX_OK;
+  if (!bank->base || !aligned16(bank->base) || !x || !aligned16(x) ||
+      !pair_row || !blocks || !aligned16(blocks) || !out || !aligned16(out))
+    return fail(SLX_ERR_INVALID, "prefill: NULL or misaligned pointer");
+  const size_t need = slx::prefill_scratch_bytes(n_blocks, H, I);
+  if (!scratch || scratch_bytes < need || (reinterpret_cast<uintptr_t>(scratch) & 127))
+    return fail(SLX_ERR_SCRATCH, "prefill: scratch %zu < %zu bytes (128-aligned)",
+                scratch_bytes, need);
+  const int rc = slx::launch_prefill(
+      reinterpret_cast<const uint8_t*>(bank->base), bank->slot_stride,
+      bank->n_slots, H, I, reinterpret_cast<const uint16_t*>(x), n_rows,
+      pair_row, n_pairs, reinterpret_cast<const int4*>(blocks), n_blocks,
+      out_row, reinterpret_cast<uint16_t*>(out), n_out,
+      reinterpret_cast<uint8_t*>(scratch), status, g_pf_a_tmem,
+      reinterpret_cast<cudaStream_t>(stream));
+  return rc ? cuda_check(rc, "slx_prefill_grouped") : SLX_OK;
+}
 
 int slx_set_switchglu_fused(int on) {
   const int prev = g_fused;

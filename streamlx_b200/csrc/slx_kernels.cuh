@@ -113,5 +113,12 @@ int launch_attn_decode(const uint16_t* qkv, int T, int nq, int nkv, int hd,
                        cudaStream_t s);
 int launch_argmax(const uint16_t* logits, int T, int V, int32_t* out,
                   cudaStream_t s);
+size_t prefill_scratch_bytes(int n_blocks, int H, int I);
+int launch_prefill(const uint8_t* bank, long long slot_stride, int n_slots,
+                   int H, int I, const uint16_t* x, int n_rows,
+                   const int32_t* pair_row, int n_pairs, const int4* blocks,
+                   int n_blocks, const int32_t* out_row, uint16_t* out,
+                   int n_out, uint8_t* scratch, int32_t* status, int a_tmem,
+                   cudaStream_t s);
 
 }  // namespace slx

@@ -176,6 +176,13 @@ class StreamingSwitchGLU:
         pool = self.pool
         B, T, k = idx.shape
         x2d = ops.as_bf16_2d(x)
+        if (B * T * k >= ops.PREFILL_MIN_PAIRS and
+                pool.store.__class__.__name__ == "HbmSlotStore" and
+                ops.prefill_supported(pool.hidden, pool.inter, pool.bits)):
+            y = self._pool_prefill(x2d, idx)
+            if scores is None:
+                return y
+            return self._combine(x, y, scores)
         pool.sync_device()
         ids = ops.as_ids_2d(indices, k, x2d.device)
         sh = self.shared
@@ -188,6 +195,23 @@ class StreamingSwitchGLU:
         if scores is None:
             return y.reshape(B, T, k, -1)
         return y.reshape(B, T, -1)
+
+    def _pool_prefill(self, x2d, idx):
+        """Resident experts of a multi-token call on the tensor-core grouped
+        prefill: pairs grouped by the slot of their expert (the host holds
+        the id -> slot map after the call's bookkeeping), each output written
+        at its (token, pick) row.  Returns [B, T, k, H]."""
+        from . import ops
+        pool = self.pool
+        B, T, k = idx.shape
+        flat = idx.reshape(-1).astype(np.int64)
+        slot_of = np.array([pool.id2slot[int(e)] for e in flat], dtype=np.int64)
+        order = np.argsort(slot_of, kind="stable")
+        slots, counts = np.unique(slot_of[order], return_counts=True)
+        row_of_pair = order // k
+        y = ops.prefill_grouped(pool.store.bank, x2d, row_of_pair, slots,
+                                counts, out_row=order, n_out=flat.size)
+        return y.reshape(B, T, k, -1)
 
     def _combine(self, x, y, scores):
         """Score-weighted sum of per-expert outputs (+ shared expert) for the
@@ -249,11 +273,12 @@ class StreamingSwitchGLU:
                    for i0 in range(0, len(uniq), self.sweep_batch)]
         fut = self._sweep_ex.submit(pool.reader.read_experts_raw,
                                     pool.triples_loc, batches[0])
-        y_sorted = None
+        y = None
         if on_gpu:
             H = x_rows.shape[1]
-            y_sorted = torch.empty(sorted_e.size, H, dtype=torch.bfloat16,
-                                   device=x_rows.device)
+            # per-pair outputs land at their (token, pick) rows directly
+            y = torch.empty(sorted_e.size, H, dtype=torch.bfloat16,
+                            device=x_rows.device)
             nb, mini, stride = self._mini_pool(self.sweep_batch)
         for bi, ids in enumerate(batches):
             t0 = time.perf_counter()
@@ -270,33 +295,37 @@ class StreamingSwitchGLU:
             for e in ids:
                 if e in warm_ids:
                     adopt_items.append((pool.adopt(e, None), e))
-            if y_sorted is not None:
+            if y is not None:
                 store = pool.store
                 store.write_to(pool.reader, raw,
                                [(mini.data_ptr() + j * stride, e)
                                 for j, e in enumerate(ids)], release=False)
                 sel = order[lo:hi]
-                slot = np.searchsorted(uniq[i0:i1], sorted_e[lo:hi])
-                xb = x_rows[torch.as_tensor(row_of_pair[sel],
-                                            device=x_rows.device)]
-                sid = torch.as_tensor(slot.astype(np.int32),
-                                      device=x_rows.device).reshape(-1, 1)
                 bank = L.bank_struct(mini, len(ids), pool.hidden, pool.inter,
                                      pool.bits, stride)
-                y_sorted[lo:hi] = ops.switchglu(
-                    bank, xb.contiguous(), sid, 1,
-                    inter=pool.inter).reshape(hi - lo, H)
+                if ops.prefill_supported(pool.hidden, pool.inter, pool.bits):
+                    # tensor-core grouped GEMM over the batch's pairs, each
+                    # output written at its (token, pick) row
+                    ops.prefill_grouped(bank, x_rows, row_of_pair[sel],
+                                        list(range(len(ids))),
+                                        counts[i0:i1], out=y, out_row=sel)
+                else:
+                    slot = np.searchsorted(uniq[i0:i1], sorted_e[lo:hi])
+                    xb = x_rows[torch.as_tensor(row_of_pair[sel],
+                                                device=x_rows.device)]
+                    sid = torch.as_tensor(slot.astype(np.int32),
+                                          device=x_rows.device).reshape(-1, 1)
+                    yb = ops.switchglu(bank, xb.contiguous(), sid, 1,
+                                       inter=pool.inter).reshape(hi - lo, H)
+                    y[torch.as_tensor(sel, device=y.device)] = yb
             pool.store.write(pool.reader, raw, adopt_items)
         if warm_ids:
             for i in np.argsort(counts, kind="stable"):
                 e = int(uniq[i])
                 if e in warm_ids and e in pool.id2slot:
                     pool.id2slot.move_to_end(e)
-        if y_sorted is None:
+        if y is None:
             return None
-        inv = np.empty_like(order)
-        inv[order] = np.arange(order.size)
-        y = y_sorted[torch.as_tensor(inv, device=y_sorted.device)]
         return y.reshape(b, t, k, H)
 
     def _slice_prefill(self, x, idx):

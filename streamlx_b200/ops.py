@@ -104,3 +104,58 @@ def switch_forward_ids(pool, x, expert_ids) -> torch.Tensor:
     y = switchglu(pool.store.bank, x2d, ids, k, table=pool.store.table_dev,
                   inter=pool.inter)
     return y.reshape(1, 1, k, -1)
+
+
+PREFILL_BLOCK = 128   # pairs per block (the kernel's MMA N)
+# pairs per call from which the pool path uses the grouped tensor-core
+# prefill instead of the per-token GEMV kernels
+PREFILL_MIN_PAIRS = 64
+
+
+def prefill_supported(hidden: int, inter: int, bits: int) -> bool:
+    return bits == 2 and hidden % 512 == 0 and inter % 512 == 0 and \
+        hidden <= 4096 and inter <= 4096
+
+
+def prefill_blocks(slots, counts) -> "np.ndarray":
+    """Blocks {slot, first pair, pairs, 0} of pairs grouped by expert:
+    segment i (``counts[i]`` consecutive pairs of slot ``slots[i]``) is split
+    into runs of at most PREFILL_BLOCK pairs."""
+    import numpy as np
+    rows = []
+    p = 0
+    for s, n in zip(slots, counts):
+        n = int(n)
+        for o in range(0, n, PREFILL_BLOCK):
+            rows.append((int(s), p + o, min(PREFILL_BLOCK, n - o), 0))
+        p += n
+    return np.asarray(rows, dtype=np.int32).reshape(-1, 4)
+
+
+def prefill_grouped(bank, x2d: torch.Tensor, pair_row, slots, counts, *,
+                    out: torch.Tensor | None = None, out_row=None,
+                    n_out: int | None = None) -> torch.Tensor:
+    """Expert-major prefill on the tensor cores: pairs grouped by expert
+    (``pair_row[p]`` = x row of pair p; segment i = ``counts[i]`` pairs of
+    slot ``slots[i]``).  Returns per-pair unweighted outputs [P, H] (rows
+    ``out_row[p]`` when given)."""
+    import numpy as np
+    dev = x2d.device
+    H = x2d.shape[1]
+    blocks = prefill_blocks(slots, counts)
+    P = int(np.sum(counts)) if len(counts) else 0
+    if out is None:
+        out = torch.empty(n_out if n_out is not None else P, H,
+                          dtype=torch.bfloat16, device=dev)
+    if blocks.shape[0] == 0:
+        return out
+    pr = torch.as_tensor(np.asarray(pair_row, dtype=np.int32), device=dev)
+    bl = torch.as_tensor(blocks, device=dev)
+    orow = None if out_row is None else torch.as_tensor(
+        np.asarray(out_row, dtype=np.int32), device=dev)
+    need = L.prefill_scratch_bytes(blocks.shape[0], H, bank.inter, bank.bits)
+    if need == 0:
+        raise L.SlxError("slx_prefill_scratch_bytes", -2, "unsupported shape")
+    sc = scratch(need, dev, tag="prefill")
+    L.prefill_grouped(bank, x2d, pr, bl, out, sc, _status(dev), out_row=orow)
+    return out
