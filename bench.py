@@ -204,6 +204,267 @@ def run_reference(args) -> None:
     }), flush=True)
 
 
+PREFILL_SHAPE = dict(hidden=2560, inter=1024, experts=256, top_k=10,
+                     tokens=2048, zipf_s=1.1, layers=48)
+
+
+def prefill_measure(dev, reps: int = 10, warmup: int = 3) -> dict:
+    """Expert-major prefill of one 117B-shaped MoE layer on the tensor cores:
+    2048 tokens x top-10 of 256 2-bit experts (Zipf 1.1 popularity via
+    Gumbel-top-k on log p), every expert resident in an HBM slot pool
+    (629 MB, larger than L2).  One step = one slx_prefill_grouped call
+    (activation pack + gate/up/SwiGLU + down, three launches)."""
+    import torch
+
+    from streamlx_b200 import _lib as L
+    from streamlx_b200 import ops, synth
+    c = PREFILL_SHAPE
+    H, I, E, k, T = c["hidden"], c["inter"], c["experts"], c["top_k"], c["tokens"]
+    g = torch.Generator(device=dev).manual_seed(SEED)
+    stride = L.slot_stride(H, I, 2)
+    pool = torch.empty(E * stride, dtype=torch.uint8, device=dev)
+    for e0 in range(0, E, 16):
+        mats = []
+        for (o, i) in ((I, H), (I, H), (H, I)):
+            w = torch.randn(16, o, i, generator=g, device=dev) * 0.02
+            mats.append(synth.quantize_affine(w, 2, 64))
+            del w
+        ex = [tuple((m[0][j], m[1][j], m[2][j]) for m in mats)
+              for j in range(16)]
+        L.pack_experts(ex, H, I, 2, [pool.data_ptr() + (e0 + j) * stride
+                                     for j in range(16)])
+    torch.cuda.synchronize()
+    bank = L.bank_struct(pool, E, H, I, 2, stride)
+    rng = np.random.default_rng(SEED)
+    logp = synth.zipf_bias(E, c["zipf_s"], SEED)
+    gum = rng.gumbel(size=(T, E)).astype(np.float32)
+    ids = np.argsort(-(logp[None, :] + gum), axis=1)[:, :k]
+    flat = ids.reshape(-1)
+    order = np.argsort(flat, kind="stable")
+    slots, counts = np.unique(flat[order], return_counts=True)
+    blocks = ops.prefill_blocks(slots, counts)
+    x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    pr = torch.as_tensor((order // k).astype(np.int32), device=dev)
+    orow = torch.as_tensor(order.astype(np.int32), device=dev)
+    bl = torch.as_tensor(blocks, device=dev)
+    out = torch.empty(T * k, H, dtype=torch.bfloat16, device=dev)
+    sc = torch.empty(L.prefill_scratch_bytes(blocks.shape[0], H, I, 2),
+                     dtype=torch.uint8, device=dev)
+    st = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def step():
+        L.prefill_grouped(bank, x, pr, bl, out, sc, st, out_row=orow)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if int(st.item()) != 0:
+        raise RuntimeError(f"prefill status {int(st.item())}")
+    evs = [(torch.cuda.Event(enable_timing=True),
+            torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    for a, b in evs:
+        a.record()
+        step()
+        b.record()
+    torch.cuda.synchronize()
+    ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))
+    flops = T * k * 6.0 * H * I
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak, kind = float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:   # noqa: BLE001
+        peak, kind = 1590.0, "fallback"
+    tf = flops / (ms / 1000.0) / 1e12
+    return {"workload": "laguna_c4_layer", "tokens": T, "pairs": T * k,
+            "blocks": int(blocks.shape[0]), "experts_routed": int(len(slots)),
+            "ms_per_layer": round(ms, 4), "tflops": round(tf, 1),
+            "peak_tflops": peak, "peak_kind": kind,
+            "frac": round(tf / peak, 4), "bound": "tensor",
+            "flops_per_layer": flops,
+            "tokens_per_s_48_layers": round(T / (c["layers"] * ms / 1000.0), 1),
+            "weights": "all 256 experts resident (629 MB); the sweep's disk "
+                       "streaming is not in this number",
+            "launches_per_layer": 3}
+
+
+def run_prefill(args) -> None:
+    import torch
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    res = prefill_measure(torch.device("cuda", local), reps=args.steps,
+                          warmup=args.warmup)
+    if rank == 0:
+        print(json.dumps({"metric": "prefill_tflops", "value": res["tflops"],
+                          "unit": "TFLOP/s", "n_gpus": 1, **res}), flush=True)
+
+
+def _random_experts(E, H, I, dev, seed, pool=None, ids=None):
+    """Tile-format pool of E 2-bit experts with random codes and sane
+    scales/biases (throughput runs: values only need to be finite).  With
+    ``ids``, slot j holds expert ids[j] of the seeded set (same bytes on every
+    rank)."""
+    import torch
+
+    from streamlx_b200 import _lib as L
+    stride = L.slot_stride(H, I, 2)
+    ids = list(range(E)) if ids is None else list(ids)
+    if pool is None:
+        pool = torch.empty(len(ids) * stride, dtype=torch.uint8, device=dev)
+    for j0 in range(0, len(ids), 16):
+        chunk = ids[j0:j0 + 16]
+        ex = []
+        keep = []
+        for e in chunk:
+            g = torch.Generator(device=dev).manual_seed(seed * 100003 + e)
+            trip = []
+            for (o, i) in ((I, H), (I, H), (H, I)):
+                w = torch.randint(-2**31, 2**31 - 1, (o, i // 16), generator=g,
+                                  device=dev, dtype=torch.int32)
+                sc = (torch.rand(o, i // 64, generator=g, device=dev) * 0.01
+                      + 0.005).to(torch.bfloat16)
+                bi = (torch.rand(o, i // 64, generator=g, device=dev) * -0.02
+                      - 0.01).to(torch.bfloat16)
+                trip.append((w, sc, bi))
+                keep.append((w, sc, bi))
+            ex.append(tuple(trip))
+        L.pack_experts(ex, H, I, 2, [pool.data_ptr() + (j0 + j) * stride
+                                     for j in range(len(chunk))])
+        torch.cuda.synchronize()
+    return pool, stride
+
+
+class _ResidentPool:
+    """Slot pool view for expert_parallel.pool_expert_fn: expert ids
+    [e0, e1) in slots 0.. (every expert resident)."""
+
+    def __init__(self, bank, e0, e1, hidden, inter):
+        self.id2slot = {e: e - e0 for e in range(e0, e1)}
+        self.hidden, self.inter, self.bits = hidden, inter, 2
+
+        class _S:
+            pass
+        self.store = _S()
+        self.store.bank = bank
+
+
+def run_ep(args) -> None:
+    """Expert-parallel MoE layer (117B-shaped: hidden 2560, 256 2-bit
+    experts top-10, inter 1024) over the torchrun ranks: experts 256/N per
+    GPU, NCCL all-to-all of token rows.  Workloads: batch-1 decode (the
+    token on every rank, one all-reduce), batch-64 decode and a 2048-token
+    prefill (tokens split over the ranks, dispatch + combine all-to-all)."""
+    import datetime
+
+    import torch
+    import torch.distributed as tdist
+
+    from streamlx_b200 import _lib as L
+    from streamlx_b200 import expert_parallel as EPM
+    from streamlx_b200 import synth
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                             device_id=dev)
+    H, I, E, k = 2560, 1024, 256, 10
+    n_layers = 2           # distinct weights, alternated: > L2 per rank
+    e0, e1 = EPM.local_range(E, world, rank)
+    banks = []
+    pools = []
+    for li in range(n_layers):
+        pool, stride = _random_experts(E, H, I, dev, seed=li,
+                                       ids=range(e0, e1))
+        pools.append(pool)
+        banks.append(L.bank_struct(pool, e1 - e0, H, I, 2, stride))
+    moes = [EPM.ExpertParallelMoE(
+        E, EPM.pool_expert_fn(_ResidentPool(b, e0, e1, H, I)))
+        for b in banks]
+    logp = synth.zipf_bias(E, 1.1, SEED)
+
+    def route(T, seed):
+        r = np.random.default_rng(seed)
+        g = r.gumbel(size=(T, E)).astype(np.float32)
+        ids = np.argsort(-(logp[None, :] + g), axis=1)[:, :k]
+        sc = r.random((T, k)).astype(np.float32)
+        return ids, sc / sc.sum(1, keepdims=True)
+
+    results = {}
+    for name, T_glob, mode in (("decode_b1", 1, "replicated"),
+                               ("decode_b64", 64, "sharded"),
+                               ("prefill_2048", 2048, "sharded")):
+        T = T_glob if mode == "replicated" else T_glob // world
+        gx = torch.Generator(device=dev).manual_seed(SEED + (0 if mode == "replicated" else rank))
+        x = torch.randn(T, H, generator=gx, device=dev).to(torch.bfloat16)
+        seeds = [1000 * (0 if mode == "replicated" else rank) + s
+                 for s in range(args.steps + args.warmup)]
+        plans = [route(T, s) for s in seeds]
+        for s in range(args.warmup):
+            ids, sc = plans[s]
+            moes[s % n_layers].forward(x, ids, sc, tokens=mode)
+        torch.cuda.synchronize()
+        tdist.barrier()
+        e_a, e_b = (torch.cuda.Event(enable_timing=True),
+                    torch.cuda.Event(enable_timing=True))
+        b0 = sum(m.bytes_sent for m in moes)
+        e_a.record()
+        for s in range(args.warmup, args.warmup + args.steps):
+            ids, sc = plans[s]
+            moes[s % n_layers].forward(x, ids, sc, tokens=mode)
+        e_b.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e_a.elapsed_time(e_b) / args.steps], device=dev)
+        tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
+        ms = float(t.item())
+        moved = (sum(m.bytes_sent for m in moes) - b0) / args.steps
+        uniq = len(np.unique(np.concatenate([p[0].reshape(-1) for p in plans[args.warmup:]])))
+        results[name] = {"tokens": T_glob, "ms_per_layer": round(ms, 4),
+                         "tok_s_48_layers": round(T_glob / (48 * ms / 1000.0), 2),
+                         "comm_bytes_per_layer_rank0": int(moved),
+                         "tokens_mode": mode}
+        if args.check:
+            # every rank recomputes its own tokens with all 256 experts
+            from streamlx_b200 import ops
+            full, fstride = _random_experts(E, H, I, dev, seed=(args.warmup) % n_layers)
+            fbank = L.bank_struct(full, E, H, I, 2, fstride)
+            ids, sc = plans[args.warmup]
+            y_ep = moes[args.warmup % n_layers].forward(x, ids, sc, tokens=mode)
+            flat = ids.reshape(-1)
+            order = np.argsort(flat, kind="stable")
+            sl, cn = np.unique(flat[order], return_counts=True)
+            yp = ops.prefill_grouped(fbank, x, order // k, sl, cn,
+                                     out_row=order, n_out=flat.size) \
+                if flat.size >= 64 else ops.switchglu(
+                    fbank, x[torch.as_tensor(np.arange(flat.size) // k, device=dev)].contiguous(),
+                    torch.as_tensor(flat.astype(np.int32), device=dev).reshape(-1, 1), 1,
+                    inter=I).reshape(flat.size, H)
+            want = (yp.float().view(T, k, H) *
+                    torch.as_tensor(sc, device=dev).reshape(T, k, 1)).sum(1)
+            want = want.to(torch.bfloat16).float()   # rounded like the output
+            d = (y_ep.float() - want).abs().max().item()
+            rel = ((y_ep.float() - want).norm() / want.norm()).item()
+            dd = torch.tensor([d, rel], device=dev)
+            tdist.all_reduce(dd, op=tdist.ReduceOp.MAX)
+            results[name]["check_max_abs"] = float(dd[0])
+            results[name]["check_rel_l2"] = float(dd[1])
+            del full
+    tdist.barrier()
+    tdist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps({"metric": "ep_moe_layer", "n_gpus": world,
+                          "experts_per_gpu": e1 - e0, "steps": args.steps,
+                          "warmup": args.warmup,
+                          "config": {"workload": "laguna_c5_layer",
+                                     "hidden": H, "inter": I, "experts": E,
+                                     "top_k": k, "bits": 2,
+                                     "parallelism": f"ep{world}"},
+                          **results}), flush=True)
+        if args.check:
+            bad = [n for n, r in results.items()
+                   if r["check_max_abs"] > 2e-2 or r["check_rel_l2"] > 1e-3]
+            if bad:
+                raise SystemExit(f"EP check failed: {bad}")
+
+
 def run_ours(args) -> None:
     import torch
     import torch.distributed as tdist
@@ -309,6 +570,10 @@ def run_ours(args) -> None:
     peak, peak_kind = measured_peak()
     traffic = traffic_from_profile()
 
+    pre = None
+    if not args.no_prefill:
+        pre = prefill_measure(dev)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, n, cores = cpu_oracle_rate(d, budget_s=args.cpu_seconds)
@@ -356,6 +621,8 @@ def run_ours(args) -> None:
         "setup_s": {"load": round(t_load, 1), "prompt_and_warmup":
                     round(t_prompt, 1)},
     }
+    if pre:
+        res["prefill"] = pre
     if cpu:
         res["cpu_baseline"] = cpu
     print(json.dumps(res), flush=True)
@@ -373,11 +640,22 @@ def main():
     ap.add_argument("--budget-gib", type=float, default=BUDGET / (1 << 30))
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true",
+                    help="skip the expert-major prefill measurement")
+    ap.add_argument("--check", action="store_true",
+                    help="ep mode: compare with an all-experts computation")
+    ap.add_argument("--mode", default="decode",
+                    choices=["decode", "prefill", "ep"],
+                    help="prefill: only the prefill measurement (its own line)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.mode == "prefill":
+        run_prefill(args)
+    elif args.mode == "ep":
+        run_ep(args)
     else:
         run_ours(args)
 

@@ -40,13 +40,13 @@
 //
 // Warp roles (448 threads, one CTA per SM, persistent over work items):
 //   warp 0      TMEM allocation; lane 0 streams B chunks (cp.async.bulk,
-//               the TMA engine) into a 4-stage shared-memory ring;
+//               the TMA engine) into an 8-stage shared-memory ring;
 //   warp 1      lane 0 issues the MMAs (M128 x N x K16, kind::f16) and
 //               commits them to the stage / accumulator barriers;
 //   warps 2-5   epilogue: tcgen05.ld of the accumulator (two TMEM buffers so
 //               the next item's MMAs overlap it);
 //   warps 6-13  dequantization: each thread owns one A row (TMEM lane),
-//               prefetches its packed codes with cp.async four tasks ahead,
+//               prefetches its packed codes with cp.async eight tasks ahead,
 //               and writes fp16 A columns straight into TMEM (tcgen05.st;
 //               the MMA reads A from TMEM) or, in the shared-memory
 //               variant, into a swizzled A ring.
@@ -60,16 +60,20 @@ namespace slx {
 namespace {
 
 constexpr int kNT = 128;            // max pairs per block (MMA N)
-constexpr int kS = 4;               // pipeline stages
+constexpr int kS = 8;               // max pipeline stages (64-column chunks in flight)
+// stages: 8 with the weight operand in TMEM (A ring 8 x 32 columns + two
+// 128-column accumulators = 512), 4 with it in shared memory (the A ring
+// then takes 4 x 16 KB of shared memory)
+constexpr int stages(bool atmem) { return atmem ? 8 : 4; }
 constexpr int kRowB = 128;          // bytes of one 64-column fp16 chunk row
 constexpr int kStageB = kNT * kRowB;     // B chunk (16 KB)
 constexpr int kStageA = 128 * kRowB;     // A chunk, shared-memory variant
 constexpr int kThreads = 448;
 constexpr int kDqThreads = 256;
-constexpr int kDqDepth = 4;         // cp.async tasks in flight per thread
-constexpr int kAccCol = 128;        // TMEM: A ring at 0..127, accumulators after
+constexpr int kDqDepth = 8;         // cp.async tasks in flight per thread
+constexpr int kAccCol = 32 * kS;    // TMEM: A ring at 0..255, accumulators after
 constexpr int kTmemCols = 512;
-constexpr int kXchStride = kNT + 1; // floats per row of the up-value exchange
+constexpr int kXchStride = kNT + 2; // bf16 per row of the up-value exchange
 
 // --------------------------------------------------------------- tcgen05 --
 
@@ -210,7 +214,7 @@ struct PrefillArgs {
   const int32_t* out_row;
   int n_out;
   int32_t* status;
-  int off_b, off_a, off_stg, off_btab, off_xch, off_hst;  // from the aligned base
+  int off_b, off_a, off_stg, off_btab, off_xch, off_hst, off_orow;  // from the aligned base
 };
 
 namespace {
@@ -253,29 +257,36 @@ SLX_DEV int bias_ksteps(int nG, int cb) {  // issued K steps of bias chunk cb
   return k > 4 ? 4 : k;
 }
 
-// Packed row of A row m (thread) for a task: address of its 16-byte code
-// unit of group c and of its scale|bias word.
+// Where A row m (this thread) of an item reads its packed codes: the row's
+// first byte, its swizzle key, and its scale|bias word of group 0 with the
+// word stride between groups (computed once per item).
+struct RowSrc {
+  const uint8_t* row;
+  const uint32_t* sb;
+  int swz, sbs, j;
+};
 template <int PHASE>
-SLX_DEV void a_row_src(const PrefillArgs& a, int slot, int mb, int m, int c,
-                       const uint8_t*& codes, const uint32_t*& sb) {
+SLX_DEV void row_src(const PrefillArgs& a, int slot, int mb, int m, RowSrc& o) {
   const uint8_t* e = a.bank + (size_t)slot * a.slot_stride;
   if (PHASE == 1) {
     const int RB = tile_rb(a.H, 2);
-    const bool swz = tile_swizzled(a.H, 2);
     const int r = mb * 64 + (m & 63), mat = m >> 6;
     const int t = r >> 4, tr = r & 15;
     const uint8_t* base = e + (size_t)t * pair_tile_bytes(a.H, 2);
-    codes = base + (size_t)(mat * 16 + tr) * RB + ((swz ? (c ^ (tr & 7)) : c) << 4);
-    sb = reinterpret_cast<const uint32_t*>(base + 32 * RB) + c * 32 + mat * 16 + tr;
+    o.row = base + (size_t)(mat * 16 + tr) * RB;
+    o.swz = tile_swizzled(a.H, 2) ? (tr & 7) : 0;
+    o.sb = reinterpret_cast<const uint32_t*>(base + 32 * RB) + mat * 16 + tr;
+    o.sbs = 32;
   } else {
     const int RB = tile_rb(a.I, 2);
-    const bool swz = tile_swizzled(a.I, 2);
     const int r = mb * 128 + m;
     const int t = r >> 4, tr = r & 15;
     const uint8_t* base = e + expert_a_bytes(a.H, a.I, 2) +
                           (size_t)t * single_tile_bytes(a.I, 2);
-    codes = base + (size_t)tr * RB + ((swz ? (c ^ (tr & 7)) : c) << 4);
-    sb = reinterpret_cast<const uint32_t*>(base + 16 * RB) + c * 16 + tr;
+    o.row = base + (size_t)tr * RB;
+    o.swz = tile_swizzled(a.I, 2) ? (tr & 7) : 0;
+    o.sb = reinterpret_cast<const uint32_t*>(base + 16 * RB) + tr;
+    o.sbs = 16;
   }
 }
 
@@ -284,11 +295,12 @@ SLX_DEV void a_row_src(const PrefillArgs& a, int slot, int mb, int m, int c,
 template <int PHASE, bool ATMEM>
 __global__ void __launch_bounds__(kThreads, 1)
     k_prefill(const __grid_constant__ PrefillArgs a) {
+  constexpr int S = stages(ATMEM);
   extern __shared__ __align__(16) uint8_t smem_raw[];
-  uint64_t* bar_tx = reinterpret_cast<uint64_t*>(smem_raw);  // [kS] B bytes landed
-  uint64_t* bar_dq = bar_tx + kS;                             // [kS] A written
-  uint64_t* bar_empty = bar_dq + kS;                          // [kS] MMAs done
-  uint64_t* bar_full = bar_empty + kS;                        // [2] accumulator ready
+  uint64_t* bar_tx = reinterpret_cast<uint64_t*>(smem_raw);  // [S] B bytes landed
+  uint64_t* bar_dq = bar_tx + kS;                            // [S] A written
+  uint64_t* bar_empty = bar_dq + kS;                         // [S] MMAs done
+  uint64_t* bar_full = bar_empty + kS;                       // [2] accumulator ready
   uint64_t* bar_free = bar_full + 2;                          // [2] accumulator drained
   uint64_t* bar_done = bar_free + 2;                          // all MMAs complete
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_done + 1);
@@ -300,12 +312,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sA = base + a.off_a;
   uint8_t* stg = base + a.off_stg;
   __half* btab = reinterpret_cast<__half*>(base + a.off_btab);
-  float* xch = reinterpret_cast<float*>(base + a.off_xch);
+  uint16_t* xch = reinterpret_cast<uint16_t*>(base + a.off_xch);  // up values, bf16
   uint8_t* hst = base + a.off_hst;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kS; ++i) {
+    for (int i = 0; i < S; ++i) {
       mbar_init(&bar_tx[i], 1);
       mbar_init(&bar_dq[i], kDqThreads / 32);
       mbar_init(&bar_empty[i], 1);
@@ -339,8 +351,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       cur_init(a, t);
       uint32_t g = 0;
       for (; !t.end && !*abort_flag; cur_next(a, t), ++g) {
-        const int st = g % kS;
-        if (!mbar_wait(&bar_empty[st], ((g / kS) & 1) ^ 1, a.status)) { fail(SLX_ERR_DEVICE_TIMEOUT); break; }
+        const int st = g % S;
+        if (!mbar_wait(&bar_empty[st], ((g / S) & 1) ^ 1, a.status)) { fail(SLX_ERR_DEVICE_TIMEOUT); break; }
         const uint32_t bytes = (uint32_t)npad16(t.n) * kRowB;
         const uint8_t* src = a.bimg + ((size_t)t.blk * a.nC + t.c) * kStageB;
         mbar_arrive_expect_tx(&bar_tx[st], bytes);
@@ -348,8 +360,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // drain: every issued copy has landed before the CTA exits
       const uint32_t issued = g;
-      for (uint32_t h = issued > kS ? issued - kS : 0; h < issued; ++h)
-        mbar_wait(&bar_tx[h % kS], (h / kS) & 1, a.status);
+      for (uint32_t h = issued > S ? issued - S : 0; h < issued; ++h)
+        mbar_wait(&bar_tx[h % S], (h / S) & 1, a.status);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------- MMA issue ----
@@ -366,8 +378,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t d = tmem + kAccCol + buf * kNT;
         const uint32_t idesc = idesc_f16(npad16(t.n));
         for (int c = 0; c < a.nC; ++c, ++g) {
-          const int st = g % kS;
-          const uint32_t ph = (g / kS) & 1;
+          const int st = g % S;
+          const uint32_t ph = (g / S) & 1;
           if (!mbar_wait(&bar_tx[st], ph, a.status) ||
               !mbar_wait(&bar_dq[st], ph, a.status)) {
             fail(SLX_ERR_DEVICE_TIMEOUT);
@@ -410,7 +422,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                  mbar_wait(&bar_full[buf], (jl >> 1) & 1, a.status));
       if (!ok) fail(SLX_ERR_DEVICE_TIMEOUT);
       bool stop = !ok || *abort_flag;
-      stop = PHASE == 1 ? named_bar_or(1, 128, stop) : __any_sync(0xffffffffu, stop);
+      stop = named_bar_or(1, 128, stop);
       if (stop) break;
       tc_fence_after();
       const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16) + kAccCol + buf * kNT;
@@ -426,7 +438,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_wait_ld();
 #pragma unroll
             for (int i = 0; i < 16; ++i)
-              xch[r * kXchStride + cc + i] = round_bf16(__uint_as_float(v[i]));
+              xch[r * kXchStride + cc + i] = f32_to_bf16(__uint_as_float(v[i]));
           }
         }
         named_bar(1, 128);
@@ -440,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int i = 0; i < 16; ++i) {
               const int n = cc + i;
               const float gt = round_bf16(__uint_as_float(v[i]));
-              const float up = xch[r * kXchStride + n];
+              const float up = bf16_to_f32(xch[r * kXchStride + n]);
               const float h = round_bf16(silu_f32(gt) * up);
               *reinterpret_cast<uint16_t*>(hst + sw_off(n, pos)) =
                   h_bits(__float2half_rn(h));
@@ -478,6 +490,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           bulk_commit();
         }
       } else {
+        // output rows of the item's pairs, staged once (one load per thread)
+        int32_t* orow = reinterpret_cast<int32_t*>(base + a.off_orow);
+        if (te < t.n) {
+          const int p = t.p0 + te;
+          orow[te] = a.out_row ? a.out_row[p] : p;
+        }
+        named_bar(1, 128);
         const int hr = t.mb * 128 + 32 * q + lane;
         for (int cc = 0; cc < t.n; cc += 16) {
           uint32_t v[16];
@@ -487,8 +506,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 16; ++i) {
             const int n = cc + i;
             if (n < t.n) {
-              const int p = t.p0 + n;
-              const int row = a.out_row ? a.out_row[p] : p;
+              const int row = orow[n];
               if (row >= 0 && row < a.n_out)
                 a.out[(size_t)row * a.H + hr] = f32_to_bf16(__uint_as_float(v[i]));
               else if (q == 0 && lane == 0)
@@ -497,6 +515,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         tc_fence_before();
+        named_bar(1, 128);  // orow is rewritten by the next item
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar_free[buf]);
@@ -514,14 +533,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     Cur pf, cu;
     cur_init(a, pf);
     cur_init(a, cu);
+    RowSrc rs;
+    rs.j = -1;
     auto issue = [&](int slot) {
       if (!pf.end && pf.c < a.nG) {
-        const uint8_t* codes;
-        const uint32_t* sb;
-        a_row_src<PHASE>(a, pf.slot, pf.mb, m, pf.c, codes, sb);
+        if (rs.j != pf.j) {
+          row_src<PHASE>(a, pf.slot, pf.mb, m, rs);
+          rs.j = pf.j;
+        }
         const uint32_t d = smem_u32(my_stg + slot * 16);
-        cp_async8(d, codes + 8 * grp);
-        cp_async4(d + 8, sb);
+        cp_async8(d, rs.row + ((pf.c ^ rs.swz) << 4) + 8 * grp);
+        cp_async4(d + 8, rs.sb + pf.c * rs.sbs);
       }
       cp_async_commit();
     };
@@ -568,9 +590,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           out[w] = hb | (hb << 16);
         }
       }
-      const int st = g % kS;
+      const int st = g % S;
       if (!__all_sync(0xffffffffu,
-                      mbar_wait(&bar_empty[st], ((g / kS) & 1) ^ 1, a.status))) {
+                      mbar_wait(&bar_empty[st], ((g / S) & 1) ^ 1, a.status))) {
         fail(SLX_ERR_DEVICE_TIMEOUT);
         break;
       }
@@ -672,19 +694,21 @@ namespace {
 int pf_chunks(int nG) { return nG + (nG + 31) / 32; }
 
 struct SmemPlan {
-  int off_b, off_a, off_stg, off_btab, off_xch, off_hst, bytes;
+  int off_b, off_a, off_stg, off_btab, off_xch, off_hst, off_orow, bytes;
 };
 
 SmemPlan plan_smem(int phase, bool atmem, int nG) {
   SmemPlan p = {};
   int o = 0;
-  p.off_b = o;   o += kS * kStageB;
+  p.off_b = o;   o += stages(atmem) * kStageB;
   p.off_hst = o; if (phase == 1) o += kStageB;
-  p.off_a = o;   if (!atmem) o += kS * kStageA;
+  p.off_a = o;   if (!atmem) o += stages(atmem) * kStageA;
   p.off_stg = o; o += kDqThreads * kDqDepth * 16;
   p.off_btab = o; o += nG * kDqThreads * 2;
   o = (o + 15) & ~15;
-  p.off_xch = o; if (phase == 1) o += 64 * kXchStride * 4;
+  p.off_xch = o; if (phase == 1) o += 64 * kXchStride * 2;
+  o = (o + 15) & ~15;
+  p.off_orow = o; if (phase == 2) o += kNT * 4;
   // + barrier area (256) + worst-case 1024 alignment; at least 120 KB so one
   // CTA (and one 512-column TMEM allocation) per SM
   int bytes = o + 256 + 1024;
@@ -771,6 +795,7 @@ int launch_prefill(const uint8_t* bank, long long slot_stride, int n_slots,
     const SmemPlan sp = plan_smem(1, a_tmem != 0, nG1);
     p.off_b = sp.off_b; p.off_a = sp.off_a; p.off_stg = sp.off_stg;
     p.off_btab = sp.off_btab; p.off_xch = sp.off_xch; p.off_hst = sp.off_hst;
+    p.off_orow = sp.off_orow;
     if (sp.bytes > 227 * 1024) return SLX_ERR_UNSUPPORTED;
     const int rc = a_tmem ? launch_phase<1, true>(p, sp.bytes, s)
                           : launch_phase<1, false>(p, sp.bytes, s);
@@ -787,6 +812,7 @@ int launch_prefill(const uint8_t* bank, long long slot_stride, int n_slots,
     const SmemPlan sp = plan_smem(2, a_tmem != 0, nG2);
     p.off_b = sp.off_b; p.off_a = sp.off_a; p.off_stg = sp.off_stg;
     p.off_btab = sp.off_btab; p.off_xch = sp.off_xch; p.off_hst = sp.off_hst;
+    p.off_orow = sp.off_orow;
     if (sp.bytes > 227 * 1024) return SLX_ERR_UNSUPPORTED;
     const int rc = a_tmem ? launch_phase<2, true>(p, sp.bytes, s)
                           : launch_phase<2, false>(p, sp.bytes, s);

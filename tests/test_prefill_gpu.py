@@ -48,7 +48,7 @@ def _oracle(npt, qp, x, pair_row, experts):
     return want
 
 
-@pytest.mark.parametrize("a_tmem", [True, False])
+@pytest.mark.parametrize("a_tmem", [False, True])
 @pytest.mark.parametrize("E,H,I,counts", [
     (3, 512, 512, [5, 16, 37]),                 # ragged, single blocks
     (4, 1024, 512, [1, 130, 0, 64]),            # a split block, an empty expert
