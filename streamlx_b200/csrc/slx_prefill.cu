@@ -40,13 +40,13 @@
 //
 // Warp roles (448 threads, one CTA per SM, persistent over work items):
 //   warp 0      TMEM allocation; lane 0 streams B chunks (cp.async.bulk,
-//               the TMA engine) into an 8-stage shared-memory ring;
+//               the TMA engine) into a 4-stage ring of two-chunk stages;
 //   warp 1      lane 0 issues the MMAs (M128 x N x K16, kind::f16) and
 //               commits them to the stage / accumulator barriers;
 //   warps 2-5   epilogue: tcgen05.ld of the accumulator (two TMEM buffers so
 //               the next item's MMAs overlap it);
 //   warps 6-13  dequantization: each thread owns one A row (TMEM lane),
-//               prefetches its packed codes with cp.async eight tasks ahead,
+//               prefetches its packed codes with cp.async eight chunks ahead,
 //               and writes fp16 A columns straight into TMEM (tcgen05.st;
 //               the MMA reads A from TMEM) or, in the shared-memory
 //               variant, into a swizzled A ring.
@@ -60,18 +60,19 @@ namespace slx {
 namespace {
 
 constexpr int kNT = 128;            // max pairs per block (MMA N)
-constexpr int kS = 8;               // max pipeline stages (64-column chunks in flight)
-// stages: 8 with the weight operand in TMEM (A ring 8 x 32 columns + two
-// 128-column accumulators = 512), 4 with it in shared memory (the A ring
-// then takes 4 x 16 KB of shared memory)
-constexpr int stages(bool atmem) { return atmem ? 8 : 4; }
+constexpr int kCPS = 2;             // 64-column chunks per pipeline stage
+constexpr int kS = 4;               // max pipeline stages
+// stages: 4 with the weight operand in TMEM (A ring 4 x 64 columns + two
+// 128-column accumulators = 512), 2 with it in shared memory (the A ring
+// then takes 2 x 32 KB of shared memory); 8 resp. 4 chunks in flight
+constexpr int stages(bool atmem) { return atmem ? 4 : 2; }
 constexpr int kRowB = 128;          // bytes of one 64-column fp16 chunk row
 constexpr int kStageB = kNT * kRowB;     // B chunk (16 KB)
 constexpr int kStageA = 128 * kRowB;     // A chunk, shared-memory variant
 constexpr int kThreads = 448;
 constexpr int kDqThreads = 256;
-constexpr int kDqDepth = 8;         // cp.async tasks in flight per thread
-constexpr int kAccCol = 32 * kS;    // TMEM: A ring at 0..255, accumulators after
+constexpr int kDqDepth = 4;         // cp.async tasks (stages) in flight per thread
+constexpr int kAccCol = 32 * kCPS * kS;  // TMEM: A ring at 0..255, accumulators after
 constexpr int kTmemCols = 512;
 constexpr int kXchStride = kNT + 2; // bf16 per row of the up-value exchange
 
@@ -206,7 +207,8 @@ struct PrefillArgs {
   int n_slots, H, I;
   const int4* blocks;  // {slot, first pair, pairs, 0}
   int n_blocks, n_pairs, n_items, n_mb;
-  int nG, nC;          // this phase: groups along K, chunks incl. bias chunks
+  int nG, nC, nStg;    // this phase: groups along K, chunks incl. bias
+                       // chunks, pipeline stages per item
   const uint8_t* bimg; // this phase's B image [n_blocks][nC][kNT][128]
   uint8_t* himg;       // phase 1 output: phase 2's B image
   int nG2, nC2;
@@ -246,8 +248,9 @@ SLX_DEV void cur_seek(const PrefillArgs& a, Cur& t) {
 }
 SLX_DEV void cur_init(const PrefillArgs& a, Cur& t) { t.j = 0; t.c = 0; cur_seek(a, t); }
 SLX_DEV void cur_next_item(const PrefillArgs& a, Cur& t) { t.c = 0; ++t.j; cur_seek(a, t); }
+// t.c counts the item's pipeline stages (kCPS chunks each)
 SLX_DEV void cur_next(const PrefillArgs& a, Cur& t) {
-  if (++t.c == a.nC) cur_next_item(a, t);
+  if (++t.c == a.nStg) cur_next_item(a, t);
 }
 
 SLX_DEV int npad16(int n) { return (n + 15) & ~15; }
@@ -354,9 +357,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int st = g % S;
         if (!mbar_wait(&bar_empty[st], ((g / S) & 1) ^ 1, a.status)) { fail(SLX_ERR_DEVICE_TIMEOUT); break; }
         const uint32_t bytes = (uint32_t)npad16(t.n) * kRowB;
-        const uint8_t* src = a.bimg + ((size_t)t.blk * a.nC + t.c) * kStageB;
-        mbar_arrive_expect_tx(&bar_tx[st], bytes);
-        bulk_g2s_plain(sB + (size_t)st * kStageB, src, bytes, &bar_tx[st]);
+        const int c0 = t.c * kCPS;
+        const int nch = a.nC - c0 < kCPS ? a.nC - c0 : kCPS;
+        const uint8_t* src = a.bimg + ((size_t)t.blk * a.nC + c0) * kStageB;
+        mbar_arrive_expect_tx(&bar_tx[st], bytes * nch);
+        for (int ci = 0; ci < nch; ++ci)
+          bulk_g2s_plain(sB + ((size_t)st * kCPS + ci) * kStageB,
+                         src + (size_t)ci * kStageB, bytes, &bar_tx[st]);
       }
       // drain: every issued copy has landed before the CTA exits
       const uint32_t issued = g;
@@ -377,7 +384,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d = tmem + kAccCol + buf * kNT;
         const uint32_t idesc = idesc_f16(npad16(t.n));
-        for (int c = 0; c < a.nC; ++c, ++g) {
+        for (int sg = 0; sg < a.nStg; ++sg, ++g) {
           const int st = g % S;
           const uint32_t ph = (g / S) & 1;
           if (!mbar_wait(&bar_tx[st], ph, a.status) ||
@@ -387,16 +394,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const int nk = c < a.nG ? 4 : bias_ksteps(a.nG, c - a.nG);
-          const uint32_t b0 = smem_u32(sB + (size_t)st * kStageB);
-          const uint32_t a0 = smem_u32(sA + (size_t)st * kStageA);
-          for (int s = 0; s < nk; ++s) {
-            const uint64_t bd = sdesc_sw128(b0 + 32 * s);
-            const uint32_t acc = (c | s) != 0;
-            if (ATMEM)
-              tc_mma_ts(d, tmem + st * 32 + 8 * s, bd, idesc, acc);
-            else
-              tc_mma_ss(d, sdesc_sw128(a0 + 32 * s), bd, idesc, acc);
+          const int c0 = sg * kCPS;
+          const int nch = a.nC - c0 < kCPS ? a.nC - c0 : kCPS;
+          for (int ci = 0; ci < nch; ++ci) {
+            const int c = c0 + ci;
+            const int nk = c < a.nG ? 4 : bias_ksteps(a.nG, c - a.nG);
+            const uint32_t b0 = smem_u32(sB + ((size_t)st * kCPS + ci) * kStageB);
+            const uint32_t a0 = smem_u32(sA + ((size_t)st * kCPS + ci) * kStageA);
+            for (int s = 0; s < nk; ++s) {
+              const uint64_t bd = sdesc_sw128(b0 + 32 * s);
+              const uint32_t acc = (c | s) != 0;
+              if (ATMEM)
+                tc_mma_ts(d, tmem + (st * kCPS + ci) * 32 + 8 * s, bd, idesc, acc);
+              else
+                tc_mma_ss(d, sdesc_sw128(a0 + 32 * s), bd, idesc, acc);
+            }
           }
           tc_commit(&bar_empty[st]);
         }
@@ -529,21 +541,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int grp = (warp - 6) >> 2;   // K half of every chunk: words 2grp, 2grp+1
     const int q = warp & 3;
     const int m = 32 * q + lane;       // A row = TMEM lane
-    uint8_t* my_stg = stg + (size_t)dq * kDqDepth * 16;
+    uint8_t* my_stg = stg + (size_t)dq * kDqDepth * kCPS * 16;
     Cur pf, cu;
     cur_init(a, pf);
     cur_init(a, cu);
     RowSrc rs;
     rs.j = -1;
+    // one task = one stage: the codes (8 bytes) and scale|bias word of each
+    // of its code chunks, into a 16-byte staging slot per chunk
     auto issue = [&](int slot) {
-      if (!pf.end && pf.c < a.nG) {
-        if (rs.j != pf.j) {
-          row_src<PHASE>(a, pf.slot, pf.mb, m, rs);
-          rs.j = pf.j;
+      if (!pf.end) {
+#pragma unroll
+        for (int ci = 0; ci < kCPS; ++ci) {
+          const int c = pf.c * kCPS + ci;
+          if (c < a.nG) {
+            if (rs.j != pf.j) {
+              row_src<PHASE>(a, pf.slot, pf.mb, m, rs);
+              rs.j = pf.j;
+            }
+            const uint32_t d = smem_u32(my_stg + (slot * kCPS + ci) * 16);
+            cp_async8(d, rs.row + ((c ^ rs.swz) << 4) + 8 * grp);
+            cp_async4(d + 8, rs.sb + c * rs.sbs);
+          }
         }
-        const uint32_t d = smem_u32(my_stg + slot * 16);
-        cp_async8(d, rs.row + ((pf.c ^ rs.swz) << 4) + 8 * grp);
-        cp_async4(d + 8, rs.sb + pf.c * rs.sbs);
       }
       cp_async_commit();
     };
@@ -556,58 +576,75 @@ __global__ void __launch_bounds__(kThreads, 1)
     while (!cu.end && !__any_sync(0xffffffffu, *abort_flag != 0)) {
       cp_async_wait<kDqDepth - 1>();
       const int slot = g % kDqDepth;
-      uint32_t w0 = 0, w1 = 0, sbw = 0;
-      if (cu.c < a.nG) {
-        const uint32_t* sp = reinterpret_cast<const uint32_t*>(my_stg + slot * 16);
-        w0 = sp[0];
-        w1 = sp[1];
-        sbw = sp[2];
+      const int c0 = cu.c * kCPS;
+      uint32_t w[kCPS][3];
+#pragma unroll
+      for (int ci = 0; ci < kCPS; ++ci) {
+        w[ci][0] = w[ci][1] = w[ci][2] = 0;
+        if (c0 + ci < a.nG) {
+          const uint32_t* sp =
+              reinterpret_cast<const uint32_t*>(my_stg + (slot * kCPS + ci) * 16);
+          w[ci][0] = sp[0];
+          w[ci][1] = sp[1];
+          w[ci][2] = sp[2];
+        }
       }
       issue(slot);
       cur_next(a, pf);
-      uint32_t out[16];
-      if (cu.c < a.nG) {
-        const __half s16 = __float2half_rn(bf16_lo(sbw));
-        const __half b16 = __float2half_rn(bf16_hi(sbw));
-        btab[cu.c * kDqThreads + dq] = b16;
-        const __half2 s2 = __half2half2(s16);
-        const __half2 n2 = __half2half2(__hneg(__hmul(s16, __float2half_rn(1024.f))));
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t r0 = ((w0 >> (2 * j)) & 0x00030003u) | 0x64006400u;
-          const uint32_t r1 = ((w1 >> (2 * j)) & 0x00030003u) | 0x64006400u;
-          const __half2 h0 = __hfma2(*reinterpret_cast<const __half2*>(&r0), s2, n2);
-          const __half2 h1 = __hfma2(*reinterpret_cast<const __half2*>(&r1), s2, n2);
-          out[j] = *reinterpret_cast<const uint32_t*>(&h0);
-          out[8 + j] = *reinterpret_cast<const uint32_t*>(&h1);
-        }
-      } else {
-        const int cb = cu.c - a.nG;
-#pragma unroll
-        for (int w = 0; w < 16; ++w) {
-          const int gi = 32 * cb + 16 * grp + w;
-          const uint32_t hb = gi < a.nG ? h_bits(btab[gi * kDqThreads + dq]) : 0u;
-          out[w] = hb | (hb << 16);
-        }
-      }
       const int st = g % S;
       if (!__all_sync(0xffffffffu,
                       mbar_wait(&bar_empty[st], ((g / S) & 1) ^ 1, a.status))) {
         fail(SLX_ERR_DEVICE_TIMEOUT);
         break;
       }
+#pragma unroll
+      for (int ci = 0; ci < kCPS; ++ci) {
+        const int c = c0 + ci;
+        if (c >= a.nC) break;
+        uint32_t out[16];
+        if (c < a.nG) {
+          const uint32_t sbw = w[ci][2];
+          const __half s16 = __float2half_rn(bf16_lo(sbw));
+          const __half b16 = __float2half_rn(bf16_hi(sbw));
+          btab[c * kDqThreads + dq] = b16;
+          const __half2 s2 = __half2half2(s16);
+          const __half2 n2 = __half2half2(__hneg(__hmul(s16, __float2half_rn(1024.f))));
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t r0 = ((w[ci][0] >> (2 * j)) & 0x00030003u) | 0x64006400u;
+            const uint32_t r1 = ((w[ci][1] >> (2 * j)) & 0x00030003u) | 0x64006400u;
+            const __half2 h0 = __hfma2(*reinterpret_cast<const __half2*>(&r0), s2, n2);
+            const __half2 h1 = __hfma2(*reinterpret_cast<const __half2*>(&r1), s2, n2);
+            out[j] = *reinterpret_cast<const uint32_t*>(&h0);
+            out[8 + j] = *reinterpret_cast<const uint32_t*>(&h1);
+          }
+        } else {
+          const int cb = c - a.nG;
+#pragma unroll
+          for (int k2 = 0; k2 < 16; ++k2) {
+            const int gi = 32 * cb + 16 * grp + k2;
+            const uint32_t hb = gi < a.nG ? h_bits(btab[gi * kDqThreads + dq]) : 0u;
+            out[k2] = hb | (hb << 16);
+          }
+        }
+        if (ATMEM) {
+          tc_st16(tmem + ((uint32_t)(32 * q) << 16) + (st * kCPS + ci) * 32 + 16 * grp,
+                  out);
+        } else {
+          uint8_t* rowp = sA + ((size_t)st * kCPS + ci) * kStageA + (m >> 3) * 1024 +
+                          (m & 7) * kRowB;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int pu = (4 * grp + u) ^ (m & 7);
+            *reinterpret_cast<uint4*>(rowp + pu * 16) =
+                make_uint4(out[4 * u], out[4 * u + 1], out[4 * u + 2], out[4 * u + 3]);
+          }
+        }
+      }
       if (ATMEM) {
-        tc_st16(tmem + ((uint32_t)(32 * q) << 16) + st * 32 + 16 * grp, out);
         tc_wait_st();
         tc_fence_before();
       } else {
-        uint8_t* rowp = sA + (size_t)st * kStageA + (m >> 3) * 1024 + (m & 7) * kRowB;
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int pu = (4 * grp + u) ^ (m & 7);
-          *reinterpret_cast<uint4*>(rowp + pu * 16) =
-              make_uint4(out[4 * u], out[4 * u + 1], out[4 * u + 2], out[4 * u + 3]);
-        }
         fence_proxy_async();
       }
       __syncwarp();
@@ -700,10 +737,10 @@ struct SmemPlan {
 SmemPlan plan_smem(int phase, bool atmem, int nG) {
   SmemPlan p = {};
   int o = 0;
-  p.off_b = o;   o += stages(atmem) * kStageB;
+  p.off_b = o;   o += stages(atmem) * kCPS * kStageB;
   p.off_hst = o; if (phase == 1) o += kStageB;
-  p.off_a = o;   if (!atmem) o += stages(atmem) * kStageA;
-  p.off_stg = o; o += kDqThreads * kDqDepth * 16;
+  p.off_a = o;   if (!atmem) o += stages(atmem) * kCPS * kStageA;
+  p.off_stg = o; o += kDqThreads * kDqDepth * kCPS * 16;
   p.off_btab = o; o += nG * kDqThreads * 2;
   o = (o + 15) & ~15;
   p.off_xch = o; if (phase == 1) o += 64 * kXchStride * 2;
@@ -789,6 +826,7 @@ int launch_prefill(const uint8_t* bank, long long slot_stride, int n_slots,
     PrefillArgs p = a;
     p.nG = nG1;
     p.nC = pf_chunks(nG1);
+    p.nStg = (p.nC + kCPS - 1) / kCPS;
     p.n_mb = I / 64;
     p.n_items = n_blocks * p.n_mb;
     p.bimg = ximg;
@@ -806,6 +844,7 @@ int launch_prefill(const uint8_t* bank, long long slot_stride, int n_slots,
     PrefillArgs p = a;
     p.nG = nG2;
     p.nC = pf_chunks(nG2);
+    p.nStg = (p.nC + kCPS - 1) / kCPS;
     p.n_mb = H / 128;
     p.n_items = n_blocks * p.n_mb;
     p.bimg = himg;

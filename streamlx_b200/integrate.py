@@ -124,6 +124,10 @@ class StreamingSwitchGLU:
         if decode:
             pool.prefetch_absorb(uniq)
         if len(uniq) <= pool.n_slots:
+            if decode and pool.hit_all(uniq):
+                if start_prefetch:
+                    self.start_prefetch(pred)
+                return "pool"
             if decode:
                 hits = [e for e in uniq if pool.resident(e)]
                 miss = [e for e in uniq if not pool.resident(e)]

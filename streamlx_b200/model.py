@@ -16,6 +16,8 @@ from __future__ import annotations
 import json
 import os
 
+import time
+
 import numpy as np
 import torch
 
@@ -162,6 +164,10 @@ class SynthDecoder:
         self._pending = None
         self._pf_done = 0
         self.glu_times: list | None = None
+        # host seconds per phase of the graph-launched step (launch, the
+        # previous step's deferred bookkeeping, waiting for the device log)
+        self.host_times = {"launch": 0.0, "bookkeeping": 0.0, "wait": 0.0,
+                           "steps": 0}
         # temporal-reuse routing override of the workloads: per (token,
         # layer) a seeded coin decides whether the previous token's expert
         # set is kept (applied identically to the CPU oracle)
@@ -606,9 +612,18 @@ class SynthDecoder:
         # this step's device work is queued before the host replays the
         # previous step: that replay's slot fills and table pushes run after
         # it on the stream, and this step is judged by its own log
+        ht = self.host_times
+        t0 = time.perf_counter()
         self._launch(0)
+        t1 = time.perf_counter()
         self.flush()
+        t2 = time.perf_counter()
         log = self._read_log()
+        t3 = time.perf_counter()
+        ht["launch"] += t1 - t0
+        ht["bookkeeping"] += t2 - t1
+        ht["wait"] += t3 - t2
+        ht["steps"] += 1
         self._glu_timing(0)
         lst = log[self._lst_off:self._lst_off + n]
         if self.pipeline and not (lst == self._UNMAPPED).any():

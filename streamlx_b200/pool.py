@@ -322,6 +322,26 @@ class StreamingSwitchMLP:
     def resident(self, e: int) -> bool:
         return e in self.id2slot
 
+    def hit_all(self, ids: list[int]) -> bool:
+        """``ensure(ids)`` when every id is resident -- the common decode
+        call -- without building the slot list: the same policy hits, in
+        order, and hit counts.  Returns False (and changes nothing) if any
+        id is missing."""
+        id2slot = self.id2slot
+        for e in ids:
+            if e not in id2slot:
+                return False
+        self._protect.update(ids)
+        if self.policy == "s3fifo":
+            for e in ids:
+                self._policy_hit(e)
+        else:
+            mte = id2slot.move_to_end
+            for e in ids:
+                mte(e)
+        self.hits += len(ids)
+        return True
+
     def touch(self, ids: list[int]) -> None:
         for e in ids:
             e = int(e)
