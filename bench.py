@@ -17,13 +17,23 @@ eight inside the timed region with CUDA events recorded as graph nodes
 (algorithmic bytes = routed experts + shared expert + activations per
 launch) against the measured HBM copy peak.
 ``cpu_baseline`` times the CPU oracle decoder on a bounded sample.
+``prefill`` (also ``--mode prefill`` on its own line) times the expert-major
+prefill of one 117B-shaped MoE layer (2048 tokens x top-10 of 256 2-bit
+experts) on the tensor cores, as TFLOP/s against the measured bf16 peak.
+``host_ms_per_step`` splits the decode step's host time into the graph
+launch, the previous step's deferred pool bookkeeping and the wait for the
+device log.
 
 ``--impl reference`` times the reference's path restated on the CPU (the
 oracle decoder; the reference's MLX backend is not installable here) on the
 same checkpoint and metric.
 
 Multi-GPU (torchrun): every rank decodes an independent replica (weak
-scaling; expert-parallel serving is a separate mode).
+scaling).  ``--mode ep`` (under torchrun) measures the expert-parallel MoE
+layer instead: experts sharded 256/N per GPU, token rows exchanged by NCCL
+all-to-all (batch-1 decode with the token replicated and one all-reduce;
+batch-64 decode and a 2048-token prefill with tokens split over ranks);
+``--check`` compares every rank's outputs with all experts run locally.
 """
 
 from __future__ import annotations
@@ -533,7 +543,8 @@ def run_ours(args) -> None:
     launches = L.LAUNCHES[0] - l0
     ht = dict(model.host_times)
     host_ms = {k_: round(1000 * v / max(ht["steps"], 1), 3)
-               for k_, v in ht.items() if k_ != "steps"}
+               for k_, v in ht.items() if k_ not in ("steps", "miss_steps")}
+    host_ms["steps_with_a_miss"] = ht["miss_steps"]
     timing, ops.TIMING = ops.TIMING, None
     glu_ms, model.glu_times = model.glu_times, None
     ms = e0.elapsed_time(e1)
@@ -622,6 +633,7 @@ def run_ours(args) -> None:
         "host_ms_per_step": host_ms,
         "clocks": clk,
         "pool": {"miss_rate": round(st["miss_rate"], 5),
+                 "fetch_s": st["fetch_s"],
                  "hits": st["hits"], "misses": st["misses"],
                  "prefetch_used": st["pf_used"]},
         "setup_s": {"load": round(t_load, 1), "prompt_and_warmup":

@@ -126,16 +126,42 @@ SLX_DEV void tc_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "r"(taddr));
 }
 SLX_DEV void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-SLX_DEV void tc_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+SLX_DEV void tc_st32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
       ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]),
         "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]),
-        "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+        "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]),
+        "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]),
+        "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
 }
 SLX_DEV void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Bounded mbarrier wait whose polls let the thread sleep in the hardware
+// (try_wait with a suspend-time hint of 0.2 ms) instead of spinning: the
+// waiting warps then leave their issue slots to the working ones.
+SLX_DEV bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, int32_t* status) {
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(200000u)
+        : "memory");
+    if (done) return true;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      set_status(status, SLX_ERR_DEVICE_TIMEOUT);
+      return false;
+    }
+  }
+}
 
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms of
 // 1024 bytes stacked along M/N (stride 1024), descriptor version 1.
@@ -155,8 +181,8 @@ SLX_DEV uint32_t idesc_f16(int n) {
 
 // ------------------------------------------------------- misc async ops --
 
-SLX_DEV void cp_async8(uint32_t dst, const void* src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+SLX_DEV void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
 SLX_DEV void cp_async4(uint32_t dst, const void* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
@@ -173,6 +199,9 @@ SLX_DEV void bulk_g2s_plain(void* dst, const void* src, uint32_t bytes, uint64_t
 SLX_DEV void bulk_s2g(void* dst, const void* src, uint32_t bytes) {
   asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
                ::"l"(dst), "r"(smem_u32(src)), "r"(bytes) : "memory");
+}
+SLX_DEV void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 SLX_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 SLX_DEV void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
@@ -350,12 +379,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ---------------------------------------------------- B producer ----
     if (lane == 0) {
-      Cur t;
+      Cur t, pb;  // pb runs one ring ahead: its chunks are prefetched to L2
       cur_init(a, t);
+      cur_init(a, pb);
+      for (int i = 0; i < S && !pb.end; ++i) cur_next(a, pb);
       uint32_t g = 0;
       for (; !t.end && !*abort_flag; cur_next(a, t), ++g) {
         const int st = g % S;
-        if (!mbar_wait(&bar_empty[st], ((g / S) & 1) ^ 1, a.status)) { fail(SLX_ERR_DEVICE_TIMEOUT); break; }
+        if (!pb.end) {
+          const int p0 = pb.c * kCPS;
+          const int pn = a.nC - p0 < kCPS ? a.nC - p0 : kCPS;
+          const uint8_t* ps = a.bimg + ((size_t)pb.blk * a.nC + p0) * kStageB;
+          for (int ci = 0; ci < pn; ++ci)
+            bulk_prefetch_l2(ps + (size_t)ci * kStageB, (uint32_t)npad16(pb.n) * kRowB);
+          cur_next(a, pb);
+        }
+        if (!mbar_wait_sleep(&bar_empty[st], ((g / S) & 1) ^ 1, a.status)) { fail(SLX_ERR_DEVICE_TIMEOUT); break; }
         const uint32_t bytes = (uint32_t)npad16(t.n) * kRowB;
         const int c0 = t.c * kCPS;
         const int nch = a.nC - c0 < kCPS ? a.nC - c0 : kCPS;
@@ -431,7 +470,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     while (!t.end) {
       const int buf = jl & 1;
       const bool ok = __all_sync(0xffffffffu,
-                                 mbar_wait(&bar_full[buf], (jl >> 1) & 1, a.status));
+                                 mbar_wait_sleep(&bar_full[buf], (jl >> 1) & 1, a.status));
       if (!ok) fail(SLX_ERR_DEVICE_TIMEOUT);
       bool stop = !ok || *abort_flag;
       stop = named_bar_or(1, 128, stop);
@@ -480,7 +519,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           float s = 0.f;
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
-            const uint4 w = row[u];
+            const uint4 w = row[(u + te) & 7];  // 8 threads: 8 distinct units
             const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
@@ -537,32 +576,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (PHASE == 1 && issuer) bulk_wait_all();
   } else {
     // -------------------------------------------------- dequantization ----
+    // Group grp (warps 6-9 / 10-13) dequantizes chunk grp of every stage:
+    // each thread one A row (TMEM lane), the row's whole 16-byte code unit.
     const int dq = threadIdx.x - 192;  // 0..255
-    const int grp = (warp - 6) >> 2;   // K half of every chunk: words 2grp, 2grp+1
+    const int grp = (warp - 6) >> 2;   // chunk of the stage this group owns
     const int q = warp & 3;
     const int m = 32 * q + lane;       // A row = TMEM lane
-    uint8_t* my_stg = stg + (size_t)dq * kDqDepth * kCPS * 16;
+    const int gt = dq & 127;           // thread within the group
+    // staging, thread-contiguous (conflict-free): codes [slot][group thread]
+    // 16 bytes, scale|bias words [slot][group thread] 4 bytes, per group
+    uint4* stg_codes = reinterpret_cast<uint4*>(stg) + grp * kDqDepth * 128;
+    uint32_t* stg_sb = reinterpret_cast<uint32_t*>(stg + 2 * kDqDepth * 128 * 16) +
+                       grp * kDqDepth * 128;
     Cur pf, cu;
     cur_init(a, pf);
     cur_init(a, cu);
     RowSrc rs;
     rs.j = -1;
-    // one task = one stage: the codes (8 bytes) and scale|bias word of each
-    // of its code chunks, into a 16-byte staging slot per chunk
     auto issue = [&](int slot) {
       if (!pf.end) {
-#pragma unroll
-        for (int ci = 0; ci < kCPS; ++ci) {
-          const int c = pf.c * kCPS + ci;
-          if (c < a.nG) {
-            if (rs.j != pf.j) {
-              row_src<PHASE>(a, pf.slot, pf.mb, m, rs);
-              rs.j = pf.j;
-            }
-            const uint32_t d = smem_u32(my_stg + (slot * kCPS + ci) * 16);
-            cp_async8(d, rs.row + ((c ^ rs.swz) << 4) + 8 * grp);
-            cp_async4(d + 8, rs.sb + c * rs.sbs);
+        const int c = pf.c * kCPS + grp;
+        if (c < a.nG) {
+          if (rs.j != pf.j) {
+            row_src<PHASE>(a, pf.slot, pf.mb, m, rs);
+            rs.j = pf.j;
           }
+          const int u = slot * 128 + gt;
+          cp_async16(smem_u32(stg_codes + u), rs.row + ((c ^ rs.swz) << 4));
+          cp_async4(smem_u32(stg_sb + u), rs.sb + c * rs.sbs);
         }
       }
       cp_async_commit();
@@ -576,76 +617,70 @@ __global__ void __launch_bounds__(kThreads, 1)
     while (!cu.end && !__any_sync(0xffffffffu, *abort_flag != 0)) {
       cp_async_wait<kDqDepth - 1>();
       const int slot = g % kDqDepth;
-      const int c0 = cu.c * kCPS;
-      uint32_t w[kCPS][3];
-#pragma unroll
-      for (int ci = 0; ci < kCPS; ++ci) {
-        w[ci][0] = w[ci][1] = w[ci][2] = 0;
-        if (c0 + ci < a.nG) {
-          const uint32_t* sp =
-              reinterpret_cast<const uint32_t*>(my_stg + (slot * kCPS + ci) * 16);
-          w[ci][0] = sp[0];
-          w[ci][1] = sp[1];
-          w[ci][2] = sp[2];
-        }
+      const int c = cu.c * kCPS + grp;
+      // bias table [g][row] of this item; two buffers by item parity (the
+      // other group may already be in the next item, at most a ring ahead)
+      __half* bt = btab + (cu.j & 1) * a.nG * 128;
+      uint4 cw = make_uint4(0, 0, 0, 0);
+      uint32_t sbw = 0;
+      if (c < a.nG) {
+        cw = stg_codes[slot * 128 + gt];
+        sbw = stg_sb[slot * 128 + gt];
       }
       issue(slot);
       cur_next(a, pf);
       const int st = g % S;
-      if (!__all_sync(0xffffffffu,
-                      mbar_wait(&bar_empty[st], ((g / S) & 1) ^ 1, a.status))) {
+      bool ok = mbar_wait_sleep(&bar_empty[st], ((g / S) & 1) ^ 1, a.status);
+      if (ok && c >= a.nG && c < a.nC && g > 0) {
+        // bias chunk: every code chunk of the item (both groups) has written
+        // its biases once the previous stage's arrivals are complete
+        ok = mbar_wait_sleep(&bar_dq[(g - 1) % S], ((g - 1) / S) & 1, a.status);
+      }
+      if (!__all_sync(0xffffffffu, ok)) {
         fail(SLX_ERR_DEVICE_TIMEOUT);
         break;
       }
-#pragma unroll
-      for (int ci = 0; ci < kCPS; ++ci) {
-        const int c = c0 + ci;
-        if (c >= a.nC) break;
-        uint32_t out[16];
+      if (c < a.nC) {
+        uint32_t out[32];
         if (c < a.nG) {
-          const uint32_t sbw = w[ci][2];
           const __half s16 = __float2half_rn(bf16_lo(sbw));
-          const __half b16 = __float2half_rn(bf16_hi(sbw));
-          btab[c * kDqThreads + dq] = b16;
+          bt[c * 128 + m] = __float2half_rn(bf16_hi(sbw));
           const __half2 s2 = __half2half2(s16);
           const __half2 n2 = __half2half2(__hneg(__hmul(s16, __float2half_rn(1024.f))));
+          const uint32_t wd[4] = {cw.x, cw.y, cw.z, cw.w};
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const uint32_t r0 = ((w[ci][0] >> (2 * j)) & 0x00030003u) | 0x64006400u;
-            const uint32_t r1 = ((w[ci][1] >> (2 * j)) & 0x00030003u) | 0x64006400u;
-            const __half2 h0 = __hfma2(*reinterpret_cast<const __half2*>(&r0), s2, n2);
-            const __half2 h1 = __hfma2(*reinterpret_cast<const __half2*>(&r1), s2, n2);
-            out[j] = *reinterpret_cast<const uint32_t*>(&h0);
-            out[8 + j] = *reinterpret_cast<const uint32_t*>(&h1);
+          for (int i = 0; i < 4; ++i) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const uint32_t r = ((wd[i] >> (2 * j)) & 0x00030003u) | 0x64006400u;
+              const __half2 h = __hfma2(*reinterpret_cast<const __half2*>(&r), s2, n2);
+              out[8 * i + j] = *reinterpret_cast<const uint32_t*>(&h);
+            }
           }
         } else {
           const int cb = c - a.nG;
 #pragma unroll
-          for (int k2 = 0; k2 < 16; ++k2) {
-            const int gi = 32 * cb + 16 * grp + k2;
-            const uint32_t hb = gi < a.nG ? h_bits(btab[gi * kDqThreads + dq]) : 0u;
+          for (int k2 = 0; k2 < 32; ++k2) {
+            const int gi = 32 * cb + k2;
+            const uint32_t hb = gi < a.nG ? h_bits(bt[gi * 128 + m]) : 0u;
             out[k2] = hb | (hb << 16);
           }
         }
         if (ATMEM) {
-          tc_st16(tmem + ((uint32_t)(32 * q) << 16) + (st * kCPS + ci) * 32 + 16 * grp,
-                  out);
+          tc_st32(tmem + ((uint32_t)(32 * q) << 16) + (st * kCPS + grp) * 32, out);
+          tc_wait_st();
+          tc_fence_before();
         } else {
-          uint8_t* rowp = sA + ((size_t)st * kCPS + ci) * kStageA + (m >> 3) * 1024 +
+          uint8_t* rowp = sA + ((size_t)st * kCPS + grp) * kStageA + (m >> 3) * 1024 +
                           (m & 7) * kRowB;
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int pu = (4 * grp + u) ^ (m & 7);
+          for (int u = 0; u < 8; ++u) {
+            const int pu = u ^ (m & 7);
             *reinterpret_cast<uint4*>(rowp + pu * 16) =
                 make_uint4(out[4 * u], out[4 * u + 1], out[4 * u + 2], out[4 * u + 3]);
           }
+          fence_proxy_async();
         }
-      }
-      if (ATMEM) {
-        tc_wait_st();
-        tc_fence_before();
-      } else {
-        fence_proxy_async();
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar_dq[st]);
@@ -740,8 +775,8 @@ SmemPlan plan_smem(int phase, bool atmem, int nG) {
   p.off_b = o;   o += stages(atmem) * kCPS * kStageB;
   p.off_hst = o; if (phase == 1) o += kStageB;
   p.off_a = o;   if (!atmem) o += stages(atmem) * kCPS * kStageA;
-  p.off_stg = o; o += kDqThreads * kDqDepth * kCPS * 16;
-  p.off_btab = o; o += nG * kDqThreads * 2;
+  p.off_stg = o; o += 2 * kDqDepth * 128 * (16 + 4);
+  p.off_btab = o; o += 2 * nG * 128 * 2;
   o = (o + 15) & ~15;
   p.off_xch = o; if (phase == 1) o += 64 * kXchStride * 2;
   o = (o + 15) & ~15;

@@ -167,7 +167,9 @@ class SynthDecoder:
         # host seconds per phase of the graph-launched step (launch, the
         # previous step's deferred bookkeeping, waiting for the device log)
         self.host_times = {"launch": 0.0, "bookkeeping": 0.0, "wait": 0.0,
-                           "steps": 0}
+                           "miss_path": 0.0, "miss_replay": 0.0,
+                           "miss_relaunch": 0.0, "miss_wait": 0.0,
+                           "tail": 0.0, "steps": 0, "miss_steps": 0}
         # temporal-reuse routing override of the workloads: per (token,
         # layer) a seeded coin decides whether the previous token's expert
         # set is kept (applied identically to the CPU oracle)
@@ -626,6 +628,7 @@ class SynthDecoder:
         ht["steps"] += 1
         self._glu_timing(0)
         lst = log[self._lst_off:self._lst_off + n]
+        t4 = time.perf_counter()
         if self.pipeline and not (lst == self._UNMAPPED).any():
             # bookkeeping (and the prefetch reads it starts) waits for the
             # next call, where it overlaps that step's device work
@@ -635,21 +638,31 @@ class SynthDecoder:
             self._prefetch_upto(log)
             start = 0
             while True:
+                r0 = time.perf_counter()
                 redo = self._replay(log, start)
+                r1 = time.perf_counter()
+                ht["miss_replay"] += r1 - r0
                 if redo is None:
                     break
                 self._launch(redo)
+                r2 = time.perf_counter()
                 log = self._read_log()
+                ht["miss_relaunch"] += r2 - r1
+                ht["miss_wait"] += time.perf_counter() - r2
                 self._glu_timing(redo)
                 self._prefetch_upto(log)
                 if int(log[self._lst_off + redo]) != 0:
                     raise RuntimeError(f"layer {redo} still unmapped after "
                                        "its slots were filled")
                 start = redo + 1
+            ht["miss_path"] += time.perf_counter() - t4
+            ht["miss_steps"] += 1
+        t5 = time.perf_counter()
         self.g_prev_ids.copy_(self.g_ids)
         self.n_pos += 1
         nxt = torch.empty(1, dtype=torch.int32, device=self.device)
         nxt.copy_(self.g_tok_out)
+        ht["tail"] += time.perf_counter() - t5
         return nxt
 
     @torch.no_grad()
