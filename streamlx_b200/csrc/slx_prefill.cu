@@ -60,18 +60,32 @@ namespace slx {
 namespace {
 
 constexpr int kNT = 128;            // max pairs per block (MMA N)
+// Tuning (compile-time; the defaults are the shipped configuration).
+#ifndef SLX_PF_STAGES
+#define SLX_PF_STAGES 4       // stages with the operand in TMEM (2 or 4)
+#endif
+#ifndef SLX_PF_L2_PREFETCH
+#define SLX_PF_L2_PREFETCH 1  // prefetch B chunks one ring ahead into L2
+#endif
+#ifndef SLX_PF_SLEEP_WAIT
+#define SLX_PF_SLEEP_WAIT 1   // barrier polls with a suspend-time hint
+#endif
+#ifndef SLX_PF_DQ_DEPTH
+#define SLX_PF_DQ_DEPTH 4     // code prefetch depth in stages (2..4)
+#endif
+
 constexpr int kCPS = 2;             // 64-column chunks per pipeline stage
 constexpr int kS = 4;               // max pipeline stages
 // stages: 4 with the weight operand in TMEM (A ring 4 x 64 columns + two
 // 128-column accumulators = 512), 2 with it in shared memory (the A ring
 // then takes 2 x 32 KB of shared memory); 8 resp. 4 chunks in flight
-constexpr int stages(bool atmem) { return atmem ? 4 : 2; }
+constexpr int stages(bool atmem) { return atmem ? SLX_PF_STAGES : 2; }
 constexpr int kRowB = 128;          // bytes of one 64-column fp16 chunk row
 constexpr int kStageB = kNT * kRowB;     // B chunk (16 KB)
 constexpr int kStageA = 128 * kRowB;     // A chunk, shared-memory variant
 constexpr int kThreads = 448;
 constexpr int kDqThreads = 256;
-constexpr int kDqDepth = 4;         // cp.async tasks (stages) in flight per thread
+constexpr int kDqDepth = SLX_PF_DQ_DEPTH;  // cp.async tasks (stages) in flight per thread
 constexpr int kAccCol = 32 * kCPS * kS;  // TMEM: A ring at 0..255, accumulators after
 constexpr int kTmemCols = 512;
 constexpr int kXchStride = kNT + 2; // bf16 per row of the up-value exchange
@@ -145,6 +159,7 @@ SLX_DEV void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "m
 // (try_wait with a suspend-time hint of 0.2 ms) instead of spinning: the
 // waiting warps then leave their issue slots to the working ones.
 SLX_DEV bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, int32_t* status) {
+  if (!SLX_PF_SLEEP_WAIT) return mbar_wait(bar, parity, status);
   const uint64_t t0 = globaltimer_ns();
   for (;;) {
     uint32_t done;
@@ -386,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t g = 0;
       for (; !t.end && !*abort_flag; cur_next(a, t), ++g) {
         const int st = g % S;
-        if (!pb.end) {
+        if (SLX_PF_L2_PREFETCH && !pb.end) {
           const int p0 = pb.c * kCPS;
           const int pn = a.nC - p0 < kCPS ? a.nC - p0 : kCPS;
           const uint8_t* ps = a.bimg + ((size_t)pb.blk * a.nC + p0) * kStageB;

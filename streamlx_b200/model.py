@@ -498,23 +498,35 @@ class SynthDecoder:
             self._join_side()
             self._record_tail()
         self._kernels_full = L.LAUNCHES[0] - c0
+        # suffix graphs: layers i..n-1 and the tail as one launch, for the
+        # re-run after a slot fill (one graph launch instead of n - i + 1)
+        self._suffix = [None] * n
+        self._kernels_suffix = [0] * n
+        for i in range(1, n):
+            g = torch.cuda.CUDAGraph()
+            c0 = L.LAUNCHES[0]
+            with torch.cuda.graph(g, stream=s, capture_error_mode=mode):
+                self.g_lstatus[i:].zero_()
+                for j in range(i, n):
+                    self._record_layer(j, join=False)
+                self._join_side()
+                self._record_tail()
+            self._kernels_suffix[i] = L.LAUNCHES[0] - c0
+            self._suffix[i] = g
         return graphs, tail, full
 
     def _graph_kernels(self, start: int) -> int:
         """Library kernels one launch from layer `start` runs."""
         if start == 0:
             return self._kernels_full
-        return sum(self._kernels_layer[start:]) + self._kernels_tail
+        return self._kernels_suffix[start]
 
     def _launch(self, start: int) -> None:
         graphs, tail, full = self._graphs
         if start == 0:
             full.replay()
         else:
-            self.g_lstatus[start:].zero_()
-            for i in range(start, self.cfg.layers):
-                graphs[i].replay()
-            tail.replay()
+            self._suffix[start].replay()
         L._count(self._graph_kernels(start))
 
     def _read_log(self) -> np.ndarray:
@@ -584,13 +596,15 @@ class SynthDecoder:
 
     def flush(self) -> None:
         """Finish the deferred bookkeeping of the last step, if any: start
-        its next-layer prefetches, then replay its pool calls."""
+        its next-layer prefetches not yet started, then replay its pool
+        calls from the first layer not yet replayed."""
         pend, self._pending = self._pending, None
         if pend is None:
             return
-        self._pf_done = 0
-        self._prefetch_upto(pend)
-        if self._replay(pend, 0) is not None:
+        log, start, pf_done = pend
+        self._pf_done = pf_done
+        self._prefetch_upto(log)
+        if self._replay(log, start) is not None:
             raise RuntimeError("deferred step had an unmapped expert")
 
     def _step_graph(self, token: torch.Tensor) -> torch.Tensor:
@@ -632,7 +646,7 @@ class SynthDecoder:
         if self.pipeline and not (lst == self._UNMAPPED).any():
             # bookkeeping (and the prefetch reads it starts) waits for the
             # next call, where it overlaps that step's device work
-            self._pending = log
+            self._pending = (log, 0, 0)
         else:
             self._pf_done = 0
             self._prefetch_upto(log)
@@ -655,6 +669,13 @@ class SynthDecoder:
                     raise RuntimeError(f"layer {redo} still unmapped after "
                                        "its slots were filled")
                 start = redo + 1
+                rest = log[self._lst_off + start:self._lst_off + n]
+                if self.pipeline and not (rest == self._UNMAPPED).any():
+                    # the layers after the refilled one all ran on resident
+                    # experts: their bookkeeping waits for the next call,
+                    # like a miss-free step's
+                    self._pending = (log, start, self._pf_done)
+                    break
             ht["miss_path"] += time.perf_counter() - t4
             ht["miss_steps"] += 1
         t5 = time.perf_counter()
