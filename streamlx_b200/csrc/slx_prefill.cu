@@ -56,6 +56,25 @@
 #include "slx_kernels.cuh"
 #include "slx_tiles.cuh"
 
+// Diagnostics build only (-DSLX_PF_TRACE): %globaltimer stamps of each
+// warp role at pipeline stages 8..15 of phase 1, per CTA.
+#ifdef SLX_PF_TRACE
+static __device__ unsigned long long g_pf_trace[148][8][8];
+extern "C" int slx_pf_trace_read(unsigned long long* host) {
+  return cudaMemcpyFromSymbol(host, g_pf_trace, sizeof(g_pf_trace)) ==
+                 cudaSuccess ? 0 : -1;
+}
+#define PF_STAMP(G, E)                                                     \
+  do {                                                                     \
+    if (PHASE == 1 && blockIdx.x < 148 && (G) >= 8 && (G) < 16)            \
+      g_pf_trace[blockIdx.x][(G) - 8][E] = slx::globaltimer_ns();          \
+  } while (0)
+#else
+#define PF_STAMP(G, E) \
+  do {                 \
+  } while (0)
+#endif
+
 namespace slx {
 namespace {
 
@@ -410,6 +429,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           cur_next(a, pb);
         }
         if (!mbar_wait_sleep(&bar_empty[st], ((g / S) & 1) ^ 1, a.status)) { fail(SLX_ERR_DEVICE_TIMEOUT); break; }
+        PF_STAMP(g, 0);
         const uint32_t bytes = (uint32_t)npad16(t.n) * kRowB;
         const int c0 = t.c * kCPS;
         const int nch = a.nC - c0 < kCPS ? a.nC - c0 : kCPS;
@@ -418,6 +438,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int ci = 0; ci < nch; ++ci)
           bulk_g2s_plain(sB + ((size_t)st * kCPS + ci) * kStageB,
                          src + (size_t)ci * kStageB, bytes, &bar_tx[st]);
+        PF_STAMP(g, 1);
       }
       // drain: every issued copy has landed before the CTA exits
       const uint32_t issued = g;
@@ -441,8 +462,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int sg = 0; sg < a.nStg; ++sg, ++g) {
           const int st = g % S;
           const uint32_t ph = (g / S) & 1;
-          if (!mbar_wait(&bar_tx[st], ph, a.status) ||
-              !mbar_wait(&bar_dq[st], ph, a.status)) {
+          bool okw = mbar_wait(&bar_tx[st], ph, a.status);
+          PF_STAMP(g, 2);
+          okw = okw && mbar_wait(&bar_dq[st], ph, a.status);
+          PF_STAMP(g, 3);
+          if (!okw) {
             fail(SLX_ERR_DEVICE_TIMEOUT);
             ok = false;
             break;
@@ -465,6 +489,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           tc_commit(&bar_empty[st]);
+          PF_STAMP(g, 4);
         }
         if (!ok) break;
         tc_commit(&bar_full[buf]);
@@ -631,6 +656,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t g = 0;
     while (!cu.end && !__any_sync(0xffffffffu, *abort_flag != 0)) {
       cp_async_wait<kDqDepth - 1>();
+      if (warp == 6 && lane == 0) PF_STAMP(g, 5);
       const int slot = g % kDqDepth;
       const int c = cu.c * kCPS + grp;
       // bias table [g][row] of this item; two buffers by item parity (the
@@ -646,6 +672,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       cur_next(a, pf);
       const int st = g % S;
       bool ok = mbar_wait_sleep(&bar_empty[st], ((g / S) & 1) ^ 1, a.status);
+      if (warp == 6 && lane == 0) PF_STAMP(g, 6);
       if (ok && c >= a.nG && c < a.nC && g > 0) {
         // bias chunk: every code chunk of the item (both groups) has written
         // its biases once the previous stage's arrivals are complete
@@ -698,6 +725,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       __syncwarp();
+      if (warp == 6 && lane == 0) PF_STAMP(g, 7);
       if (lane == 0) mbar_arrive(&bar_dq[st]);
       cur_next(a, cu);
       ++g;
