@@ -625,6 +625,10 @@ def run_ours(args) -> None:
                      "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                      "frac": round(achieved / peak, 4),
                      "traffic": traffic,
+                     "traffic_source": "ncu DRAM bytes of the two-launch "
+                                       "form of the same SwitchGLU (same "
+                                       "tiles read); the fused launch was "
+                                       "not captured at steady state",
                      "algorithmic_bytes_per_launch": per_launch,
                      "launches_timed": len(durs),
                      "sampling": "layers 3, 11, 19, 27, 35 of every step",
