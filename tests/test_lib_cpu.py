@@ -41,3 +41,30 @@ def test_host_side_errors_without_gpu():
                            None, 0, None, None, 0, None, None)
     assert rc == -2 or rc == -1
     assert lib.slx_last_error_string() != b""
+
+
+def test_prefill_host_helpers_need_no_gpu():
+    """Block splitting of expert-grouped pairs and the prefill entry's
+    host-side checks (streamlx/integrate.py:141-232 groups the sweep's pairs
+    by expert; the library takes them as blocks of at most PREFILL_BLOCK)."""
+    import numpy as np
+
+    from streamlx_b200 import ops
+    nb = ops.PREFILL_BLOCK
+    blocks = ops.prefill_blocks([5, 2, 9], [3, 2 * nb + 1, 0])
+    assert blocks.tolist() == [[5, 0, 3, 0], [2, 3, nb, 0],
+                               [2, 3 + nb, nb, 0], [2, 3 + 2 * nb, 1, 0]]
+    assert ops.prefill_blocks([], []).shape == (0, 4)
+    assert ops.prefill_supported(2560, 1024, 2)
+    assert not ops.prefill_supported(2560, 1024, 4)
+    assert not ops.prefill_supported(2048, 768, 2)
+    # scratch: both phases' operand images, 16 KB per chunk of a block
+    n = L.prefill_scratch_bytes(10, 2560, 1024, 2)
+    assert n == 10 * ((40 + 2) + (16 + 1)) * 128 * 128
+    assert L.prefill_scratch_bytes(10, 2560, 1024, 4) == 0
+    lib = L.lib()
+    bank = L.slx_expert_bank(None, 0, 1, 2560, 1024, 4)
+    rc = lib.slx_prefill_grouped(ctypes.byref(bank), None, 0, None, 0, None,
+                                 1, None, None, 0, None, 0, None, None)
+    assert rc == -2 and b"2-bit" in lib.slx_last_error_string()
+    assert np.dtype(np.int32) == blocks.dtype
