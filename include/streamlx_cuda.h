@@ -168,12 +168,6 @@ int slx_prefill_grouped(const slx_expert_bank* bank, const void* x,
                         void* scratch, size_t scratch_bytes, int32_t* status,
                         void* stream);
 
-/* Where slx_prefill_grouped's dequantised weight operand lives for the
- * calling thread: 1 = tensor memory (default; tcgen05.st, no shared-memory
- * round trip), 0 = a swizzled shared-memory ring.  Same results; returns the
- * previous setting. */
-int slx_set_prefill_a_tmem(int on);
-
 /* Dense quantized linear y[T, out] = x[T, in] @ dequant(W)^T (bf16 out,
  * fp32 accumulate) over a tile-format matrix (slx_pack_dense).  Trunk
  * projections of the decoder around the expert path (no reference

@@ -37,7 +37,6 @@ EXPORTS = (
     "slx_router_topk_multi", "slx_set_pdl", "slx_pread_many",
     "slx_set_switchglu_fused", "slx_switchglu_last_kernels",
     "slx_prefill_scratch_bytes", "slx_prefill_grouped",
-    "slx_set_prefill_a_tmem",
 )
 
 
@@ -161,8 +160,6 @@ def lib() -> C.CDLL:
         L.slx_prefill_grouped.argtypes = [C.POINTER(slx_expert_bank), vp, i32,
                                           vp, i32, vp, i32, vp, vp, i32, vp,
                                           sz, vp, vp]
-        L.slx_set_prefill_a_tmem.restype = i32
-        L.slx_set_prefill_a_tmem.argtypes = [i32]
         _lib = L
     return _lib
 
@@ -434,11 +431,6 @@ def copy_many(dsts: list[int], srcs: list[int], sizes: list[int],
 def prefill_scratch_bytes(n_blocks: int, hidden: int, inter: int,
                           bits: int) -> int:
     return int(lib().slx_prefill_scratch_bytes(n_blocks, hidden, inter, bits))
-
-
-def set_prefill_a_tmem(on: bool) -> bool:
-    """Prefill weight operand in tensor memory (default) or shared memory."""
-    return bool(lib().slx_set_prefill_a_tmem(1 if on else 0))
 
 
 def prefill_grouped(bank: slx_expert_bank, x: torch.Tensor,

@@ -17,7 +17,6 @@ thread_local std::string g_err;
 thread_local int g_pdl = 0;
 thread_local int g_fused = 1;
 thread_local int g_glu_kernels = 0;  // kernels the last slx_switchglu launched
-thread_local int g_pf_a_tmem = 1;    // prefill: A operand in TMEM (else smem)
 
 int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -268,12 +267,6 @@ size_t slx_prefill_scratch_bytes(int n_blocks, int hidden, int inter,
   return slx::prefill_scratch_bytes(n_blocks, hidden, inter);
 }
 
-int slx_set_prefill_a_tmem(int on) {
-  const int prev = g_pf_a_tmem;
-  g_pf_a_tmem = on ? 1 : 0;
-  return prev;
-}
-
 int slx_prefill_grouped(const slx_expert_bank* bank, const void* x,
                         int n_rows, const int32_t* pair_row, int n_pairs,
                         const int32_t* blocks, int n_blocks,
@@ -309,7 +302,7 @@ int slx_prefill_grouped(const slx_expert_bank* bank, const void* x,
       bank->n_slots, H, I, reinterpret_cast<const uint16_t*>(x), n_rows,
       pair_row, n_pairs, reinterpret_cast<const int4*>(blocks), n_blocks,
       out_row, reinterpret_cast<uint16_t*>(out), n_out,
-      reinterpret_cast<uint8_t*>(scratch), status, g_pf_a_tmem,
+      reinterpret_cast<uint8_t*>(scratch), status,
       reinterpret_cast<cudaStream_t>(stream));
   return rc ? cuda_check(rc, "slx_prefill_grouped") : SLX_OK;
 }

@@ -118,7 +118,7 @@ int launch_prefill(const uint8_t* bank, long long slot_stride, int n_slots,
                    int H, int I, const uint16_t* x, int n_rows,
                    const int32_t* pair_row, int n_pairs, const int4* blocks,
                    int n_blocks, const int32_t* out_row, uint16_t* out,
-                   int n_out, uint8_t* scratch, int32_t* status, int a_tmem,
+                   int n_out, uint8_t* scratch, int32_t* status,
                    cudaStream_t s);
 
 }  // namespace slx

@@ -7,17 +7,19 @@
 // gather_qmm down) over the pairs of each 16-expert batch.  Here one launch
 // pair covers every pair of the chunk whose expert has a slot:
 //
-//   k_pf_pack_x   gathers each pair's token row into the B-operand image of
-//                 phase 1 (fp16, 128-byte swizzled K-major rows, one
-//                 64-column chunk per quantization group) plus per-group sums;
-//   k_prefill<1>  D[128 x N] = [gate rows r..r+63 ; up rows r..r+63] x X^T
-//                 over K = hidden, then SwiGLU in the epilogue, written as
-//                 phase 2's B image (chunk r/64) + its group sums;
-//   k_prefill<2>  D[128 x N] = down rows h..h+127 x Hact^T over K = inter,
-//                 rounded to bf16 and stored per pair.
+//   k_pf_pack_x   gathers each pair's token row into phase 1's activation
+//                 image (fp16, 128-byte swizzled K-major rows, one 64-column
+//                 chunk per quantization group) plus per-group sums;
+//   k_prefill<1>  D[128 pairs x 256] = X x [gate rows r..r+127 ; up rows
+//                 r..r+127]^T over K = hidden; SwiGLU in the epilogue (a
+//                 thread = one pair holds both its gate and up values),
+//                 written as phase 2's activation image + group sums;
+//   k_prefill<2>  D[128 pairs x 256] = Hact x [down rows h..h+255]^T over
+//                 K = inter, rounded to bf16 and stored per pair.
 //
-// Swap-AB: weight rows fill the M = 128 side of the MMA, the pairs of one
-// expert (up to 128, padded to a multiple of 16) are N.
+// The pairs of one expert (up to 128, a block) are the MMA's M side and 256
+// weight rows its N side: a tcgen05.mma costs about the same whether N is
+// 64 or 256 here, so the widest N halves the instructions per layer.
 //
 // Exact affine arithmetic on fp16 tensor cores.  MLX affine 2-bit weights
 // are w = s*q + b per group of 64 (s, b bf16, q in 0..3).  s*q has at most
@@ -25,31 +27,34 @@
 // 2^-17 <= |s| and 3|s| <= 65504; the dequant warps produce it with one fp16
 // FMA on the magic-number expansion (1024 + q) * s - 1024 * s.  The bias
 // term b * sum(x over the group) rides on extra K columns: per group two
-// columns, A = (b, b), B = (hi, lo) with hi + lo = fp32 group sum (hi/lo
-// fp16).  The activations enter as fp16 (bf16 values are exact in fp16 for
+// columns, weights (b, b), activations (hi, lo) with hi + lo = the fp32
+// group sum.  Activations enter as fp16 (bf16 values are exact in fp16 for
 // 2^-14 <= |x| < 65504; below that the rounding error is < 2^-25).  So each
-// output is sum_i s*q_i*x_i + b*sum x accumulated in fp32 -- the same value
-// MLX's quantized matrix-vector product forms (scale * dot(q, x) + bias *
-// sum(x)) -- and the rounding points are those of switch_forward: gate / up
-// outputs to bf16, silu(gate)*up to bf16, down output to bf16.
+// output is sum_i s*q_i*x_i + b*sum x accumulated in fp32 -- the value MLX's
+// quantized matrix-vector product forms (scale * dot(q, x) + bias * sum(x))
+// -- and the rounding points are those of switch_forward: gate / up to bf16,
+// silu(gate)*up to bf16, down output to bf16.
 //
 // Inside each 16-code word the K order is permuted so a code pair
-// (q[j], q[j+8]) -- one AND of the packed word -- fills one 32-bit A column;
-// the B images use the same order (position 16i + 2j + t <- element
-// 16i + j + 8t).
+// (q[j], q[j+8]) -- one AND of the packed word -- fills one 32-bit column;
+// the activation images use the same order (position 16i + 2j + t <-
+// element 16i + j + 8t).
 //
 // Warp roles (448 threads, one CTA per SM, persistent over work items):
-//   warp 0      TMEM allocation; lane 0 streams B chunks (cp.async.bulk,
-//               the TMA engine) into a 4-stage ring of two-chunk stages;
-//   warp 1      lane 0 issues the MMAs (M128 x N x K16, kind::f16) and
-//               commits them to the stage / accumulator barriers;
-//   warps 2-5   epilogue: tcgen05.ld of the accumulator (two TMEM buffers so
-//               the next item's MMAs overlap it);
-//   warps 6-13  dequantization: each thread owns one A row (TMEM lane),
-//               prefetches its packed codes with cp.async eight chunks ahead,
-//               and writes fp16 A columns straight into TMEM (tcgen05.st;
-//               the MMA reads A from TMEM) or, in the shared-memory
-//               variant, into a swizzled A ring.
+//   warp 0      TMEM allocation; lane 0 streams activation chunks
+//               (cp.async.bulk, the TMA engine) into a 6-stage ring, with
+//               an L2 prefetch of the chunks one ring ahead (a copy takes
+//               ~3 us to land);
+//   warp 1      lane 0 issues the MMAs (M128 x N256 x K16, kind::f16, both
+//               operands in shared memory) and commits them to the ring /
+//               accumulator barriers;
+//   warps 2-5   epilogue: each thread one pair (TMEM lane), tcgen05.ld of
+//               its 256 accumulator columns (two TMEM buffers, so the next
+//               item's MMAs overlap it);
+//   warps 6-13  dequantization: each thread one weight row; its 16-byte
+//               code unit and scale|bias word prefetched with cp.async four
+//               chunks ahead; fp16 weights written into a 2-stage ring of
+//               swizzled K-major chunks.
 // Every wait is bounded (2 s); on expiry the kernel records
 // SLX_ERR_DEVICE_TIMEOUT, drains its in-flight copies and MMAs, frees TMEM
 // and returns.
@@ -78,36 +83,25 @@ extern "C" int slx_pf_trace_read(unsigned long long* host) {
 namespace slx {
 namespace {
 
-constexpr int kNT = 128;            // max pairs per block (MMA N)
+constexpr int kNT = 128;            // max pairs per block (MMA M)
+constexpr int kNW = 256;            // weight rows per item (MMA N)
+constexpr int kRowB = 128;          // bytes of one 64-column fp16 chunk row
+constexpr int kActB = kNT * kRowB;  // activation chunk (16 KB)
+constexpr int kWB = kNW * kRowB;    // weight chunk (32 KB)
+constexpr int kSX = 6;              // activation ring stages (one chunk each)
+constexpr int kSW = 2;              // weight ring stages (one chunk each)
+constexpr int kThreads = 448;
+constexpr int kDqThreads = 256;     // one weight row each
+constexpr int kDqDepth = 4;         // cp.async chunks in flight per thread
+constexpr int kTmemCols = 512;      // two 256-column accumulators
+
 // Tuning (compile-time; the defaults are the shipped configuration).
-#ifndef SLX_PF_STAGES
-#define SLX_PF_STAGES 4       // stages with the operand in TMEM (2 or 4)
-#endif
 #ifndef SLX_PF_L2_PREFETCH
-#define SLX_PF_L2_PREFETCH 1  // prefetch B chunks one ring ahead into L2
+#define SLX_PF_L2_PREFETCH 1  // prefetch activation chunks one ring ahead into L2
 #endif
 #ifndef SLX_PF_SLEEP_WAIT
 #define SLX_PF_SLEEP_WAIT 1   // barrier polls with a suspend-time hint
 #endif
-#ifndef SLX_PF_DQ_DEPTH
-#define SLX_PF_DQ_DEPTH 4     // code prefetch depth in stages (2..4)
-#endif
-
-constexpr int kCPS = 2;             // 64-column chunks per pipeline stage
-constexpr int kS = 4;               // max pipeline stages
-// stages: 4 with the weight operand in TMEM (A ring 4 x 64 columns + two
-// 128-column accumulators = 512), 2 with it in shared memory (the A ring
-// then takes 2 x 32 KB of shared memory); 8 resp. 4 chunks in flight
-constexpr int stages(bool atmem) { return atmem ? SLX_PF_STAGES : 2; }
-constexpr int kRowB = 128;          // bytes of one 64-column fp16 chunk row
-constexpr int kStageB = kNT * kRowB;     // B chunk (16 KB)
-constexpr int kStageA = 128 * kRowB;     // A chunk, shared-memory variant
-constexpr int kThreads = 448;
-constexpr int kDqThreads = 256;
-constexpr int kDqDepth = SLX_PF_DQ_DEPTH;  // cp.async tasks (stages) in flight per thread
-constexpr int kAccCol = 32 * kCPS * kS;  // TMEM: A ring at 0..255, accumulators after
-constexpr int kTmemCols = 512;
-constexpr int kXchStride = kNT + 2; // bf16 per row of the up-value exchange
 
 // --------------------------------------------------------------- tcgen05 --
 
@@ -141,13 +135,6 @@ SLX_DEV void tc_mma_ss(uint32_t d, uint64_t adesc, uint64_t bdesc,
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
       ::"r"(d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc) : "memory");
 }
-SLX_DEV void tc_mma_ts(uint32_t d, uint32_t a_tmem, uint64_t bdesc,
-                       uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
-      ::"r"(d), "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(acc) : "memory");
-}
 SLX_DEV void tc_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
@@ -159,21 +146,6 @@ SLX_DEV void tc_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "r"(taddr));
 }
 SLX_DEV void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-SLX_DEV void tc_st32(uint32_t taddr, const uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
-      ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]),
-        "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]),
-        "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
-        "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]),
-        "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]),
-        "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
-      : "memory");
-}
-SLX_DEV void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-
 // Bounded mbarrier wait whose polls let the thread sleep in the hardware
 // (try_wait with a suspend-time hint of 0.2 ms) instead of spinning: the
 // waiting warps then leave their issue slots to the working ones.
@@ -230,32 +202,9 @@ SLX_DEV void bulk_g2s_plain(void* dst, const void* src, uint32_t bytes, uint64_t
       "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
       ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
-SLX_DEV void bulk_s2g(void* dst, const void* src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
-               ::"l"(dst), "r"(smem_u32(src)), "r"(bytes) : "memory");
-}
 SLX_DEV void bulk_prefetch_l2(const void* src, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
-SLX_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-SLX_DEV void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
-SLX_DEV void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-SLX_DEV void named_bar(int id, int n) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
-}
-// Named barrier that also ORs a predicate over its n threads: every thread
-// gets the same answer, so a decision to stop is taken by all alike.
-SLX_DEV bool named_bar_or(int id, int n, bool p) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred pi, po;\n\tsetp.ne.u32 pi, %1, 0;\n\t"
-      "bar.red.or.pred po, %2, %3, pi;\n\tselp.u32 %0, 1, 0, po;\n\t}"
-      : "=r"(r) : "r"((uint32_t)p), "r"(id), "r"(n) : "memory");
-  return r != 0;
-}
-
-// Position of element r (0..63) of a group inside the permuted K order.
-SLX_HOST_DEV int kpos(int r) { return (r & ~15) + 2 * (r & 7) + ((r >> 3) & 1); }
 // Byte offset of fp16 position pos of row n inside a 128-byte-swizzled chunk.
 SLX_DEV int sw_off(int n, int pos) {
   return n * kRowB + ((((pos >> 3) ^ (n & 7))) << 4) + ((pos & 7) << 1);
@@ -270,16 +219,15 @@ struct PrefillArgs {
   int n_slots, H, I;
   const int4* blocks;  // {slot, first pair, pairs, 0}
   int n_blocks, n_pairs, n_items, n_mb;
-  int nG, nC, nStg;    // this phase: groups along K, chunks incl. bias
-                       // chunks, pipeline stages per item
-  const uint8_t* bimg; // this phase's B image [n_blocks][nC][kNT][128]
-  uint8_t* himg;       // phase 1 output: phase 2's B image
+  int nG, nC;          // this phase: groups along K, chunks incl. bias chunks
+  const uint8_t* ximg; // this phase's activation image [n_blocks][nC][kNT][128]
+  uint8_t* himg;       // phase 1 output: phase 2's activation image
   int nG2, nC2;
   uint16_t* out;       // phase 2: [n_out, H] bf16
   const int32_t* out_row;
   int n_out;
   int32_t* status;
-  int off_b, off_a, off_stg, off_btab, off_xch, off_hst, off_orow;  // from the aligned base
+  int off_x, off_w, off_stg, off_btab;  // from the aligned base
 };
 
 namespace {
@@ -290,7 +238,8 @@ SLX_DEV bool block_ok(const PrefillArgs& a, int4 bl) {
 }
 
 // Cursor over this CTA's (item, chunk) tasks; invalid blocks are skipped by
-// every role alike.
+// every role alike.  An item is (block, 128 I rows) in phase 1 and
+// (block, 256 H rows) in phase 2.
 struct Cur {
   int j, c, item, blk, mb, slot, p0, n;
   bool end;
@@ -311,9 +260,8 @@ SLX_DEV void cur_seek(const PrefillArgs& a, Cur& t) {
 }
 SLX_DEV void cur_init(const PrefillArgs& a, Cur& t) { t.j = 0; t.c = 0; cur_seek(a, t); }
 SLX_DEV void cur_next_item(const PrefillArgs& a, Cur& t) { t.c = 0; ++t.j; cur_seek(a, t); }
-// t.c counts the item's pipeline stages (kCPS chunks each)
 SLX_DEV void cur_next(const PrefillArgs& a, Cur& t) {
-  if (++t.c == a.nStg) cur_next_item(a, t);
+  if (++t.c == a.nC) cur_next_item(a, t);
 }
 
 SLX_DEV int npad16(int n) { return (n + 15) & ~15; }
@@ -323,29 +271,29 @@ SLX_DEV int bias_ksteps(int nG, int cb) {  // issued K steps of bias chunk cb
   return k > 4 ? 4 : k;
 }
 
-// Where A row m (this thread) of an item reads its packed codes: the row's
-// first byte, its swizzle key, and its scale|bias word of group 0 with the
-// word stride between groups (computed once per item).
+// Where weight row n (this thread) of an item reads its packed codes: the
+// row's first byte, its swizzle key, and its scale|bias word of group 0
+// with the word stride between groups (computed once per item).
 struct RowSrc {
   const uint8_t* row;
   const uint32_t* sb;
   int swz, sbs, j;
 };
 template <int PHASE>
-SLX_DEV void row_src(const PrefillArgs& a, int slot, int mb, int m, RowSrc& o) {
+SLX_DEV void row_src(const PrefillArgs& a, int slot, int mb, int n, RowSrc& o) {
   const uint8_t* e = a.bank + (size_t)slot * a.slot_stride;
-  if (PHASE == 1) {
+  if (PHASE == 1) {  // n < 128: gate row mb*128 + n, else up row mb*128 + n - 128
     const int RB = tile_rb(a.H, 2);
-    const int r = mb * 64 + (m & 63), mat = m >> 6;
+    const int r = mb * 128 + (n & 127), mat = n >> 7;
     const int t = r >> 4, tr = r & 15;
     const uint8_t* base = e + (size_t)t * pair_tile_bytes(a.H, 2);
     o.row = base + (size_t)(mat * 16 + tr) * RB;
     o.swz = tile_swizzled(a.H, 2) ? (tr & 7) : 0;
     o.sb = reinterpret_cast<const uint32_t*>(base + 32 * RB) + mat * 16 + tr;
     o.sbs = 32;
-  } else {
+  } else {           // down row mb*256 + n
     const int RB = tile_rb(a.I, 2);
-    const int r = mb * 128 + m;
+    const int r = mb * kNW + n;
     const int t = r >> 4, tr = r & 15;
     const uint8_t* base = e + expert_a_bytes(a.H, a.I, 2) +
                           (size_t)t * single_tile_bytes(a.I, 2);
@@ -358,35 +306,36 @@ SLX_DEV void row_src(const PrefillArgs& a, int slot, int mb, int m, RowSrc& o) {
 
 }  // namespace
 
-template <int PHASE, bool ATMEM>
+template <int PHASE>
 __global__ void __launch_bounds__(kThreads, 1)
     k_prefill(const __grid_constant__ PrefillArgs a) {
-  constexpr int S = stages(ATMEM);
   extern __shared__ __align__(16) uint8_t smem_raw[];
-  uint64_t* bar_tx = reinterpret_cast<uint64_t*>(smem_raw);  // [S] B bytes landed
-  uint64_t* bar_dq = bar_tx + kS;                            // [S] A written
-  uint64_t* bar_empty = bar_dq + kS;                         // [S] MMAs done
-  uint64_t* bar_full = bar_empty + kS;                       // [2] accumulator ready
-  uint64_t* bar_free = bar_full + 2;                          // [2] accumulator drained
-  uint64_t* bar_done = bar_free + 2;                          // all MMAs complete
+  uint64_t* bar_tx = reinterpret_cast<uint64_t*>(smem_raw);  // [kSX] activations landed
+  uint64_t* bar_xfree = bar_tx + kSX;                        // [kSX] activation slot consumed
+  uint64_t* bar_dq = bar_xfree + kSX;                        // [kSW] weights written
+  uint64_t* bar_wfree = bar_dq + kSW;                        // [kSW] weight slot consumed
+  uint64_t* bar_full = bar_wfree + kSW;                      // [2] accumulator ready
+  uint64_t* bar_free = bar_full + 2;                         // [2] accumulator drained
+  uint64_t* bar_done = bar_free + 2;                         // all MMAs complete
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  // 1024-aligned region for the swizzled buffers
+  // 1024-aligned region for the swizzled operand rings
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* base = smem_raw + ((1024u - ((raw + 256u) & 1023u)) & 1023u) + 256;
-  uint8_t* sB = base + a.off_b;
-  uint8_t* sA = base + a.off_a;
+  uint8_t* sX = base + a.off_x;
+  uint8_t* sW = base + a.off_w;
   uint8_t* stg = base + a.off_stg;
   __half* btab = reinterpret_cast<__half*>(base + a.off_btab);
-  uint16_t* xch = reinterpret_cast<uint16_t*>(base + a.off_xch);  // up values, bf16
-  uint8_t* hst = base + a.off_hst;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < S; ++i) {
+    for (int i = 0; i < kSX; ++i) {
       mbar_init(&bar_tx[i], 1);
+      mbar_init(&bar_xfree[i], 1);
+    }
+    for (int i = 0; i < kSW; ++i) {
       mbar_init(&bar_dq[i], kDqThreads / 32);
-      mbar_init(&bar_empty[i], 1);
+      mbar_init(&bar_wfree[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bar_full[i], 1);
@@ -411,39 +360,36 @@ __global__ void __launch_bounds__(kThreads, 1)
   };
 
   if (warp == 0) {
-    // ---------------------------------------------------- B producer ----
+    // ------------------------------------------- activation producer ----
     if (lane == 0) {
       Cur t, pb;  // pb runs one ring ahead: its chunks are prefetched to L2
       cur_init(a, t);
       cur_init(a, pb);
-      for (int i = 0; i < S && !pb.end; ++i) cur_next(a, pb);
+      for (int i = 0; i < kSX && !pb.end; ++i) cur_next(a, pb);
       uint32_t g = 0;
       for (; !t.end && !*abort_flag; cur_next(a, t), ++g) {
-        const int st = g % S;
+        const int st = g % kSX;
         if (SLX_PF_L2_PREFETCH && !pb.end) {
-          const int p0 = pb.c * kCPS;
-          const int pn = a.nC - p0 < kCPS ? a.nC - p0 : kCPS;
-          const uint8_t* ps = a.bimg + ((size_t)pb.blk * a.nC + p0) * kStageB;
-          for (int ci = 0; ci < pn; ++ci)
-            bulk_prefetch_l2(ps + (size_t)ci * kStageB, (uint32_t)npad16(pb.n) * kRowB);
+          bulk_prefetch_l2(a.ximg + ((size_t)pb.blk * a.nC + pb.c) * kActB,
+                           (uint32_t)npad16(pb.n) * kRowB);
           cur_next(a, pb);
         }
-        if (!mbar_wait_sleep(&bar_empty[st], ((g / S) & 1) ^ 1, a.status)) { fail(SLX_ERR_DEVICE_TIMEOUT); break; }
+        if (!mbar_wait_sleep(&bar_xfree[st], ((g / kSX) & 1) ^ 1, a.status)) {
+          fail(SLX_ERR_DEVICE_TIMEOUT);
+          break;
+        }
         PF_STAMP(g, 0);
         const uint32_t bytes = (uint32_t)npad16(t.n) * kRowB;
-        const int c0 = t.c * kCPS;
-        const int nch = a.nC - c0 < kCPS ? a.nC - c0 : kCPS;
-        const uint8_t* src = a.bimg + ((size_t)t.blk * a.nC + c0) * kStageB;
-        mbar_arrive_expect_tx(&bar_tx[st], bytes * nch);
-        for (int ci = 0; ci < nch; ++ci)
-          bulk_g2s_plain(sB + ((size_t)st * kCPS + ci) * kStageB,
-                         src + (size_t)ci * kStageB, bytes, &bar_tx[st]);
+        mbar_arrive_expect_tx(&bar_tx[st], bytes);
+        bulk_g2s_plain(sX + (size_t)st * kActB,
+                       a.ximg + ((size_t)t.blk * a.nC + t.c) * kActB, bytes,
+                       &bar_tx[st]);
         PF_STAMP(g, 1);
       }
       // drain: every issued copy has landed before the CTA exits
       const uint32_t issued = g;
-      for (uint32_t h = issued > S ? issued - S : 0; h < issued; ++h)
-        mbar_wait(&bar_tx[h % S], (h / S) & 1, a.status);
+      for (uint32_t h = issued > kSX ? issued - kSX : 0; h < issued; ++h)
+        mbar_wait(&bar_tx[h % kSX], (h / kSX) & 1, a.status);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------- MMA issue ----
@@ -453,18 +399,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t g = 0;
       int jl = 0;
       bool ok = true;
+      const uint32_t idesc = idesc_f16(kNW);  // M 128 pairs, N 256 weight rows
       while (!t.end && ok && !*abort_flag) {
         const int buf = jl & 1;
-        if (!mbar_wait(&bar_free[buf], ((jl >> 1) & 1) ^ 1, a.status)) { fail(SLX_ERR_DEVICE_TIMEOUT); break; }
+        if (!mbar_wait(&bar_free[buf], ((jl >> 1) & 1) ^ 1, a.status)) {
+          fail(SLX_ERR_DEVICE_TIMEOUT);
+          break;
+        }
         tc_fence_after();
-        const uint32_t d = tmem + kAccCol + buf * kNT;
-        const uint32_t idesc = idesc_f16(npad16(t.n));
-        for (int sg = 0; sg < a.nStg; ++sg, ++g) {
-          const int st = g % S;
-          const uint32_t ph = (g / S) & 1;
-          bool okw = mbar_wait(&bar_tx[st], ph, a.status);
+        const uint32_t d = tmem + buf * kNW;
+        for (int c = 0; c < a.nC; ++c, ++g) {
+          const int sx = g % kSX, sw = g % kSW;
+          bool okw = mbar_wait(&bar_tx[sx], (g / kSX) & 1, a.status);
           PF_STAMP(g, 2);
-          okw = okw && mbar_wait(&bar_dq[st], ph, a.status);
+          okw = okw && mbar_wait(&bar_dq[sw], (g / kSW) & 1, a.status);
           PF_STAMP(g, 3);
           if (!okw) {
             fail(SLX_ERR_DEVICE_TIMEOUT);
@@ -472,23 +420,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const int c0 = sg * kCPS;
-          const int nch = a.nC - c0 < kCPS ? a.nC - c0 : kCPS;
-          for (int ci = 0; ci < nch; ++ci) {
-            const int c = c0 + ci;
-            const int nk = c < a.nG ? 4 : bias_ksteps(a.nG, c - a.nG);
-            const uint32_t b0 = smem_u32(sB + ((size_t)st * kCPS + ci) * kStageB);
-            const uint32_t a0 = smem_u32(sA + ((size_t)st * kCPS + ci) * kStageA);
-            for (int s = 0; s < nk; ++s) {
-              const uint64_t bd = sdesc_sw128(b0 + 32 * s);
-              const uint32_t acc = (c | s) != 0;
-              if (ATMEM)
-                tc_mma_ts(d, tmem + (st * kCPS + ci) * 32 + 8 * s, bd, idesc, acc);
-              else
-                tc_mma_ss(d, sdesc_sw128(a0 + 32 * s), bd, idesc, acc);
-            }
-          }
-          tc_commit(&bar_empty[st]);
+          const int nk = c < a.nG ? 4 : bias_ksteps(a.nG, c - a.nG);
+          const uint32_t x0 = smem_u32(sX + (size_t)sx * kActB);
+          const uint32_t w0 = smem_u32(sW + (size_t)sw * kWB);
+          for (int s = 0; s < nk; ++s)
+            tc_mma_ss(d, sdesc_sw128(x0 + 32 * s), sdesc_sw128(w0 + 32 * s),
+                      idesc, (c | s) != 0);
+          tc_commit(&bar_xfree[sx]);
+          tc_commit(&bar_wfree[sw]);
           PF_STAMP(g, 4);
         }
         if (!ok) break;
@@ -501,9 +440,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp < 6) {
     // -------------------------------------------------------- epilogue ----
+    // thread = pair m of the block (TMEM lane); columns = weight rows
     const int q = warp & 3;
-    const int te = threadIdx.x - 64;  // 0..127
-    const bool issuer = te == 0;
+    const int m = 32 * q + lane;
     Cur t;
     cur_init(a, t);
     int jl = 0;
@@ -512,139 +451,109 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool ok = __all_sync(0xffffffffu,
                                  mbar_wait_sleep(&bar_full[buf], (jl >> 1) & 1, a.status));
       if (!ok) fail(SLX_ERR_DEVICE_TIMEOUT);
-      bool stop = !ok || *abort_flag;
-      stop = named_bar_or(1, 128, stop);
-      if (stop) break;
+      if (__any_sync(0xffffffffu, !ok || *abort_flag != 0)) break;
       tc_fence_after();
-      const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16) + kAccCol + buf * kNT;
-      const int np = npad16(t.n);
+      const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16) + buf * kNW;
+      const bool valid = m < t.n;
       if (PHASE == 1) {
-        if (issuer) bulk_wait_read();  // the previous item's store left hst
-        named_bar(1, 128);
-        const int r = 32 * (q & 1) + lane;  // I row within the block
-        if (q >= 2) {
-          for (int cc = 0; cc < np; cc += 16) {
-            uint32_t v[16];
-            tc_ld16(tq + cc, v);
+        // columns 0..127 gate, 128..255 up of I rows mb*128 + 0..127: two
+        // groups of 64 = two chunks of phase 2's activation image
+        for (int jg = 0; jg < 2; ++jg) {
+          const int chunk = t.mb * 2 + jg;
+          uint8_t* dst = a.himg + ((size_t)t.blk * a.nC2 + chunk) * kActB +
+                         (size_t)m * kRowB;
+          float hs = 0.f;
+          for (int cc = 0; cc < 64; cc += 16) {
+            uint32_t gv[16], uv[16];
+            tc_ld16(tq + 64 * jg + cc, gv);
+            tc_ld16(tq + 128 + 64 * jg + cc, uv);
             tc_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-              xch[r * kXchStride + cc + i] = f32_to_bf16(__uint_as_float(v[i]));
-          }
-        }
-        named_bar(1, 128);
-        if (q < 2) {
-          const int pos = kpos(r);
-          for (int cc = 0; cc < np; cc += 16) {
-            uint32_t v[16];
-            tc_ld16(tq + cc, v);
-            tc_wait_ld();
+            float h[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-              const int n = cc + i;
-              const float gt = round_bf16(__uint_as_float(v[i]));
-              const float up = bf16_to_f32(xch[r * kXchStride + n]);
-              const float h = round_bf16(silu_f32(gt) * up);
-              *reinterpret_cast<uint16_t*>(hst + sw_off(n, pos)) =
-                  h_bits(__float2half_rn(h));
+              const float gt = round_bf16(__uint_as_float(gv[i]));
+              const float up = round_bf16(__uint_as_float(uv[i]));
+              h[i] = round_bf16(silu_f32(gt) * up);
+              hs += h[i];
+            }
+            // 16 I rows 16w..16w+15 of the group fill positions 16w..16w+15
+            // (permuted order): word j = (h[j], h[j+8]), units 2w and 2w+1
+            uint32_t hw[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              hw[j] = (uint32_t)h_bits(__float2half_rn(h[j])) |
+                      ((uint32_t)h_bits(__float2half_rn(h[j + 8])) << 16);
+            if (valid) {
+              const int w = cc >> 4;
+              *reinterpret_cast<uint4*>(dst + (((2 * w) ^ (m & 7)) << 4)) =
+                  make_uint4(hw[0], hw[1], hw[2], hw[3]);
+              *reinterpret_cast<uint4*>(dst + (((2 * w + 1) ^ (m & 7)) << 4)) =
+                  make_uint4(hw[4], hw[5], hw[6], hw[7]);
             }
           }
-          fence_proxy_async();
-        }
-        tc_fence_before();
-        named_bar(1, 128);
-        // group sums of the 64 h values of each pair -> phase 2 bias columns
-        if (te < t.n) {
-          const uint4* row = reinterpret_cast<const uint4*>(hst + te * kRowB);
-          float s = 0.f;
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const uint4 w = row[(u + te) & 7];  // 8 threads: 8 distinct units
-            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&ww[k]));
-              s += f.x + f.y;
-            }
+          if (valid) {
+            const __half hi = __float2half_rn(hs);
+            const __half lo = __float2half_rn(hs - __half2float(hi));
+            uint8_t* bd = a.himg +
+                          ((size_t)t.blk * a.nC2 + a.nG2 + (chunk >> 5)) * kActB +
+                          sw_off(m, 2 * (chunk & 31));
+            *reinterpret_cast<uint32_t*>(bd) =
+                (uint32_t)h_bits(hi) | ((uint32_t)h_bits(lo) << 16);
           }
-          const __half hi = __float2half_rn(s);
-          const __half lo = __float2half_rn(s - __half2float(hi));
-          const int pos = 2 * (t.mb & 31);
-          uint8_t* dst = a.himg + ((size_t)t.blk * a.nC2 + a.nG2 + (t.mb >> 5)) * kStageB +
-                         sw_off(te, pos);
-          *reinterpret_cast<uint32_t*>(dst) =
-              (uint32_t)h_bits(hi) | ((uint32_t)h_bits(lo) << 16);
-        }
-        if (issuer) {
-          bulk_s2g(a.himg + ((size_t)t.blk * a.nC2 + t.mb) * kStageB, hst,
-                   (uint32_t)np * kRowB);
-          bulk_commit();
         }
       } else {
-        // output rows of the item's pairs, staged once (one load per thread)
-        int32_t* orow = reinterpret_cast<int32_t*>(base + a.off_orow);
-        if (te < t.n) {
-          const int p = t.p0 + te;
-          orow[te] = a.out_row ? a.out_row[p] : p;
+        int row = -1;
+        if (valid) {
+          const int p = t.p0 + m;
+          row = a.out_row ? a.out_row[p] : p;
+          if (row < 0 || row >= a.n_out) {
+            set_status(a.status, SLX_ERR_OUT_OF_RANGE);
+            row = -1;
+          }
         }
-        named_bar(1, 128);
-        const int hr = t.mb * 128 + 32 * q + lane;
-        for (int cc = 0; cc < t.n; cc += 16) {
+        uint16_t* orow = row >= 0 ? a.out + (size_t)row * a.H + t.mb * kNW : nullptr;
+        for (int cc = 0; cc < kNW; cc += 16) {
           uint32_t v[16];
           tc_ld16(tq + cc, v);
           tc_wait_ld();
+          if (orow) {
+            uint32_t o[8];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int n = cc + i;
-            if (n < t.n) {
-              const int row = orow[n];
-              if (row >= 0 && row < a.n_out)
-                a.out[(size_t)row * a.H + hr] = f32_to_bf16(__uint_as_float(v[i]));
-              else if (q == 0 && lane == 0)
-                set_status(a.status, SLX_ERR_OUT_OF_RANGE);
-            }
+            for (int j = 0; j < 8; ++j)
+              o[j] = pack_bf16x2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+            uint4* dp = reinterpret_cast<uint4*>(orow + cc);
+            dp[0] = make_uint4(o[0], o[1], o[2], o[3]);
+            dp[1] = make_uint4(o[4], o[5], o[6], o[7]);
           }
         }
-        tc_fence_before();
-        named_bar(1, 128);  // orow is rewritten by the next item
       }
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar_free[buf]);
       ++jl;
       cur_next_item(a, t);
     }
-    if (PHASE == 1 && issuer) bulk_wait_all();
   } else {
     // -------------------------------------------------- dequantization ----
-    // Group grp (warps 6-9 / 10-13) dequantizes chunk grp of every stage:
-    // each thread one A row (TMEM lane), the row's whole 16-byte code unit.
-    const int dq = threadIdx.x - 192;  // 0..255
-    const int grp = (warp - 6) >> 2;   // chunk of the stage this group owns
-    const int q = warp & 3;
-    const int m = 32 * q + lane;       // A row = TMEM lane
-    const int gt = dq & 127;           // thread within the group
-    // staging, thread-contiguous (conflict-free): codes [slot][group thread]
-    // 16 bytes, scale|bias words [slot][group thread] 4 bytes, per group
-    uint4* stg_codes = reinterpret_cast<uint4*>(stg) + grp * kDqDepth * 128;
-    uint32_t* stg_sb = reinterpret_cast<uint32_t*>(stg + 2 * kDqDepth * 128 * 16) +
-                       grp * kDqDepth * 128;
+    const int n = threadIdx.x - 192;  // weight row of the item, 0..255
+    // staging, thread-contiguous (conflict-free): codes [slot][row] 16
+    // bytes, then scale|bias words [slot][row] 4 bytes
+    uint4* stg_codes = reinterpret_cast<uint4*>(stg);
+    uint32_t* stg_sb = reinterpret_cast<uint32_t*>(stg + kDqDepth * kDqThreads * 16);
     Cur pf, cu;
     cur_init(a, pf);
     cur_init(a, cu);
     RowSrc rs;
     rs.j = -1;
     auto issue = [&](int slot) {
-      if (!pf.end) {
-        const int c = pf.c * kCPS + grp;
-        if (c < a.nG) {
-          if (rs.j != pf.j) {
-            row_src<PHASE>(a, pf.slot, pf.mb, m, rs);
-            rs.j = pf.j;
-          }
-          const int u = slot * 128 + gt;
-          cp_async16(smem_u32(stg_codes + u), rs.row + ((c ^ rs.swz) << 4));
-          cp_async4(smem_u32(stg_sb + u), rs.sb + c * rs.sbs);
+      if (!pf.end && pf.c < a.nG) {
+        if (rs.j != pf.j) {
+          row_src<PHASE>(a, pf.slot, pf.mb, n, rs);
+          rs.j = pf.j;
         }
+        const int u = slot * kDqThreads + n;
+        cp_async16(smem_u32(stg_codes + u), rs.row + ((pf.c ^ rs.swz) << 4));
+        cp_async4(smem_u32(stg_sb + u), rs.sb + pf.c * rs.sbs);
       }
       cp_async_commit();
     };
@@ -658,75 +567,59 @@ __global__ void __launch_bounds__(kThreads, 1)
       cp_async_wait<kDqDepth - 1>();
       if (warp == 6 && lane == 0) PF_STAMP(g, 5);
       const int slot = g % kDqDepth;
-      const int c = cu.c * kCPS + grp;
-      // bias table [g][row] of this item; two buffers by item parity (the
-      // other group may already be in the next item, at most a ring ahead)
-      __half* bt = btab + (cu.j & 1) * a.nG * 128;
+      const int c = cu.c;
       uint4 cw = make_uint4(0, 0, 0, 0);
       uint32_t sbw = 0;
       if (c < a.nG) {
-        cw = stg_codes[slot * 128 + gt];
-        sbw = stg_sb[slot * 128 + gt];
+        cw = stg_codes[slot * kDqThreads + n];
+        sbw = stg_sb[slot * kDqThreads + n];
       }
       issue(slot);
       cur_next(a, pf);
-      const int st = g % S;
-      bool ok = mbar_wait_sleep(&bar_empty[st], ((g / S) & 1) ^ 1, a.status);
+      const int sw = g % kSW;
+      const bool ok = mbar_wait_sleep(&bar_wfree[sw], ((g / kSW) & 1) ^ 1, a.status);
       if (warp == 6 && lane == 0) PF_STAMP(g, 6);
-      if (ok && c >= a.nG && c < a.nC && g > 0) {
-        // bias chunk: every code chunk of the item (both groups) has written
-        // its biases once the previous stage's arrivals are complete
-        ok = mbar_wait_sleep(&bar_dq[(g - 1) % S], ((g - 1) / S) & 1, a.status);
-      }
       if (!__all_sync(0xffffffffu, ok)) {
         fail(SLX_ERR_DEVICE_TIMEOUT);
         break;
       }
-      if (c < a.nC) {
-        uint32_t out[32];
-        if (c < a.nG) {
-          const __half s16 = __float2half_rn(bf16_lo(sbw));
-          bt[c * 128 + m] = __float2half_rn(bf16_hi(sbw));
-          const __half2 s2 = __half2half2(s16);
-          const __half2 n2 = __half2half2(__hneg(__hmul(s16, __float2half_rn(1024.f))));
-          const uint32_t wd[4] = {cw.x, cw.y, cw.z, cw.w};
+      uint32_t out[32];
+      if (c < a.nG) {
+        const __half s16 = __float2half_rn(bf16_lo(sbw));
+        // this thread's row only: written here, read back at the bias chunk
+        btab[c * kDqThreads + n] = __float2half_rn(bf16_hi(sbw));
+        const __half2 s2 = __half2half2(s16);
+        const __half2 n2 = __half2half2(__hneg(__hmul(s16, __float2half_rn(1024.f))));
+        const uint32_t wd[4] = {cw.x, cw.y, cw.z, cw.w};
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < 4; ++i) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const uint32_t r = ((wd[i] >> (2 * j)) & 0x00030003u) | 0x64006400u;
-              const __half2 h = __hfma2(*reinterpret_cast<const __half2*>(&r), s2, n2);
-              out[8 * i + j] = *reinterpret_cast<const uint32_t*>(&h);
-            }
-          }
-        } else {
-          const int cb = c - a.nG;
-#pragma unroll
-          for (int k2 = 0; k2 < 32; ++k2) {
-            const int gi = 32 * cb + k2;
-            const uint32_t hb = gi < a.nG ? h_bits(bt[gi * 128 + m]) : 0u;
-            out[k2] = hb | (hb << 16);
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t r = ((wd[i] >> (2 * j)) & 0x00030003u) | 0x64006400u;
+            const __half2 h = __hfma2(*reinterpret_cast<const __half2*>(&r), s2, n2);
+            out[8 * i + j] = *reinterpret_cast<const uint32_t*>(&h);
           }
         }
-        if (ATMEM) {
-          tc_st32(tmem + ((uint32_t)(32 * q) << 16) + (st * kCPS + grp) * 32, out);
-          tc_wait_st();
-          tc_fence_before();
-        } else {
-          uint8_t* rowp = sA + ((size_t)st * kCPS + grp) * kStageA + (m >> 3) * 1024 +
-                          (m & 7) * kRowB;
+      } else {
+        const int cb = c - a.nG;
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const int pu = u ^ (m & 7);
-            *reinterpret_cast<uint4*>(rowp + pu * 16) =
-                make_uint4(out[4 * u], out[4 * u + 1], out[4 * u + 2], out[4 * u + 3]);
-          }
-          fence_proxy_async();
+        for (int k2 = 0; k2 < 32; ++k2) {
+          const int gi = 32 * cb + k2;
+          const uint32_t hb = gi < a.nG ? h_bits(btab[gi * kDqThreads + n]) : 0u;
+          out[k2] = hb | (hb << 16);
         }
       }
+      uint8_t* rowp = sW + (size_t)sw * kWB + (n >> 3) * 1024 + (n & 7) * kRowB;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int pu = u ^ (n & 7);
+        *reinterpret_cast<uint4*>(rowp + pu * 16) =
+            make_uint4(out[4 * u], out[4 * u + 1], out[4 * u + 2], out[4 * u + 3]);
+      }
+      fence_proxy_async();
       __syncwarp();
       if (warp == 6 && lane == 0) PF_STAMP(g, 7);
-      if (lane == 0) mbar_arrive(&bar_dq[st]);
+      if (lane == 0) mbar_arrive(&bar_dq[sw]);
       cur_next(a, cu);
       ++g;
     }
@@ -765,7 +658,7 @@ __global__ void __launch_bounds__(256)
     return;
   }
   const uint16_t* xrow = x + (size_t)xr * H;
-  uint8_t* blk = img + (size_t)b * nC * kStageB;
+  uint8_t* blk = img + (size_t)b * nC * kActB;
   const int u = lane & 7;            // 16-byte unit of the chunk row
   const int i = u >> 1, j0 = 4 * (u & 1);
   for (int c0 = 0; c0 < nG; c0 += 4) {
@@ -785,7 +678,7 @@ __global__ void __launch_bounds__(256)
       o[k] = (uint32_t)h_bits(__float2half_rn(a0)) |
              ((uint32_t)h_bits(__float2half_rn(a1)) << 16);
     }
-    *reinterpret_cast<uint4*>(blk + (size_t)c * kStageB + n * kRowB +
+    *reinterpret_cast<uint4*>(blk + (size_t)c * kActB + n * kRowB +
                               ((u ^ (n & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
     s += __shfl_xor_sync(0xffffffffu, s, 1);
     s += __shfl_xor_sync(0xffffffffu, s, 2);
@@ -794,7 +687,7 @@ __global__ void __launch_bounds__(256)
       const __half hi = __float2half_rn(s);
       const __half lo = __float2half_rn(s - __half2float(hi));
       const int pos = 2 * (c & 31);
-      *reinterpret_cast<uint32_t*>(blk + (size_t)(nG + (c >> 5)) * kStageB +
+      *reinterpret_cast<uint32_t*>(blk + (size_t)(nG + (c >> 5)) * kActB +
                                    n * kRowB + ((((pos >> 3) ^ (n & 7))) << 4) +
                                    ((pos & 7) << 1)) =
           (uint32_t)h_bits(hi) | ((uint32_t)h_bits(lo) << 16);
@@ -809,21 +702,16 @@ namespace {
 int pf_chunks(int nG) { return nG + (nG + 31) / 32; }
 
 struct SmemPlan {
-  int off_b, off_a, off_stg, off_btab, off_xch, off_hst, off_orow, bytes;
+  int off_x, off_w, off_stg, off_btab, bytes;
 };
 
-SmemPlan plan_smem(int phase, bool atmem, int nG) {
+SmemPlan plan_smem(int nG) {
   SmemPlan p = {};
   int o = 0;
-  p.off_b = o;   o += stages(atmem) * kCPS * kStageB;
-  p.off_hst = o; if (phase == 1) o += kStageB;
-  p.off_a = o;   if (!atmem) o += stages(atmem) * kCPS * kStageA;
-  p.off_stg = o; o += 2 * kDqDepth * 128 * (16 + 4);
-  p.off_btab = o; o += 2 * nG * 128 * 2;
-  o = (o + 15) & ~15;
-  p.off_xch = o; if (phase == 1) o += 64 * kXchStride * 2;
-  o = (o + 15) & ~15;
-  p.off_orow = o; if (phase == 2) o += kNT * 4;
+  p.off_x = o;    o += kSX * kActB;
+  p.off_w = o;    o += kSW * kWB;
+  p.off_stg = o;  o += kDqDepth * kDqThreads * (16 + 4);
+  p.off_btab = o; o += nG * kDqThreads * 2;
   // + barrier area (256) + worst-case 1024 alignment; at least 120 KB so one
   // CTA (and one 512-column TMEM allocation) per SM
   int bytes = o + 256 + 1024;
@@ -834,11 +722,11 @@ SmemPlan plan_smem(int phase, bool atmem, int nG) {
 
 int g_num_sms_pf = 0;
 
-template <int PHASE, bool ATMEM>
+template <int PHASE>
 int launch_phase(PrefillArgs a, int smem, cudaStream_t s) {
   static int attr_set = 0;
   if (!attr_set) {
-    if (cudaFuncSetAttribute(k_prefill<PHASE, ATMEM>,
+    if (cudaFuncSetAttribute(k_prefill<PHASE>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              227 * 1024) != cudaSuccess)
       return SLX_ERR_CUDA;
@@ -846,7 +734,7 @@ int launch_phase(PrefillArgs a, int smem, cudaStream_t s) {
   }
   if (a.n_items == 0) return SLX_OK;
   const int grid = a.n_items < g_num_sms_pf ? a.n_items : g_num_sms_pf;
-  k_prefill<PHASE, ATMEM><<<grid, kThreads, smem, s>>>(a);
+  k_prefill<PHASE><<<grid, kThreads, smem, s>>>(a);
   return cudaGetLastError() == cudaSuccess ? SLX_OK : SLX_ERR_CUDA;
 }
 
@@ -854,14 +742,14 @@ int launch_phase(PrefillArgs a, int smem, cudaStream_t s) {
 
 size_t prefill_scratch_bytes(int n_blocks, int H, int I) {
   const size_t c1 = pf_chunks(H / 64), c2 = pf_chunks(I / 64);
-  return (size_t)n_blocks * (c1 + c2) * kStageB;
+  return (size_t)n_blocks * (c1 + c2) * kActB;
 }
 
 int launch_prefill(const uint8_t* bank, long long slot_stride, int n_slots,
                    int H, int I, const uint16_t* x, int n_rows,
                    const int32_t* pair_row, int n_pairs, const int4* blocks,
                    int n_blocks, const int32_t* out_row, uint16_t* out,
-                   int n_out, uint8_t* scratch, int32_t* status, int a_tmem,
+                   int n_out, uint8_t* scratch, int32_t* status,
                    cudaStream_t s) {
   if (g_num_sms_pf == 0) {
     int dev = 0;
@@ -871,7 +759,7 @@ int launch_prefill(const uint8_t* bank, long long slot_stride, int n_slots,
       return SLX_ERR_CUDA;
   }
   const int nG1 = H / 64, nG2 = I / 64;
-  if (nG1 > 64 || nG2 > 64) return SLX_ERR_UNSUPPORTED;
+  if (nG1 > 64 || nG2 > 64 || I % 128 || H % kNW) return SLX_ERR_UNSUPPORTED;
   PrefillArgs a = {};
   a.bank = bank;
   a.slot_stride = slot_stride;
@@ -885,13 +773,13 @@ int launch_prefill(const uint8_t* bank, long long slot_stride, int n_slots,
   a.nG2 = nG2;
   a.nC2 = pf_chunks(nG2);
   uint8_t* ximg = scratch;
-  uint8_t* himg = scratch + (size_t)n_blocks * pf_chunks(nG1) * kStageB;
+  uint8_t* himg = scratch + (size_t)n_blocks * pf_chunks(nG1) * kActB;
   a.himg = himg;
   a.out = out;
   a.out_row = out_row;
   a.n_out = n_out;
 
-  // phase 0: gather x rows into phase 1's B image
+  // phase 0: gather x rows into phase 1's activation image
   {
     dim3 grid(n_blocks, kNT / 8);
     k_pf_pack_x<<<grid, 256, 0, s>>>(x, n_rows, H, pair_row, blocks, n_blocks,
@@ -899,22 +787,19 @@ int launch_prefill(const uint8_t* bank, long long slot_stride, int n_slots,
                                      ximg, status);
     if (cudaGetLastError() != cudaSuccess) return SLX_ERR_CUDA;
   }
-  // phase 1: gate/up -> SwiGLU -> phase 2's B image
+  // phase 1: gate/up -> SwiGLU -> phase 2's activation image
   {
     PrefillArgs p = a;
     p.nG = nG1;
     p.nC = pf_chunks(nG1);
-    p.nStg = (p.nC + kCPS - 1) / kCPS;
-    p.n_mb = I / 64;
+    p.n_mb = I / 128;
     p.n_items = n_blocks * p.n_mb;
-    p.bimg = ximg;
-    const SmemPlan sp = plan_smem(1, a_tmem != 0, nG1);
-    p.off_b = sp.off_b; p.off_a = sp.off_a; p.off_stg = sp.off_stg;
-    p.off_btab = sp.off_btab; p.off_xch = sp.off_xch; p.off_hst = sp.off_hst;
-    p.off_orow = sp.off_orow;
+    p.ximg = ximg;
+    const SmemPlan sp = plan_smem(nG1);
+    p.off_x = sp.off_x; p.off_w = sp.off_w; p.off_stg = sp.off_stg;
+    p.off_btab = sp.off_btab;
     if (sp.bytes > 227 * 1024) return SLX_ERR_UNSUPPORTED;
-    const int rc = a_tmem ? launch_phase<1, true>(p, sp.bytes, s)
-                          : launch_phase<1, false>(p, sp.bytes, s);
+    const int rc = launch_phase<1>(p, sp.bytes, s);
     if (rc) return rc;
   }
   // phase 2: down projection -> per-pair outputs
@@ -922,17 +807,14 @@ int launch_prefill(const uint8_t* bank, long long slot_stride, int n_slots,
     PrefillArgs p = a;
     p.nG = nG2;
     p.nC = pf_chunks(nG2);
-    p.nStg = (p.nC + kCPS - 1) / kCPS;
-    p.n_mb = H / 128;
+    p.n_mb = H / kNW;
     p.n_items = n_blocks * p.n_mb;
-    p.bimg = himg;
-    const SmemPlan sp = plan_smem(2, a_tmem != 0, nG2);
-    p.off_b = sp.off_b; p.off_a = sp.off_a; p.off_stg = sp.off_stg;
-    p.off_btab = sp.off_btab; p.off_xch = sp.off_xch; p.off_hst = sp.off_hst;
-    p.off_orow = sp.off_orow;
+    p.ximg = himg;
+    const SmemPlan sp = plan_smem(nG2);
+    p.off_x = sp.off_x; p.off_w = sp.off_w; p.off_stg = sp.off_stg;
+    p.off_btab = sp.off_btab;
     if (sp.bytes > 227 * 1024) return SLX_ERR_UNSUPPORTED;
-    const int rc = a_tmem ? launch_phase<2, true>(p, sp.bytes, s)
-                          : launch_phase<2, false>(p, sp.bytes, s);
+    const int rc = launch_phase<2>(p, sp.bytes, s);
     if (rc) return rc;
   }
   return SLX_OK;
