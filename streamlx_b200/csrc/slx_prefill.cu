@@ -42,7 +42,7 @@
 //
 // Warp roles (448 threads, one CTA per SM, persistent over work items):
 //   warp 0      TMEM allocation; lane 0 streams activation chunks
-//               (cp.async.bulk, the TMA engine) into a 6-stage ring, with
+//               (cp.async.bulk, the TMA engine) into a 4-stage ring, with
 //               an L2 prefetch of the chunks one ring ahead (a copy takes
 //               ~3 us to land);
 //   warp 1      lane 0 issues the MMAs (M128 x N256 x K16, kind::f16, both
@@ -53,8 +53,8 @@
 //               item's MMAs overlap it);
 //   warps 6-13  dequantization: each thread one weight row; its 16-byte
 //               code unit and scale|bias word prefetched with cp.async four
-//               chunks ahead; fp16 weights written into a 2-stage ring of
-//               swizzled K-major chunks.
+//               chunks ahead; fp16 weights written into a ring of
+//               swizzled K-major chunks (a 3-stage ring).
 // Every wait is bounded (2 s); on expiry the kernel records
 // SLX_ERR_DEVICE_TIMEOUT, drains its in-flight copies and MMAs, frees TMEM
 // and returns.
@@ -88,8 +88,14 @@ constexpr int kNW = 256;            // weight rows per item (MMA N)
 constexpr int kRowB = 128;          // bytes of one 64-column fp16 chunk row
 constexpr int kActB = kNT * kRowB;  // activation chunk (16 KB)
 constexpr int kWB = kNW * kRowB;    // weight chunk (32 KB)
-constexpr int kSX = 6;              // activation ring stages (one chunk each)
-constexpr int kSW = 2;              // weight ring stages (one chunk each)
+#ifndef SLX_PF_SX
+#define SLX_PF_SX 4
+#endif
+#ifndef SLX_PF_SW
+#define SLX_PF_SW 3
+#endif
+constexpr int kSX = SLX_PF_SX;      // activation ring stages (one chunk each)
+constexpr int kSW = SLX_PF_SW;      // weight ring stages (one chunk each)
 constexpr int kThreads = 448;
 constexpr int kDqThreads = 256;     // one weight row each
 constexpr int kDqDepth = 4;         // cp.async chunks in flight per thread
