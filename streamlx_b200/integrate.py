@@ -403,17 +403,31 @@ def install_streaming(model, model_dir: str, n_slots: int):
 
 def plan_residency(layers: list, bpe: dict, n_exp: dict, budget_bytes: int,
                    k: int) -> tuple[set, float]:
-    """Greedy water-fill of fully resident layers (integrate.py:322-346)."""
+    """Which MoE layers hold ALL their experts (no pool, no streaming), and
+    the budget left for the pools of the others (streamlx/integrate.py:
+    322-346 decides the same way).
+
+    Layers are visited from the smallest whole-layer size up.  A layer is
+    made resident when its whole size fits the fair share of what is left
+    (``left / still-streamed layers``) and, after paying for it, every other
+    still-streamed layer can keep ``k`` slots.  Paying for a small layer
+    raises the fair share of the rest, so on a budget near the total expert
+    bytes the decision cascades to every layer; on a small budget none
+    qualifies."""
+    streamed = sorted(layers, key=lambda j: n_exp[j] * bpe[j])
+    order = list(streamed)
     resident: set = set()
-    streamed = list(layers)
     left = float(budget_bytes)
-    for i in sorted(layers, key=lambda j: n_exp[j] * bpe[j]):
-        full = n_exp[i] * bpe[i]
-        min_rest = sum(k * bpe[j] for j in streamed if j != i)
-        if left / len(streamed) >= full and left - full >= min_rest:
+    # k-slot floor of every still-streamed layer, kept as a running sum
+    floor = float(sum(k * bpe[j] for j in streamed))
+    for i in order:
+        whole = n_exp[i] * bpe[i]
+        others = floor - k * bpe[i]
+        if whole <= left / len(streamed) and left - whole >= others:
             resident.add(i)
             streamed.remove(i)
-            left -= full
+            floor = others
+            left -= whole
     return resident, left
 
 
@@ -480,32 +494,35 @@ def load_streaming_model(model_dir: str, budget_bytes: int, k: int = 8,
 
 
 def preload_popular(pools: dict, trace_npz: str) -> int:
-    """Warm-start each pool with its layer's most-routed experts from a
-    routing trace (integrate.py:476-506)."""
-    import json
-    from pathlib import Path
-    d = np.load(trace_npz)
-    e = d["experts"]
-    p = Path(trace_npz)
-    side = p.parent / (p.stem + ".meta.json")
-    if side.exists():
-        layer_ids = json.loads(side.read_text())["layer_ids"]
-    else:
-        layer_ids = list(range(e.shape[1]))
-    axis_of = {int(lid): i for i, lid in enumerate(layer_ids)}
-    total = 0
+    """Warm-start every pool with the experts its layer routed to most often
+    in a routing trace (``streamlx_b200.trace`` format; streamlx/integrate.py:
+    476-506 reads the same file).
+
+    The trace's axis of each model layer comes from the sidecar's
+    ``layer_ids`` (identity when there is no sidecar); a layer absent from
+    the trace is left cold.  Per pool the ``n_slots`` largest counts are
+    taken in the order numpy's default argsort of the counts gives, reversed
+    (the same call as the reference, so ties fall the same way), then loaded
+    in ascending id order (one ``ensure``: file-ordered reads).  Pad entries
+    (0xFFFF) are not counted.  Returns the number of experts loaded."""
+    from .trace import PAD, read_trace
+    arrays, meta = read_trace(trace_npz)
+    routed = arrays["experts"]
+    axes = (meta["layer_ids"] if meta is not None
+            else list(range(routed.shape[1])))
+    axis_of = {int(lid): a for a, lid in enumerate(axes)}
+    loaded = 0
     for lid, pool in pools.items():
-        ax = axis_of.get(lid)
-        if ax is None:
+        a = axis_of.get(int(lid))
+        if a is None:
             continue
-        col = e[:, ax, :].ravel()
-        col = col[col != 0xFFFF]
-        hist = np.bincount(col, minlength=pool.n_experts)
-        top = np.argsort(hist)[::-1][: pool.n_slots]
+        col = routed[:, a, :].reshape(-1)
+        counts = np.bincount(col[col != PAD], minlength=pool.n_experts)
+        pick = np.argsort(counts)[::-1][:pool.n_slots]
         pool.begin_call()
-        pool.ensure(sorted(int(x) for x in top))
-        total += len(top)
-    return total
+        pool.ensure(sorted(int(e) for e in pick))
+        loaded += len(pick)
+    return loaded
 
 
 def aggregate_stats(pools: dict) -> dict:

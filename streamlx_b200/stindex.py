@@ -1,39 +1,59 @@
-"""Header-only safetensors index: tensor name -> byte range, and the byte range
-of one expert's row inside a stacked ``[n_experts, ...]`` tensor.
+"""Byte-range index over a safetensors checkpoint, built from the shard
+headers alone.
 
-Same public surface as the reference's ``streamlx/stindex.py``:
-``TensorLoc`` (stindex.py:22-39), ``SafetensorsIndex`` with
-``switch_triples`` / ``layer_expert_bytes`` / ``quant_params``
-(stindex.py:43-119).  Behaviour kept identical because the expert reader, the
-slot pool and the budget split all key off these ranges:
+Format facts this module relies on (the safetensors container and MLX's
+quantized-checkpoint conventions, not any particular loader):
 
-* only shards matching ``model-*.safetensors`` are indexed, in sorted order;
-* absolute data offset = 8 + header length + ``data_offsets[0]``;
-* bits / group_size come from ``config.json``'s ``quantization`` table
-  (per-path override, then top level, then inference at group 64), with the
-  ``language_model.`` prefix stripped from keys;
-* errors: ``IndexError`` (expert out of range), ``KeyError`` (missing switch
-  tensors), ``ValueError`` (packing mismatch), ``FileNotFoundError`` (no
-  shards).
+* a shard is ``u64 little-endian header length N`` + ``N`` bytes of JSON +
+  the raw tensor bytes; each JSON entry gives ``dtype``, ``shape`` and
+  ``data_offsets = [begin, end)`` relative to the first byte after the
+  header, so a tensor's absolute file offset is ``8 + N + begin``;
+  the optional ``__metadata__`` entry is not a tensor;
+* tensors are row-major, so row ``e`` of a stacked ``[E, ...]`` expert
+  tensor is the contiguous range ``start + e * (bytes per row)``;
+* an MLX affine-quantized matrix ``[out, in]`` is stored as ``weight``
+  uint32 ``[out, in * bits / 32]`` plus ``scales`` / ``biases``
+  ``[out, in / group_size]``; ``config.json``'s ``quantization`` object holds
+  the default ``bits`` / ``group_size`` and, as nested objects keyed by module
+  path, per-module overrides (mlx-vlm exports prefix paths with
+  ``language_model.``, which is ignored when matching).
+
+The public surface is the one streamlx's loader, reader and pool call
+(streamlx/stindex.py:22-119): ``TensorLoc`` with ``row_stride`` /
+``expert_range``; ``SafetensorsIndex(model_dir)`` with ``tensors``,
+``switch_triples(layer)``, ``layer_expert_bytes(layer)`` and
+``quant_params(triple)``; only shards named ``model-*.safetensors`` are
+indexed (in name order, a later shard's entry replacing an earlier one's);
+the exception types are ``FileNotFoundError`` (no shard), ``IndexError``
+(expert row out of range), ``KeyError`` (a layer lacks one of its nine
+stacked switch tensors) and ``ValueError`` (shapes that do not pack at the
+configured bit width).  The byte ranges are checked against the reference's
+own output by tests/golden.
 """
 
 from __future__ import annotations
 
-import glob
+import fnmatch
 import json
 import os
+import re
 import struct
 from dataclasses import dataclass
-from math import prod
 
 DTYPE_SIZE = {"U32": 4, "BF16": 2, "F16": 2, "F32": 4, "U16": 2, "U8": 1}
 PROJS = ("gate_proj", "up_proj", "down_proj")
 PARTS = ("weight", "scales", "biases")
+SUPPORTED_BITS = frozenset((2, 3, 4, 5, 6, 8))
+DEFAULT_GROUP = 64
 _VLM_PREFIX = "language_model."
+# "...layers.<L>.mlp.switch_mlp.<anything>" -- the stacked expert tensors
+_SWITCH_RE = re.compile(r"layers\.(\d+)\.mlp\.switch_mlp\.(.+)$")
 
 
 @dataclass(frozen=True)
 class TensorLoc:
+    """Where one tensor's bytes live: shard path, absolute file offset,
+    byte count, safetensors dtype tag, shape, and its key."""
     path: str
     abs_start: int
     nbytes: int
@@ -43,106 +63,166 @@ class TensorLoc:
 
     @property
     def row_stride(self) -> int:
-        """Bytes of one leading-axis row (one expert of a stacked tensor)."""
-        return DTYPE_SIZE[self.dtype] * prod(self.shape[1:])
+        """Bytes of one slice along the leading axis."""
+        n = DTYPE_SIZE[self.dtype]
+        for d in self.shape[1:]:
+            n *= d
+        return n
 
     def expert_range(self, e: int) -> tuple[str, int, int]:
-        """(path, absolute offset, nbytes) of row ``e``."""
-        n = self.shape[0]
-        if e < 0 or e >= n:
-            raise IndexError(f"expert {e} out of range {n}")
-        stride = self.row_stride
-        return self.path, self.abs_start + e * stride, stride
+        """(path, absolute offset, nbytes) of leading-axis row ``e``."""
+        rows = self.shape[0]
+        if not (0 <= e < rows):
+            raise IndexError(f"row {e} outside 0..{rows - 1} of {self.name}")
+        step = self.row_stride
+        return self.path, self.abs_start + step * e, step
 
 
-def _read_header(path: str) -> tuple[int, dict]:
+def parse_shard_header(path: str) -> list[TensorLoc]:
+    """Every tensor entry of one shard, located in absolute file offsets."""
     with open(path, "rb") as f:
-        (hlen,) = struct.unpack("<Q", f.read(8))
-        return 8 + hlen, json.loads(f.read(hlen))
+        head = f.read(8)
+        if len(head) != 8:
+            raise ValueError(f"{path}: not a safetensors file")
+        n = struct.unpack("<Q", head)[0]
+        meta = json.loads(f.read(n))
+    data0 = 8 + n
+    locs = []
+    for key, ent in meta.items():
+        if key == "__metadata__":
+            continue
+        begin, end = ent["data_offsets"]
+        locs.append(TensorLoc(path, data0 + begin, end - begin, ent["dtype"],
+                              tuple(ent["shape"]), key))
+    return locs
+
+
+def _module_key(name: str) -> str:
+    """Module path of a tensor key for quantization lookups."""
+    if name.startswith(_VLM_PREFIX):
+        name = name[len(_VLM_PREFIX):]
+    if name.endswith(".weight"):
+        name = name[:-len(".weight")]
+    return name
+
+
+class QuantTable:
+    """``config.json``'s quantization object: defaults plus per-module
+    overrides (keys compared without the ``language_model.`` prefix)."""
+
+    def __init__(self, table: dict | None):
+        table = table or {}
+        self.default_bits = None
+        self.default_group = None
+        self.modules: dict[str, dict] = {}
+        for key, val in table.items():
+            if isinstance(val, dict):
+                mk = key[len(_VLM_PREFIX):] if key.startswith(_VLM_PREFIX) \
+                    else key
+                self.modules[mk] = val
+            elif key == "bits":
+                self.default_bits = val
+            elif key == "group_size":
+                self.default_group = val
+
+    @classmethod
+    def from_model_dir(cls, model_dir: str) -> "QuantTable":
+        p = os.path.join(model_dir, "config.json")
+        if not os.path.exists(p):
+            return cls(None)
+        with open(p) as f:
+            return cls(json.load(f).get("quantization"))
+
+    def lookup(self, tensor_name: str) -> tuple:
+        """(bits or None, group size or None) for a weight tensor."""
+        over = self.modules.get(_module_key(tensor_name), {})
+        return (over.get("bits", self.default_bits),
+                over.get("group_size", self.default_group))
 
 
 class SafetensorsIndex:
+    """Tensor name -> TensorLoc over the ``model-*.safetensors`` shards of a
+    checkpoint directory, plus the per-layer stacked-expert view."""
+
     def __init__(self, model_dir: str):
         self.model_dir = str(model_dir)
+        shards = sorted(f for f in os.listdir(self.model_dir)
+                        if fnmatch.fnmatch(f, "model-*.safetensors")) \
+            if os.path.isdir(self.model_dir) else []
         self.tensors: dict[str, TensorLoc] = {}
-        pattern = os.path.join(self.model_dir, "model-*.safetensors")
-        for shard in sorted(glob.glob(pattern)):
-            base, hdr = _read_header(shard)
-            for name, info in hdr.items():
-                if name == "__metadata__":
-                    continue
-                lo, hi = info["data_offsets"]
-                self.tensors[name] = TensorLoc(shard, base + lo, hi - lo,
-                                               info["dtype"],
-                                               tuple(info["shape"]), name)
+        for fn in shards:
+            for loc in parse_shard_header(os.path.join(self.model_dir, fn)):
+                self.tensors[loc.name] = loc
         if not self.tensors:
-            raise FileNotFoundError(f"no shards under {model_dir}")
-        qtab: dict = {}
-        cfg_path = os.path.join(self.model_dir, "config.json")
-        if os.path.exists(cfg_path):
-            with open(cfg_path) as f:
-                qtab = json.load(f).get("quantization") or {}
-        self._quant_default = {k: v for k, v in qtab.items()
-                               if not isinstance(v, dict)}
-        self._quant_by_path = {self._norm(k): v for k, v in qtab.items()
-                               if isinstance(v, dict)}
-
-    @staticmethod
-    def _norm(key: str) -> str:
-        return key[len(_VLM_PREFIX):] if key.startswith(_VLM_PREFIX) else key
-
-    def switch_triples(self, layer: int) -> dict[str, dict[str, TensorLoc]]:
-        """{proj: {part: TensorLoc}} of one MoE layer's stacked experts."""
-        tag = f"layers.{layer}.mlp.switch_mlp."
-        found: dict[str, dict[str, TensorLoc]] = {}
-        for name, loc in self.tensors.items():
-            if tag not in name:
+            raise FileNotFoundError(
+                f"{self.model_dir}: no model-*.safetensors shard with tensors")
+        self.quant = QuantTable.from_model_dir(self.model_dir)
+        # layer -> {(proj, part): TensorLoc}, in tensor order (a later key
+        # with the same (proj, part) suffix replaces an earlier one)
+        self._switch: dict[int, dict] = {}
+        for key, loc in self.tensors.items():
+            m = _SWITCH_RE.search(key)
+            if m is None:
                 continue
+            tail = m.group(2)
             for proj in PROJS:
                 for part in PARTS:
-                    if name.endswith(f"{proj}.{part}"):
-                        found.setdefault(proj, {})[part] = loc
-        missing = [(p, q) for p in PROJS for q in PARTS
-                   if q not in found.get(p, {})]
-        if missing:
-            raise KeyError(f"layer {layer}: missing switch tensors {missing}")
-        return found
+                    if tail.endswith(f"{proj}.{part}"):
+                        self._switch.setdefault(int(m.group(1)), {})[
+                            (proj, part)] = loc
+
+    def switch_triples(self, layer: int) -> dict[str, dict[str, TensorLoc]]:
+        """{proj: {part: TensorLoc}} of one layer's stacked expert tensors."""
+        have = self._switch.get(int(layer), {})
+        absent = [(proj, part) for proj in PROJS for part in PARTS
+                  if (proj, part) not in have]
+        if absent:
+            raise KeyError(f"layer {layer} has no stacked expert tensor for "
+                           f"{absent}")
+        return {proj: {part: have[(proj, part)] for part in PARTS}
+                for proj in PROJS}
 
     def layer_expert_bytes(self, layer: int) -> int:
-        """Bytes of ONE expert of ``layer`` (3 projections x W/S/B)."""
-        return sum(loc.row_stride for parts in self.switch_triples(layer)
-                   .values() for loc in parts.values())
+        """Bytes of one expert of ``layer``: its row of all nine tensors."""
+        tri = self.switch_triples(layer)
+        return sum(tri[proj][part].row_stride for proj in PROJS
+                   for part in PARTS)
 
     def quant_params(self, triple: dict[str, TensorLoc]
                      ) -> tuple[int, int, int, int]:
-        """(in_features, out_features, bits, group_size) of one projection."""
+        """(in_features, out_features, bits, group_size) of one quantized
+        projection: bits and group size from the quantization table (the
+        module's override, else the default; group size 64 and bits inferred
+        from the packed width when the table is silent), then checked
+        against the stored shapes."""
         w, s = triple["weight"], triple["scales"]
-        n_groups, packed = s.shape[-1], w.shape[-1]
-        key = self._norm(w.name)
-        if key.endswith(".weight"):
-            key = key[: -len(".weight")]
-        ov = self._quant_by_path.get(key, {})
-        bits = ov.get("bits", self._quant_default.get("bits"))
-        gs = ov.get("group_size", self._quant_default.get("group_size"))
-        if gs is None:
-            gs = 64
-        in_features = n_groups * gs
+        bits, group = self.quant.lookup(w.name)
+        group = DEFAULT_GROUP if group is None else group
+        words, groups = w.shape[-1], s.shape[-1]
+        in_features = groups * group
         if bits is None:
-            bits = packed * 32 // in_features
-        if packed * 32 != in_features * bits or bits not in (2, 3, 4, 5, 6, 8):
-            raise ValueError(f"quant mismatch for {w.name}: W{w.shape} "
-                             f"S{s.shape} with bits={bits} group_size={gs}")
-        return in_features, w.shape[1], bits, gs
+            bits = (32 * words) // in_features if in_features else 0
+        if bits not in SUPPORTED_BITS or 32 * words != bits * in_features:
+            raise ValueError(
+                f"{w.name}: weight {tuple(w.shape)} / scales "
+                f"{tuple(s.shape)} do not pack {bits}-bit codes in groups "
+                f"of {group}")
+        return in_features, w.shape[1], bits, group
 
     def get(self, name: str) -> TensorLoc:
         return self.tensors[name]
 
     def read_tensor(self, name: str) -> bytes:
-        """Whole tensor bytes (trunk weights; experts go through the reader)."""
+        """All bytes of one tensor (trunk weights; experts go through the
+        reader)."""
         loc = self.tensors[name]
+        buf = bytearray(loc.nbytes)
+        view = memoryview(buf)
+        done = 0
         with open(loc.path, "rb") as f:
-            f.seek(loc.abs_start)
-            data = f.read(loc.nbytes)
-        if len(data) != loc.nbytes:
-            raise IOError(f"short read of {name}")
-        return data
+            while done < loc.nbytes:
+                n = os.preadv(f.fileno(), [view[done:]], loc.abs_start + done)
+                if n <= 0:
+                    raise IOError(f"{name}: read {done} of {loc.nbytes} bytes")
+                done += n
+        return bytes(buf)

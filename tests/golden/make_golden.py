@@ -1,17 +1,19 @@
 """Generate the golden fixtures in tests/golden/ by running the REFERENCE's own
-Python code (streamlx/stindex.py, reader.py, pool.py, integrate.py) from
-/root/reference under a numpy stand-in for mlx (tests/golden/mlx_stub).
+Python code (streamlx/stindex.py, reader.py, pool.py, integrate.py) under a
+numpy stand-in for mlx (tests/golden/mlx_stub).
 
-Run from the repo root in a container that has /root/reference:
+Run from the repo root, naming the reference checkout (the directory that
+holds the ``streamlx`` package):
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py --reference <path-to-streamlx-checkout>
 
-The fixtures pin, bit-exactly, what the reference decides: safetensors byte
-ranges, span-merge plans, and the per-call pool state (LRU order, slots,
-S3-FIFO queues, hit/miss/eviction/adopt/prefetch counters) for decode,
-prefetch, expert-major prefill sweeps and slice prefill.  The routing inputs
-are stored beside the traces, so replaying them needs neither the reference
-nor this script.
+(or set ``STREAMLX_REFERENCE``).  The fixtures pin, bit-exactly, what the
+reference decides: safetensors byte ranges, span-merge plans, the per-call
+pool state (LRU order, slots, S3-FIFO queues, hit/miss/eviction/adopt/
+prefetch counters) for decode, prefetch, expert-major prefill sweeps and
+slice prefill, the residency water-fill, and the warm-start preload.  The
+routing inputs are stored beside the traces, so replaying them needs neither
+the reference nor this script.
 
 The reference's S3-FIFO raises KeyError whenever one call inserts more new
 experts than its small FIFO holds (streamlx/pool.py:139-150 evicts them, then
@@ -19,8 +21,8 @@ pool.py:195-196 looks them up).  That is recorded as-is (``s3_unpatched``),
 and the S3-FIFO traces are taken from a runtime-patched copy in which ids
 touched or inserted during the current wrapper call are protected: a
 protected small-queue head is promoted to main instead of being ghosted, and
-main eviction skips protected entries.  /root/reference itself is never
-modified.
+main eviction skips protected entries.  The reference checkout itself is
+never modified.
 """
 
 from __future__ import annotations
@@ -33,23 +35,30 @@ import tempfile
 
 import numpy as np
 
-REF = "/root/reference"
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.join(HERE, "mlx_stub"))
-sys.path.insert(0, REF)
 
 import ml_dtypes  # noqa: E402
 
 from streamlx_b200 import synth  # noqa: E402
 
-import streamlx.integrate as ref_int  # noqa: E402
-import streamlx.pool as ref_pool  # noqa: E402
-import streamlx.reader as ref_reader  # noqa: E402
-import streamlx.stindex as ref_st  # noqa: E402
-
 BF16 = ml_dtypes.bfloat16
+ref_int = ref_pool = ref_reader = ref_st = None
+
+
+def load_reference(path: str) -> None:
+    """Import the reference's streamlx modules from a checkout directory."""
+    global ref_int, ref_pool, ref_reader, ref_st
+    if not os.path.isdir(os.path.join(path, "streamlx")):
+        raise SystemExit(f"{path}: no streamlx package there")
+    sys.path.insert(0, path)
+    import streamlx.integrate as ri
+    import streamlx.pool as rp
+    import streamlx.reader as rr
+    import streamlx.stindex as rs
+    ref_int, ref_pool, ref_reader, ref_st = ri, rp, rr, rs
 
 
 # ---------------------------------------------------------------- inputs --
@@ -278,11 +287,90 @@ def save_decode(name, snaps, pools, ids, pi, ps, meta, pf_rank):
 
 
 def main():
+    import argparse
+    ap = argparse.ArgumentParser(description="write tests/golden fixtures")
+    ap.add_argument("--reference",
+                    default=os.environ.get("STREAMLX_REFERENCE"),
+                    help="reference checkout (holds the streamlx package)")
+    ap.add_argument("--only", default=None,
+                    help="comma list of fixture groups to (re)write: "
+                         "core,residency")
+    args = ap.parse_args()
+    if not args.reference:
+        raise SystemExit("name the reference checkout with --reference or "
+                         "STREAMLX_REFERENCE")
+    load_reference(args.reference)
+    only = set(args.only.split(",")) if args.only else {"core", "residency"}
     tmp = tempfile.mkdtemp(prefix="slx_golden_")
     try:
-        _main(tmp)
+        if "core" in only:
+            _main(tmp)
+        if "residency" in only:
+            _residency(tmp)
     finally:
         shutil.rmtree(tmp, ignore_errors=True)
+
+
+def _residency(tmp):
+    """plan_residency water-fill decisions and preload_popular warm starts
+    (streamlx/integrate.py:322-346, 476-506)."""
+    cases = []
+    # uniform widths: flips near the total expert bytes
+    for budget in (0, 5, 40, 47, 48, 60, 100):
+        cases.append(dict(layers=[0, 1, 2, 3], bpe={i: 10 for i in range(4)},
+                          n_exp={i: 12 for i in range(4)},
+                          budget=budget * 10, k=4))
+    # mixed widths (dense-first style models): partial residency
+    bpe = {0: 3, 1: 9, 2: 9, 3: 27, 4: 5}
+    n_exp = {0: 8, 1: 16, 2: 16, 3: 64, 4: 32}
+    for budget in (50, 200, 400, 700, 1500, 2300, 2600):
+        for k in (2, 8):
+            cases.append(dict(layers=[0, 1, 2, 3, 4], bpe=bpe, n_exp=n_exp,
+                              budget=budget, k=k))
+    out = []
+    for c in cases:
+        res, left = ref_int.plan_residency(c["layers"], c["bpe"], c["n_exp"],
+                                           c["budget"], c["k"])
+        out.append(dict(c, bpe={str(a): b for a, b in c["bpe"].items()},
+                        n_exp={str(a): b for a, b in c["n_exp"].items()},
+                        resident=sorted(res), left=left))
+
+    # preload_popular on a 3-layer 256-expert stack, trace axes -> layers
+    # [2, 0] (layer 1 absent from the trace), 24 slots per pool
+    cfg = synth.SynthConfig(name="golden_e256", hidden=64, layers=3,
+                            n_experts=256, top_k=10, inter=64, expert_bits=2,
+                            zipf_s=1.1)
+    d = synth.write_model(os.path.join(tmp, "e256r"), cfg, seed=3)
+    rng = np.random.default_rng(41)
+    ids = zipf_routing(256, 10, 120, 2, 1.1, 0.3, seed=42)
+    # a popularity tie among rarely used experts: the argsort order decides
+    ids[:, :, 9] = rng.integers(100, 140, size=ids.shape[:2])
+    tr = os.path.join(tmp, "warm.npz")
+    np.savez_compressed(tr, experts=ids.astype(np.uint16),
+                        seq_id=np.zeros(ids.shape[0], np.uint32),
+                        pos=np.arange(ids.shape[0], dtype=np.uint32),
+                        prompt_class=np.zeros(ids.shape[0], np.uint8))
+    with open(os.path.join(tmp, "warm.meta.json"), "w") as f:
+        json.dump({"schema_version": 1, "layer_ids": [2, 0]}, f)
+    os.environ["STREAMLX_EVICT"] = "lru"
+    index = ref_st.SafetensorsIndex(d)
+    reader = ref_reader.ExpertReader(index)
+    pools = {i: ref_pool.StreamingSwitchMLP(d, i, 24, index=index,
+                                            reader=reader) for i in range(3)}
+    n = ref_int.preload_popular(pools, tr)
+    pre = {"loaded": n,
+           "pools": {str(i): {"id2slot": [[int(a), int(b)] for a, b in
+                                          p.id2slot.items()],
+                              "free": [int(x) for x in p.free],
+                              "misses": p.misses, "hits": p.hits}
+                     for i, p in pools.items()}}
+    reader.close()
+    np.savez_compressed(os.path.join(HERE, "warm_trace.npz"),
+                        experts=ids.astype(np.uint16))
+    with open(os.path.join(HERE, "residency.json"), "w") as f:
+        json.dump({"plan_residency": out, "preload_popular": pre,
+                   "preload_layer_ids": [2, 0], "preload_slots": 24},
+                  f, indent=1, sort_keys=True)
 
 
 def _main(tmp):
