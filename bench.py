@@ -543,8 +543,10 @@ def run_ours(args) -> None:
     launches = L.LAUNCHES[0] - l0
     ht = dict(model.host_times)
     host_ms = {k_: round(1000 * v / max(ht["steps"], 1), 3)
-               for k_, v in ht.items() if k_ not in ("steps", "miss_steps")}
-    host_ms["steps_with_a_miss"] = ht["miss_steps"]
+               for k_, v in ht.items()
+               if k_ not in ("steps", "parks", "park_steps")}
+    host_ms["parks"] = ht["parks"]
+    host_ms["steps_with_a_park"] = ht["park_steps"]
     timing, ops.TIMING = ops.TIMING, None
     glu_ms, model.glu_times = model.glu_times, None
     ms = e0.elapsed_time(e1)

@@ -129,6 +129,86 @@ int slx_switchglu(const slx_expert_bank* bank, const slx_shared_expert* shared,
                   void* out, void* scratch, size_t scratch_bytes,
                   int32_t* status, void* stream);
 
+/* In-kernel slot fill of a graph-launched decode step.  Replaces, for the
+ * CUDA-graph decoder, the per-layer host round trip of
+ * streamlx/integrate.py:234-250 (host sync on the routed ids, then
+ * touch/ensure) and its hits-first overlap (streamlx/integrate.py:97-139):
+ * a layer whose routed experts all have slots never waits on the host; a
+ * layer with a miss parks in its own SwitchGLU launch until the host has run
+ * the pool bookkeeping up to that layer, and then repacks the newly read
+ * experts into their slots itself.
+ *
+ * Protocol (one decode token = one step, stamped by the host):
+ *   1. On entry, CTA 0 writes this layer's record to `log` (host-mapped):
+ *      word 1 = 1 when some routed id has no slot, word 2 = k, words
+ *      4..4+k = routed ids, 20..20+k = predicted next-layer ids, 36..36+k =
+ *      their fp32 scores (bit patterns); word 0 (written last) = the stamp.
+ *   2. If an id has no slot, CTA 0 writes park[1] = layer, park[2] = stamp
+ *      and then park[0] = ticket = (stamp << 8) | layer, and every CTA waits
+ *      (bounded by wait_ns) until the device word `release` equals the
+ *      ticket (-ticket aborts: the layer then reports
+ *      SLX_ERR_UNMAPPED_EXPERT).
+ *   3. The host writes the descriptor `desc` (slx_fill_header, then
+ *      max_items slx_fill_item, then n_table int32 of the new expert -> slot
+ *      table) and the raw MLX bytes of the experts it names into device
+ *      memory with copies on a stream of its own, and then the ticket into
+ *      `release` on that same stream.
+ *   4. The kernel repacks each item into its slot, installs the new table
+ *      into slot_table and continues with the layer.
+ * The host must not touch `desc`, `release` or the slots of this layer's
+ * pool while the layer runs, except through step 3. */
+#define SLX_FILL_LOG_WORDS 64
+#define SLX_FILL_MAX_K 16
+
+typedef struct slx_fill_header {
+  int32_t ticket;  /* must equal the parked kernel's ticket */
+  int32_t layer;
+  int32_t n_items; /* <= max_items */
+  int32_t n_table; /* == n_table of the call */
+  int32_t pad[4];
+} slx_fill_header;
+
+typedef struct slx_fill_item {
+  int32_t slot;
+  int32_t pad;
+  /* device pointers (16-byte aligned) to the expert's MLX rows: gate
+   * weight, scales, biases, up weight, scales, biases, down weight, scales,
+   * biases */
+  const void* part[9];
+} slx_fill_item;
+
+typedef struct slx_fill_service {
+  int32_t layer;          /* 0..255 */
+  int32_t max_items;      /* items the descriptor has room for */
+  const int32_t* stamp;   /* device int32: the step's stamp, < 2^23 */
+  int32_t* log;           /* host-mapped int32[SLX_FILL_LOG_WORDS] or NULL */
+  const int32_t* pred_ids;  /* device [k] next-layer prediction, or NULL */
+  const float* pred_scores; /* device [k] or NULL */
+  int32_t* park;          /* host-mapped int32[4] */
+  const int32_t* release; /* device int32 */
+  const void* desc;       /* device descriptor (see above) */
+  int32_t* go;            /* device int32 scratch word of this service */
+  int64_t wait_ns;        /* bound of the park wait */
+} slx_fill_service;
+
+/* slx_switchglu for one decode token (T = 1, scores given: combined
+ * output + shared expert) with the in-kernel slot fill described above.
+ * slot_table is written by the kernel when it parks.  Needs the fused
+ * single-launch form (SLX_ERR_UNSUPPORTED otherwise) and k <=
+ * SLX_FILL_MAX_K. */
+int slx_switchglu_serviced(const slx_expert_bank* bank,
+                           const slx_shared_expert* shared, const void* x,
+                           int k, const int32_t* ids, const float* scores,
+                           int32_t* slot_table, int n_table, void* out,
+                           void* scratch, size_t scratch_bytes,
+                           int32_t* status, const slx_fill_service* svc,
+                           void* stream);
+
+/* Device address of page-locked host memory (cudaHostGetDevicePointer):
+ * the `log` and `park` words of slx_fill_service live in host memory that
+ * the kernel writes.  Returns SLX_ERR_CUDA if `host` is not mapped. */
+int slx_host_device_ptr(const void* host, void** dev);
+
 /* Decode calls (T == 1) of slx_switchglu run both phases in one cooperative
  * launch when the token's tiles fit one CTA per SM; the first 256 bytes of
  * the scratch hold that launch's grid-barrier words and must be zero before

@@ -37,7 +37,14 @@ EXPORTS = (
     "slx_router_topk_multi", "slx_set_pdl", "slx_pread_many",
     "slx_set_switchglu_fused", "slx_switchglu_last_kernels",
     "slx_prefill_scratch_bytes", "slx_prefill_grouped",
+    "slx_switchglu_serviced", "slx_host_device_ptr",
 )
+
+# slx_fill_service layout constants (include/streamlx_cuda.h)
+FILL_LOG_WORDS = 64
+FILL_MAX_K = 16
+FILL_HEADER_BYTES = 32
+FILL_ITEM_BYTES = 80
 
 
 class slx_qmat(C.Structure):
@@ -70,6 +77,15 @@ LAUNCHES = [0]
 
 def _count(n: int = 1) -> None:
     LAUNCHES[0] += n
+
+
+class slx_fill_service(C.Structure):
+    _fields_ = [("layer", C.c_int32), ("max_items", C.c_int32),
+                ("stamp", C.c_void_p), ("log", C.c_void_p),
+                ("pred_ids", C.c_void_p), ("pred_scores", C.c_void_p),
+                ("park", C.c_void_p), ("release", C.c_void_p),
+                ("desc", C.c_void_p), ("go", C.c_void_p),
+                ("wait_ns", C.c_int64)]
 
 
 class slx_router_head(C.Structure):
@@ -156,6 +172,13 @@ def lib() -> C.CDLL:
         L.slx_copy_many.argtypes = [vp, vp, vp, i32, vp]
         L.slx_prefill_scratch_bytes.restype = sz
         L.slx_prefill_scratch_bytes.argtypes = [i32, i32, i32, i32]
+        L.slx_switchglu_serviced.restype = i32
+        L.slx_switchglu_serviced.argtypes = [
+            C.POINTER(slx_expert_bank), C.POINTER(slx_shared_expert), vp,
+            i32, vp, vp, vp, i32, vp, vp, sz, vp,
+            C.POINTER(slx_fill_service), vp]
+        L.slx_host_device_ptr.restype = i32
+        L.slx_host_device_ptr.argtypes = [vp, C.POINTER(vp)]
         L.slx_prefill_grouped.restype = i32
         L.slx_prefill_grouped.argtypes = [C.POINTER(slx_expert_bank), vp, i32,
                                           vp, i32, vp, i32, vp, vp, i32, vp,
@@ -268,6 +291,33 @@ def switchglu(bank: slx_expert_bank, x: torch.Tensor, ids: torch.Tensor,
         status.data_ptr(), stream_ptr(stream))
     _check("slx_switchglu", rc)
     _count(lib().slx_switchglu_last_kernels())
+
+
+def switchglu_serviced(bank: slx_expert_bank, x: torch.Tensor,
+                       ids: torch.Tensor, scores: torch.Tensor,
+                       slot_table: torch.Tensor, out: torch.Tensor,
+                       scratch: torch.Tensor, status: torch.Tensor,
+                       svc: slx_fill_service,
+                       shared: slx_shared_expert | None = None,
+                       stream: torch.cuda.Stream | None = None) -> None:
+    """One decode token's SwitchGLU with the in-kernel slot fill."""
+    k = ids.shape[-1]
+    rc = lib().slx_switchglu_serviced(
+        C.byref(bank), C.byref(shared) if shared is not None else None,
+        x.data_ptr(), k, ids.data_ptr(), scores.data_ptr(),
+        slot_table.data_ptr(), int(slot_table.numel()), out.data_ptr(),
+        scratch.data_ptr(), scratch.numel() * scratch.element_size(),
+        status.data_ptr(), C.byref(svc), stream_ptr(stream))
+    _check("slx_switchglu_serviced", rc)
+    _count(1)
+
+
+def host_device_ptr(host_ptr: int) -> int:
+    """Device address of page-locked host memory."""
+    out = C.c_void_p()
+    rc = lib().slx_host_device_ptr(host_ptr, C.byref(out))
+    _check("slx_host_device_ptr", rc)
+    return int(out.value or 0)
 
 
 def qlinear(w_tiled: torch.Tensor, out_features: int, in_features: int,

@@ -135,12 +135,60 @@ int slx_pack_dense(const slx_qmat* w, int out_features, int in_features,
   return rc ? cuda_check(rc, "slx_pack_dense") : SLX_OK;
 }
 
+static int switchglu_impl(const slx_expert_bank* bank,
+                          const slx_shared_expert* shared, const void* x,
+                          int T, int k, const int32_t* ids, const float* scores,
+                          const int32_t* slot_table, int n_table, void* out,
+                          void* scratch, size_t scratch_bytes, int32_t* status,
+                          void* stream, const slx_fill_service* svc);
+
 int slx_switchglu(const slx_expert_bank* bank, const slx_shared_expert* shared,
                   const void* x, int T, int k, const int32_t* ids,
                   const float* scores, const int32_t* slot_table, int n_table,
                   void* out, void* scratch, size_t scratch_bytes,
                   int32_t* status, void* stream) {
   g_err.clear();
+  return switchglu_impl(bank, shared, x, T, k, ids, scores, slot_table,
+                        n_table, out, scratch, scratch_bytes, status, stream,
+                        nullptr);
+}
+
+int slx_switchglu_serviced(const slx_expert_bank* bank,
+                           const slx_shared_expert* shared, const void* x,
+                           int k, const int32_t* ids, const float* scores,
+                           int32_t* slot_table, int n_table, void* out,
+                           void* scratch, size_t scratch_bytes,
+                           int32_t* status, const slx_fill_service* svc,
+                           void* stream) {
+  g_err.clear();
+  if (!svc) return fail(SLX_ERR_INVALID, "switchglu_serviced: svc is NULL");
+  if (!scores || !slot_table)
+    return fail(SLX_ERR_INVALID, "switchglu_serviced: scores and slot_table "
+                "are required");
+  if (k < 1 || k > SLX_FILL_MAX_K)
+    return fail(SLX_ERR_UNSUPPORTED, "switchglu_serviced: k %d (1..%d)", k,
+                SLX_FILL_MAX_K);
+  if (svc->layer < 0 || svc->layer > 255 || svc->max_items < 0)
+    return fail(SLX_ERR_INVALID, "switchglu_serviced: layer %d max_items %d",
+                svc->layer, svc->max_items);
+  if (!svc->stamp || !svc->park || !svc->release || !svc->desc || !svc->go ||
+      !aligned16(svc->desc) || svc->wait_ns <= 0)
+    return fail(SLX_ERR_INVALID, "switchglu_serviced: NULL/misaligned "
+                "service pointer or wait_ns <= 0");
+  if ((svc->pred_ids == nullptr) != (svc->pred_scores == nullptr))
+    return fail(SLX_ERR_INVALID, "switchglu_serviced: pred_ids and "
+                "pred_scores go together");
+  return switchglu_impl(bank, shared, x, 1, k, ids, scores, slot_table,
+                        n_table, out, scratch, scratch_bytes, status, stream,
+                        svc);
+}
+
+static int switchglu_impl(const slx_expert_bank* bank,
+                          const slx_shared_expert* shared, const void* x,
+                          int T, int k, const int32_t* ids, const float* scores,
+                          const int32_t* slot_table, int n_table, void* out,
+                          void* scratch, size_t scratch_bytes, int32_t* status,
+                          void* stream, const slx_fill_service* svc) {
   if (!bank) return fail(SLX_ERR_INVALID, "slx_switchglu: bank is NULL");
   const int H = bank->hidden, I = bank->inter, bits = bank->bits;
   if (bits != 2 && bits != 4 && bits != 8)
@@ -237,18 +285,21 @@ int slx_switchglu(const slx_expert_bank* bank, const slx_shared_expert* shared,
   d.n_units = k + (Is > 0 ? 1 : 0);
   d.pdl = 1;
   int rc = SLX_ERR_UNSUPPORTED;
-  if (g_fused && T == 1) {
+  if ((g_fused || svc) && T == 1) {
     // one cooperative launch for both phases when the token's tiles fit
     d.tile_bytes = (int)slx::single_tile_bytes(I, bits);
     d.tile_bytes_sh = Is ? (int)slx::single_tile_bytes(Is, bits) : 0;
     d.a_bytes = (long long)slx::expert_a_bytes(H, I, bits);
     d.a_bytes_sh = Is ? (long long)slx::expert_a_bytes(H, Is, bits) : 0;
-    rc = slx::launch_switchglu_fused(a, d, gbar, bits, s);
+    rc = slx::launch_switchglu_fused(a, d, gbar, bits, s, svc);
     if (rc != SLX_ERR_UNSUPPORTED) {
       g_glu_kernels = rc ? 0 : 1;
       return rc ? cuda_check(rc, "slx_switchglu fused") : SLX_OK;
     }
   }
+  if (svc)
+    return fail(SLX_ERR_UNSUPPORTED, "switchglu_serviced: the token's tiles "
+                "do not fit the single-launch form");
   g_glu_kernels = 0;
   rc = slx::launch_gemv(a, bits, s, /*pdl_secondary=*/true);
   if (rc) return cuda_check(rc, "slx_switchglu gate/up");
@@ -258,6 +309,19 @@ int slx_switchglu(const slx_expert_bank* bank, const slx_shared_expert* shared,
 }
 
 int slx_switchglu_last_kernels(void) { return g_glu_kernels; }
+
+int slx_host_device_ptr(const void* host, void** dev) {
+  g_err.clear();
+  if (!host || !dev) return fail(SLX_ERR_INVALID, "host_device_ptr: NULL");
+  const cudaError_t e =
+      cudaHostGetDevicePointer(dev, const_cast<void*>(host), 0);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(SLX_ERR_CUDA, "cudaHostGetDevicePointer: %s",
+                cudaGetErrorString(e));
+  }
+  return SLX_OK;
+}
 
 size_t slx_prefill_scratch_bytes(int n_blocks, int hidden, int inter,
                                  int bits) {

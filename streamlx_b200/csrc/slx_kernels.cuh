@@ -83,7 +83,8 @@ struct RouterArgs {
 int launch_gemv(GemvArgs a, int bits, cudaStream_t stream, bool pdl_secondary);
 int launch_down(DownArgs a, int bits, cudaStream_t stream);
 int launch_switchglu_fused(const GemvArgs& a, const DownArgs& d, void* bar,
-                           int bits, cudaStream_t stream);
+                           int bits, cudaStream_t stream,
+                           const slx_fill_service* svc = nullptr);
 int launch_dequant_rows(const uint32_t* w, const uint16_t* s, const uint16_t* b,
                         int in, int bits, int gs, const int32_t* rows,
                         int nrows, int n_src_rows, void* out, int out_bf16,

@@ -33,6 +33,7 @@
 // so no dequantised weight is ever materialised.
 // Every mbarrier wait is bounded (slx_common.cuh: mbar_wait).
 #include "slx_kernels.cuh"
+#include "slx_pack.cuh"
 #include "slx_tiles.cuh"
 
 #ifdef SLX_TRACE
@@ -64,7 +65,9 @@ SLX_DEV int lookup_slot(const int32_t* ids, int u, const int32_t* table,
                         int n_table, int n_slots) {
   const int e = ids[u];
   int s = e;
-  if (table) s = (e >= 0 && e < n_table) ? table[e] : -1;
+  // L2 read: a decode launch may rewrite the table while it runs (the
+  // in-kernel slot fill), so no L1 line of it may be reused across that
+  if (table) s = (e >= 0 && e < n_table) ? __ldcg(table + e) : -1;
   return (s >= 0 && s < n_slots) ? s : -1;
 }
 
@@ -689,6 +692,19 @@ struct FusedArgs {
   int stage_a, stage_b;  // bytes per A / B tile slot
   int b_late;            // down tiles share the gate/up slots: request them
                          // once phase A is done (they load during the barrier)
+  // in-kernel slot fill of graph-launched decode (slx_fill_service); off
+  // (svc_on = 0) for plain calls
+  int svc_on, svc_layer, svc_max_items;
+  const int32_t* svc_stamp;
+  int32_t* svc_log;
+  const int32_t* svc_pred_ids;
+  const float* svc_pred_scores;
+  int32_t* svc_park;
+  const int32_t* svc_release;
+  const uint8_t* svc_desc;
+  int32_t* svc_go;
+  int32_t* svc_table;
+  long long svc_wait_ns;
 };
 
 SLX_DEV unsigned long long ld_acquire_u64(const unsigned long long* p) {
@@ -706,19 +722,159 @@ SLX_DEV void red_release_add_u64(unsigned long long* p, unsigned long long v) {
 // complete), add one each with a release reduction (no reply to wait for,
 // unlike a returning atomic), and wait until it reaches (n + 1) * nblocks.
 SLX_DEV bool grid_barrier(unsigned long long* cnt, int nblocks,
-                          int32_t* status) {
+                          int32_t* status,
+                          unsigned long long limit_ns = kWaitLimitNs) {
   const unsigned long long nb = (unsigned long long)nblocks;
   const unsigned long long v = ld_acquire_u64(cnt);
   const unsigned long long target = v - v % nb + nb;
   red_release_add_u64(cnt, 1ull);
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 0; ld_acquire_u64(cnt) < target; ++i) {
-    if ((i & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+    if ((i & 63u) == 0 && globaltimer_ns() - t0 > limit_ns) {
       set_status(status, SLX_ERR_DEVICE_TIMEOUT);
       return false;
     }
+    if (i > 4096) __nanosleep(128);   // a long wait (a parked layer) polls gently
   }
   return true;
+}
+
+// ------------------------------------------------ in-kernel slot fill ---
+//
+// slx_fill_service protocol (include/streamlx_cuda.h): the layer record
+// goes to the host on entry; a layer with an unmapped routed expert parks
+// until the host's copy stream has landed the descriptor, the raw expert
+// bytes and the release ticket, then every CTA repacks a share of the
+// items into their slots and the new expert -> slot table is installed
+// before any weight tile is requested.
+
+SLX_DEV int ld_volatile_s32(const int32_t* p) {
+  int v;
+  asm volatile("ld.volatile.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+SLX_DEV void svc_write_log(const FusedArgs& f, const GemvArgs& a, int need) {
+  volatile int32_t* L = f.svc_log;
+  if (!L) return;
+  const int stamp = ld_volatile_s32(f.svc_stamp);
+  L[1] = need;
+  L[2] = a.k;
+  for (int j = 0; j < a.k; ++j) {
+    L[4 + j] = a.ids[j];
+    L[20 + j] = f.svc_pred_ids ? f.svc_pred_ids[j] : -1;
+    L[36 + j] = f.svc_pred_scores ? __float_as_int(f.svc_pred_scores[j]) : 0;
+  }
+  __threadfence_system();
+  L[0] = stamp;
+  __threadfence_system();
+}
+
+// Every thread of every CTA calls this after the CTA agreed that some routed
+// id of this launch has no slot.
+template <int BITS>
+SLX_DEV void svc_fill(const FusedArgs& f, const GemvArgs& a) {
+  __shared__ int s_ok;
+  __shared__ __align__(16) slx_fill_item s_item;
+  __shared__ int s_nitems;
+  const int stamp = ld_volatile_s32(f.svc_stamp);
+  const int ticket = (int)(((unsigned)stamp << 8) | (unsigned)f.svc_layer);
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    volatile int32_t* P = f.svc_park;
+    P[1] = f.svc_layer;
+    P[2] = stamp;
+    __threadfence_system();
+    P[0] = ticket;
+    __threadfence_system();
+    const uint64_t t0 = globaltimer_ns();
+    int v = 0;
+    for (uint32_t i = 0;; ++i) {
+      v = ld_volatile_s32(f.svc_release);
+      if (v == ticket || v == -ticket) break;
+      if ((i & 15u) == 0 && globaltimer_ns() - t0 > (uint64_t)f.svc_wait_ns) {
+        v = 0;
+        break;
+      }
+      __nanosleep(256);
+    }
+    *reinterpret_cast<volatile int32_t*>(f.svc_go) = v == ticket ? ticket : -ticket;
+    if (v != ticket)
+      set_status(a.status, v == 0 ? SLX_ERR_DEVICE_TIMEOUT : SLX_ERR_UNMAPPED_EXPERT);
+  }
+  __syncthreads();
+  // every CTA arrives at once; CTA 0 only after the release (or timeout)
+  if (threadIdx.x == 0) {
+    grid_barrier(f.bar, gridDim.x, a.status,
+                 (unsigned long long)f.svc_wait_ns + kWaitLimitNs);
+    s_ok = ld_volatile_s32(f.svc_go) == ticket;
+    s_nitems = 0;
+    if (s_ok) {
+      const slx_fill_header* h =
+          reinterpret_cast<const slx_fill_header*>(f.svc_desc);
+      const int n = __ldcg(&h->n_items);
+      if (__ldcg(&h->ticket) != ticket || __ldcg(&h->layer) != f.svc_layer ||
+          n < 0 || n > f.svc_max_items || __ldcg(&h->n_table) != a.n_table) {
+        set_status(a.status, SLX_ERR_INVALID);
+        s_ok = 0;
+      } else {
+        s_nitems = n;
+      }
+    }
+  }
+  __syncthreads();
+  if (s_ok) {
+    const int H = a.in, I = a.I;
+    const int na = I / 16, tpe = na + H / 16;
+    const slx_fill_item* items = reinterpret_cast<const slx_fill_item*>(
+        f.svc_desc + sizeof(slx_fill_header));
+    const int32_t* tab = reinterpret_cast<const int32_t*>(
+        f.svc_desc + sizeof(slx_fill_header) +
+        (size_t)f.svc_max_items * sizeof(slx_fill_item));
+    const int jobs = s_nitems * tpe;
+    for (int job = blockIdx.x; job < jobs; job += gridDim.x) {
+      const int it = job / tpe, t = job % tpe;
+      if (threadIdx.x < (int)(sizeof(slx_fill_item) / 16))
+        reinterpret_cast<uint4*>(&s_item)[threadIdx.x] =
+            __ldcg(reinterpret_cast<const uint4*>(items + it) + threadIdx.x);
+      __syncthreads();
+      bool good = s_item.slot >= 0 && s_item.slot < a.n_slots;
+      for (int p = 0; p < 9; ++p)
+        good &= s_item.part[p] != nullptr &&
+                (reinterpret_cast<uintptr_t>(s_item.part[p]) & 15u) == 0;
+      if (good) {
+        uint8_t* dst = const_cast<uint8_t*>(a.bank) +
+                       (size_t)s_item.slot * a.slot_stride;
+        const QSrc G = {(const uint8_t*)s_item.part[0],
+                        (const uint16_t*)s_item.part[1],
+                        (const uint16_t*)s_item.part[2]};
+        const QSrc U = {(const uint8_t*)s_item.part[3],
+                        (const uint16_t*)s_item.part[4],
+                        (const uint16_t*)s_item.part[5]};
+        const QSrc D = {(const uint8_t*)s_item.part[6],
+                        (const uint16_t*)s_item.part[7],
+                        (const uint16_t*)s_item.part[8]};
+        if (t < na)
+          pack_pair(dst + (size_t)t * pair_tile_bytes(H, BITS), G, 16 * t, U,
+                    16 * t, I, H, BITS);
+        else
+          pack_single(dst + expert_a_bytes(H, I, BITS) +
+                          (size_t)(t - na) * single_tile_bytes(I, BITS),
+                      D, 16 * (t - na), I, BITS);
+      } else if (threadIdx.x == 0 && t == 0) {
+        set_status(a.status, SLX_ERR_INVALID);
+      }
+      __syncthreads();  // s_item is reused by the next job
+    }
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.n_table;
+         i += gridDim.x * blockDim.x)
+      f.svc_table[i] = __ldcg(tab + i);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) grid_barrier(f.bar, gridDim.x, a.status);
+  __syncthreads();
+  // the slots were written through the generic proxy; the weight tiles are
+  // read by bulk copies (async proxy)
+  asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
 // One 64-column group of a 16-row down tile: per-row partial (lanes with
@@ -779,6 +935,19 @@ __global__ void __launch_bounds__(kFThreads, 1)
   __syncthreads();
   pdl_wait_primary();
   SLX_TRACE_POINT(0, 0);
+
+  if (f.svc_on) {
+    __shared__ int s_need;
+    if (threadIdx.x == 0) {
+      int need = 0;
+      for (int j = 0; j < a.k; ++j)
+        need |= lookup_slot(a.ids, j, a.slot_table, a.n_table, a.n_slots) < 0;
+      s_need = need;
+      if (bid == 0) svc_write_log(f, a, need);
+    }
+    __syncthreads();
+    if (s_need) svc_fill<BITS>(f, a);
+  }
 
   if (warp == 0) {
     // ---- every weight request of this CTA, up front ----
@@ -1043,12 +1212,28 @@ static int launch_fused_t(FusedArgs f, cudaStream_t stream) {
 }
 
 int launch_switchglu_fused(const GemvArgs& a, const DownArgs& d, void* bar,
-                           int bits, cudaStream_t stream) {
+                           int bits, cudaStream_t stream,
+                           const slx_fill_service* svc) {
   if (a.T != 1 || d.T != 1) return SLX_ERR_UNSUPPORTED;
   FusedArgs f = {};
   f.a = a;
   f.d = d;
   f.bar = reinterpret_cast<unsigned long long*>(bar);
+  if (svc) {
+    f.svc_on = 1;
+    f.svc_layer = svc->layer;
+    f.svc_max_items = svc->max_items;
+    f.svc_stamp = svc->stamp;
+    f.svc_log = svc->log;
+    f.svc_pred_ids = svc->pred_ids;
+    f.svc_pred_scores = svc->pred_scores;
+    f.svc_park = svc->park;
+    f.svc_release = svc->release;
+    f.svc_desc = reinterpret_cast<const uint8_t*>(svc->desc);
+    f.svc_go = svc->go;
+    f.svc_table = const_cast<int32_t*>(a.slot_table);
+    f.svc_wait_ns = (long long)svc->wait_ns;
+  }
   switch (bits) {
     case 2: f.a.tile_bytes = (int)pair_tile_bytes(a.in, 2); break;
     case 4: f.a.tile_bytes = (int)pair_tile_bytes(a.in, 4); break;

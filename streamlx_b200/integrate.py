@@ -474,8 +474,9 @@ def load_streaming_model(model_dir: str, budget_bytes: int, k: int = 8,
         pool = StreamingSwitchMLP(model_dir, i, slots, index=index,
                                   reader=reader, device=model.device)
         if i in res_layers:   # fully resident: fill every slot once
-            pool.begin_call()
-            pool.ensure(list(range(n_exp[i])))
+            for e0 in range(0, n_exp[i], 32):   # reads of <= 32 experts
+                pool.begin_call()
+                pool.ensure(list(range(e0, min(e0 + 32, n_exp[i]))))
         model.layers[i].mlp.switch_mlp = StreamingSwitchGLU(
             pool, model.layers[i].mlp.shared_struct())
         pools[i] = pool

@@ -157,19 +157,16 @@ class SynthDecoder:
                                       device=dev)
         self.n_pos = 0
         self.use_graphs = cfg.has_trunk
-        self.pipeline = True
         self.pdl = True             # captured kernels chain with PDL
         self.glu_events = True      # time sampled SwitchGLU pairs in graphs
         self._graphs = None
-        self._pending = None
-        self._pf_done = 0
         self.glu_times: list | None = None
         # host seconds per phase of the graph-launched step (launch, the
         # previous step's deferred bookkeeping, waiting for the device log)
-        self.host_times = {"launch": 0.0, "bookkeeping": 0.0, "wait": 0.0,
-                           "miss_path": 0.0, "miss_replay": 0.0,
-                           "miss_relaunch": 0.0, "miss_wait": 0.0,
-                           "tail": 0.0, "steps": 0, "miss_steps": 0}
+        self.host_times = {"launch": 0.0, "serve": 0.0, "bookkeeping": 0.0,
+                           "park_serve": 0.0, "flush": 0.0, "steps": 0,
+                           "parks": 0, "park_steps": 0}
+        self._step_active = False
         # temporal-reuse routing override of the workloads: per (token,
         # layer) a seeded coin decides whether the previous token's expert
         # set is kept (applied identically to the CPU oracle)
@@ -236,11 +233,11 @@ class SynthDecoder:
         """One decode step for the token id in `token` (device int32 [1]);
         returns the greedy next token (device int32 [1]).
 
-        With ``use_graphs`` the step runs as captured CUDA graphs and the
-        pool bookkeeping follows from the device log (_step_graph); with
-        ``pipeline`` the bookkeeping of a step that needed no slot fill is
-        deferred to the next call (or flush()), where it overlaps that
-        call's device work."""
+        With ``use_graphs`` the step runs as one captured CUDA graph whose
+        layers report their routing to the host as they run; the host keeps
+        the pool bookkeeping in step and serves layers that park on a miss
+        (_step_graph).  Otherwise the step runs layer by layer with one host
+        sync on the routed ids per layer (_step_eager)."""
         if self.use_graphs and all(
                 hasattr(la.mlp.switch_mlp, "route") for la in self.layers):
             return self._step_graph(token)
@@ -289,24 +286,30 @@ class SynthDecoder:
 
     # ----------------------------------------------------- graph decode --
     #
-    # A decode step runs as one CUDA graph per layer plus a tail graph, with
-    # no host sync between layers.  The host then replays every layer's pool
-    # bookkeeping from a device log (routed ids, next-layer prediction), in
-    # layer order, through the wrapper's route() -- the same calls, in the
-    # same order, as the eager path, so the hit/miss/eviction trace is the
-    # same.  A layer computed correctly iff every routed expert had a slot
-    # when its SwitchGLU ran (the kernel reads only routed experts, and a
-    # resident expert never changes slot); otherwise the kernel reported
-    # SLX_ERR_UNMAPPED_EXPERT for that layer, and after its replay has
-    # filled the slots that layer and every later one run again.  Each
-    # layer reads the previous layer's residual and MoE output from
-    # per-layer buffers, so a rerun from layer l sees exactly its inputs.
+    # A decode step is one CUDA graph of every layer plus the tail.  Each
+    # layer's SwitchGLU launch (slx_switchglu_serviced) first reports the
+    # layer's routed ids and its next-layer prediction through host-mapped
+    # memory; if one of its routed experts has no slot it parks until the
+    # host has served it (fill_service.py).  The host follows the records in
+    # layer order while the step runs: it starts each layer's next-layer
+    # prefetch, replays the layer's pool bookkeeping through the wrapper's
+    # route() -- the same calls, in the same order, as the eager path, so the
+    # hit/miss/eviction trace is the reference's -- and serves parked layers
+    # with their slot fills.  Fills of layers that did not park (the device
+    # already computed them with slots that were still valid) are recorded
+    # and applied between steps.  A layer is computed correctly because its
+    # kernel only reads slots whose table entry and bytes were installed
+    # together (between steps, or by the kernel itself after a park).
 
-    _UNMAPPED = -5
+    WAIT_S = 30.0       # bound of a parked layer's wait for its service
 
     def _graph_buffers(self) -> None:
+        from .fill_service import FillService
         cfg, dev = self.cfg, self.device
         n, k, H = cfg.layers, cfg.top_k, cfg.hidden
+        if k > L.FILL_MAX_K:
+            raise ValueError(f"top_k {k} > {L.FILL_MAX_K}: graph decode "
+                             "needs the eager path")
         bf = torch.bfloat16
         self.g_s = torch.zeros(n, 1, H, dtype=bf, device=dev)
         self.g_m = torch.zeros(n, 1, H, dtype=bf, device=dev)
@@ -314,43 +317,55 @@ class SynthDecoder:
         self.g_xm = torch.zeros(n, 1, H, dtype=bf, device=dev)  # MoE input
         self.g_emb = torch.zeros(1, H, dtype=bf, device=dev)
         self.g_fin = torch.zeros(1, H, dtype=bf, device=dev)
-        # device log, read back with one copy per launch cycle:
-        # ids [n,k] | pred ids [n,k] | pred scores [n,k] f32 | layer status
-        # [n] | status | next token
-        words = 3 * n * k + n + 2
-        self.g_log = torch.zeros(words, dtype=torch.int32, device=dev)
-        self.g_log_host = torch.zeros(words, dtype=torch.int32).pin_memory()
-        o = 0
-        self.g_ids = self.g_log[o:o + n * k].view(n, 1, k)
-        o += n * k
-        self.g_pf_ids = self.g_log[o:o + n * k].view(n, 1, k)
-        o += n * k
-        self.g_pf_scores = self.g_log[o:o + n * k].view(torch.float32) \
-            .view(n, 1, k)
-        o += n * k
-        self._lst_off = o
-        self.g_lstatus = self.g_log[o:o + n]
-        o += n
-        self.g_status = self.g_log[o:o + 1]
-        self.g_tok_out = self.g_log[o + 1:o + 2]
+        self.g_ids = torch.zeros(n, 1, k, dtype=torch.int32, device=dev)
+        self.g_pf_ids = torch.zeros(n, 1, k, dtype=torch.int32, device=dev)
+        self.g_pf_scores = torch.zeros(n, 1, k, dtype=torch.float32,
+                                       device=dev)
+        # device log read back once per step: layer status [n] | status |
+        # next token
+        self.g_log = torch.zeros(n + 2, dtype=torch.int32, device=dev)
+        self.g_log_host = torch.zeros(n + 2, dtype=torch.int32).pin_memory()
+        self.g_lstatus = self.g_log[0:n]
+        self.g_status = self.g_log[n:n + 1]
+        self.g_tok_out = self.g_log[n + 1:n + 2]
         self.g_scores = torch.zeros(n, 1, k, dtype=torch.float32, device=dev)
         self.g_prev_ids = torch.zeros(n, 1, k, dtype=torch.int32, device=dev)
-        # control, written with one copy per step: pos | force[n] | token
-        self.g_ctrl = torch.zeros(n + 2, dtype=torch.int32, device=dev)
-        self.g_ctrl_host = torch.zeros(n + 2, dtype=torch.int32).pin_memory()
+        # control, written with one copy per step:
+        # pos | force[n] | token | stamp
+        self.g_ctrl = torch.zeros(n + 3, dtype=torch.int32, device=dev)
+        self.g_ctrl_host = torch.zeros(n + 3, dtype=torch.int32).pin_memory()
         sh = [la.mlp.switch_mlp.shared for la in self.layers]
         s_inter = max([x[2] for x in sh if x] or [0])
         self.g_glu_scratch = torch.zeros(
             L.switchglu_scratch_bytes(1, k, cfg.inter, s_inter),
             dtype=torch.uint8, device=dev)
-        self._side = torch.cuda.Stream(device=dev)   # predictor branch
+        pools = [la.mlp.switch_mlp.pool for la in self.layers]
+        max_slots = max(p.n_slots for p in pools)
+        topm = max(p._PF_TOPM for p in pools)
+        # a parked layer receives its pool's fills since the last step: its
+        # own misses and prefetch adoptions (bounded by the pool size)
+        max_items = min(max_slots, max(4 * (k + topm), 32))
+        stride = max(p.store.stride for p in pools)
+        staging = min(max_items * stride * 2, 2 << 30)
+        self.svc = FillService(n, cfg.n_experts, max_items, staging, dev,
+                               wait_s=self.WAIT_S)
+        self._stamp = 0
         self.g_ev = [(torch.cuda.Event(enable_timing=True),
                       torch.cuda.Event(enable_timing=True)) for _ in range(n)]
         for pair in self.g_ev:      # torch creates the CUDA event on first use
             for e in pair:
                 e.record()
+        self._ev_done = torch.cuda.Event()
 
-    def _record_layer(self, i: int, join: bool = True) -> None:
+    def _pred_on(self, i: int) -> bool:
+        """Layer i computes the next-layer prediction in its router launch:
+        it has a prefetch link and the next pool's agreement gate is open
+        (the reference stops predicting below 55% agreement,
+        streamlx/integrate.py:76-77)."""
+        blk = self.layers[i].mlp
+        return blk.pf_link is not None and blk.switch_mlp.pred_gate()
+
+    def _record_layer(self, i: int, serviced: bool = True) -> None:
         cfg = self.cfg
         n, k, H, bits = cfg.layers, cfg.top_k, cfg.hidden, cfg.trunk_bits
         la = self.layers[i]
@@ -378,53 +393,44 @@ class SynthDecoder:
         xm = self.g_xm[i]
         L.add_rmsnorm_out(self.g_s[i], self.o, la.post_attention_layernorm,
                           eps, self.g_m[i], xm)
-        L.router_topk_multi(
-            xm, [L.router_head(blk.w_gate, blk.bias, self.g_ids[i],
+        heads = [L.router_head(blk.w_gate, blk.bias, self.g_ids[i],
                                self.g_scores[i], blk.scratch,
                                force=self.g_ctrl[1 + i:2 + i],
-                               forced_ids=self.g_prev_ids[i])],
-            cfg.n_experts, k, cfg.norm_topk_prob, self.g_status)
-        if blk.pf_link is not None:
-            # the next-layer predictor only feeds the host's prefetch: it
-            # runs on a side branch, off the layer's critical path
+                               forced_ids=self.g_prev_ids[i])]
+        pred = self._pred_on(i)
+        if pred:
+            # the next-layer predictor shares the router launch (same input)
             ratio, nxt = blk.pf_link
-            cur = torch.cuda.current_stream(self.device)
-            self._side.wait_stream(cur)
-            self._forked = True
-            prev = L.set_pdl(False)
-            try:
-                with torch.cuda.stream(self._side):
-                    L.router_topk_multi(
-                        xm, [L.router_head(nxt.w_gate, nxt.bias,
-                                           self.g_pf_ids[i],
-                                           self.g_pf_scores[i],
-                                           blk.pf_scratch, ratio=ratio)],
-                        cfg.n_experts, k, cfg.norm_topk_prob, self.g_status)
-            finally:
-                L.set_pdl(prev)
+            heads.append(L.router_head(nxt.w_gate, nxt.bias,
+                                       self.g_pf_ids[i], self.g_pf_scores[i],
+                                       blk.pf_scratch, ratio=ratio))
+        L.router_topk_multi(xm, heads, cfg.n_experts, k, cfg.norm_topk_prob,
+                            self.g_status)
         pool = w.pool
         sh = w.shared
         ev = self.g_ev[i]
         timed = self._glu_timed(i)
         if timed:
             L.event_record_external(ev[0])
-        ops.switchglu(pool.store.bank, xm, self.g_ids[i], k,
-                      scores=self.g_scores[i], table=pool.store.table_dev,
-                      shared=sh[0] if sh else None, out=self.g_d[i],
-                      inter=pool.inter, shared_inter=sh[2] if sh else 0,
-                      scratch_buf=self.g_glu_scratch,
-                      status=self.g_lstatus[i:i + 1])
+        if serviced:
+            stamp = self.g_ctrl.data_ptr() + 4 * (n + 2)
+            svc = self.svc.svc(i, stamp,
+                               self.g_pf_ids[i] if pred else None,
+                               self.g_pf_scores[i] if pred else None)
+            L.switchglu_serviced(pool.store.bank, xm, self.g_ids[i],
+                                 self.g_scores[i], pool.store.table_dev,
+                                 self.g_d[i], self.g_glu_scratch,
+                                 self.g_lstatus[i:i + 1], svc,
+                                 shared=sh[0] if sh else None)
+        else:
+            ops.switchglu(pool.store.bank, xm, self.g_ids[i], k,
+                          scores=self.g_scores[i], table=pool.store.table_dev,
+                          shared=sh[0] if sh else None, out=self.g_d[i],
+                          inter=pool.inter, shared_inter=sh[2] if sh else 0,
+                          scratch_buf=self.g_glu_scratch,
+                          status=self.g_lstatus[i:i + 1])
         if timed:
             L.event_record_external(ev[1])
-        if join:
-            self._join_side()
-
-    def _join_side(self) -> None:
-        """Rejoin the predictor branch (only if this recording forked it:
-        a capture may not wait on work from outside itself)."""
-        if getattr(self, "_forked", False):
-            torch.cuda.current_stream(self.device).wait_stream(self._side)
-            self._forked = False
 
     def _record_tail(self) -> None:
         cfg = self.cfg
@@ -439,13 +445,14 @@ class SynthDecoder:
                     [self.g_log.numel() * 4])
 
     def _capture(self) -> None:
-        """Capture the per-layer graphs, the tail graph and one graph of the
-        whole step (used when a step starts at layer 0)."""
+        """Capture the graph of one whole step."""
         if not hasattr(self, "g_log"):
             self._graph_buffers()
+        self.flush()
         n = self.cfg.layers
-        # the initialising pass below really runs: point it at the position
-        # the next step overwrites anyway, not forced, token 0
+        # the initialising pass below really runs (without the slot fill):
+        # point it at the position the next step overwrites anyway, not
+        # forced, token 0
         ch = self.g_ctrl_host.numpy()
         ch[:] = 0
         ch[0] = min(self.n_pos, self.max_len - 1)
@@ -457,233 +464,196 @@ class SynthDecoder:
         # (function attributes, lazy module loads) outside the capture
         with torch.cuda.stream(s):
             for i in range(n):
-                self._record_layer(i)
+                self._record_layer(i, serviced=False)
             self._record_tail()
         s.synchronize()
-        mode = "thread_local"
+        self._pred_flags = [self._pred_on(i) for i in range(n)]
         prev_pdl = L.set_pdl(self.pdl)
         try:
-            graphs, tail, full = self._capture_graphs(s, mode)
+            full = torch.cuda.CUDAGraph()
+            c0 = L.LAUNCHES[0]
+            with torch.cuda.graph(full, stream=s,
+                                  capture_error_mode="thread_local"):
+                self.g_lstatus.zero_()
+                for i in range(n):
+                    self._record_layer(i)
+                self._record_tail()
+            self._kernels_full = L.LAUNCHES[0] - c0
         finally:
             L.set_pdl(prev_pdl)
         torch.cuda.current_stream(self.device).wait_stream(s)
-        self._graphs = (graphs, tail, full)
+        self._graphs = full
         self.g_status.zero_()
         self.g_lstatus.zero_()
-
-    def _capture_graphs(self, s, mode):
-        """Capture the graphs; the library kernels each one launches are
-        counted while it is recorded (launch accounting of replays)."""
-        n = self.cfg.layers
-        graphs = []
-        self._kernels_layer = []
-        for i in range(n):
-            g = torch.cuda.CUDAGraph()
-            c0 = L.LAUNCHES[0]
-            with torch.cuda.graph(g, stream=s, capture_error_mode=mode):
-                self._record_layer(i)
-            self._kernels_layer.append(L.LAUNCHES[0] - c0)
-            graphs.append(g)
-        tail = torch.cuda.CUDAGraph()
-        c0 = L.LAUNCHES[0]
-        with torch.cuda.graph(tail, stream=s, capture_error_mode=mode):
-            self._record_tail()
-        self._kernels_tail = L.LAUNCHES[0] - c0
-        full = torch.cuda.CUDAGraph()
-        c0 = L.LAUNCHES[0]
-        with torch.cuda.graph(full, stream=s, capture_error_mode=mode):
-            self.g_lstatus.zero_()
-            for i in range(n):
-                self._record_layer(i, join=False)
-            self._join_side()
-            self._record_tail()
-        self._kernels_full = L.LAUNCHES[0] - c0
-        # suffix graphs: layers i..n-1 and the tail as one launch, for the
-        # re-run after a slot fill (one graph launch instead of n - i + 1)
-        self._suffix = [None] * n
-        self._kernels_suffix = [0] * n
-        for i in range(1, n):
-            g = torch.cuda.CUDAGraph()
-            c0 = L.LAUNCHES[0]
-            with torch.cuda.graph(g, stream=s, capture_error_mode=mode):
-                self.g_lstatus[i:].zero_()
-                for j in range(i, n):
-                    self._record_layer(j, join=False)
-                self._join_side()
-                self._record_tail()
-            self._kernels_suffix[i] = L.LAUNCHES[0] - c0
-            self._suffix[i] = g
-        return graphs, tail, full
-
-    def _graph_kernels(self, start: int) -> int:
-        """Library kernels one launch from layer `start` runs."""
-        if start == 0:
-            return self._kernels_full
-        return self._kernels_suffix[start]
-
-    def _launch(self, start: int) -> None:
-        graphs, tail, full = self._graphs
-        if start == 0:
-            full.replay()
-        else:
-            self._suffix[start].replay()
-        L._count(self._graph_kernels(start))
-
-    def _read_log(self) -> np.ndarray:
-        torch.cuda.current_stream(self.device).synchronize()
-        log = self.g_log_host.numpy().copy()
-        st = int(log[self._lst_off + self.cfg.layers])
-        if st != 0:
-            self.g_status.zero_()
-            raise L.SlxError("device", st, "decode step device error")
-        return log
+        self.svc.reset_words()
 
     def _glu_timed(self, i: int) -> bool:
-        """Layers whose SwitchGLU pair is bracketed by timing events: one in
+        """Layers whose SwitchGLU launch is bracketed by timing events: one in
         eight (an event node costs a few microseconds of the step)."""
         return self.glu_events and i % 8 == 3
 
-    def _glu_timing(self, start: int) -> None:
+    def _glu_timing(self) -> None:
         if self.glu_times is None or not self.glu_events:
             return
-        ev = [self.g_ev[i] for i in range(start, self.cfg.layers)
+        ev = [self.g_ev[i] for i in range(self.cfg.layers)
               if self._glu_timed(i)]
-        if not ev:
-            return
-        self.glu_times.extend(
-            L.event_elapsed_many([e[0] for e in ev], [e[1] for e in ev])
-            .tolist())
+        if ev:
+            self.glu_times.extend(
+                L.event_elapsed_many([e[0] for e in ev], [e[1] for e in ev])
+                .tolist())
 
-    def _prefetch_upto(self, log: np.ndarray) -> None:
-        """Start the next-layer prefetches of this step's layers whose logged
-        prediction is final (every layer up to and including the first
-        unmapped one), in layer order.  Layer i's prefetch touches only pool
-        i+1, and nothing changes pool i+1 between the previous step's call of
-        layer i+1 (already replayed) and this step's, so starting them here,
-        before this step's bookkeeping, gives the reference's per-pool order
-        while the reads overlap the bookkeeping and the next step."""
-        n, k = self.cfg.layers, self.cfg.top_k
-        lst = log[self._lst_off:self._lst_off + n]
-        bad = np.flatnonzero(lst == self._UNMAPPED)
-        upto = n if bad.size == 0 else int(bad[0]) + 1
-        pf_ids = log[n * k:2 * n * k].reshape(n, k)
-        pf_sc = log[2 * n * k:3 * n * k].view(np.float32).reshape(n, k)
-        for i in range(self._pf_done, upto):
-            w = self.layers[i].mlp.switch_mlp
-            if self.layers[i].mlp.pf_link is not None and w.pred_gate():
-                w.start_prefetch((pf_ids[i].copy(), pf_sc[i].copy()))
-        self._pf_done = max(self._pf_done, upto)
-
-    def _replay(self, log: np.ndarray, start: int) -> int | None:
-        """Pool bookkeeping of layers start.. from a log; returns the first
-        layer that must run again (its slots are now filled) or None.  The
-        layers' prefetches were started by _prefetch_upto."""
-        n, k = self.cfg.layers, self.cfg.top_k
-        ids = log[:n * k].reshape(n, 1, 1, k)
-        lst = log[self._lst_off:self._lst_off + n]
-        for i in range(start, n):
-            code = int(lst[i])
-            if code not in (0, self._UNMAPPED):
-                raise L.SlxError("device", code, f"layer {i} SwitchGLU")
-            w = self.layers[i].mlp.switch_mlp
-            if w.route(ids[i].copy(), None, start_prefetch=False) != "pool":
-                raise RuntimeError("decode call routed more experts than "
-                                   "the pool has slots")
-            w.pool.sync_device()
-            if code == self._UNMAPPED:
-                return i
-        return None
+    def _stores(self):
+        for la in self.layers:
+            w = la.mlp.switch_mlp
+            if hasattr(w, "pool") and hasattr(w.pool.store, "deferred"):
+                yield w.pool
 
     def flush(self) -> None:
-        """Finish the deferred bookkeeping of the last step, if any: start
-        its next-layer prefetches not yet started, then replay its pool
-        calls from the first layer not yet replayed."""
-        pend, self._pending = self._pending, None
-        if pend is None:
+        """Apply every recorded slot fill and table push now (on the current
+        stream); nothing of a decode step is left pending after it."""
+        if self._step_active:
             return
-        log, start, pf_done = pend
-        self._pf_done = pf_done
-        self._prefetch_upto(log)
-        if self._replay(log, start) is not None:
-            raise RuntimeError("deferred step had an unmapped expert")
+        stream = torch.cuda.current_stream(self.device)
+        for pool in self._stores():
+            if pool.store.has_pending():
+                pool.store.flush_pending(pool.slot_table, stream)
+
+    def _on_record(self, i: int, rec: np.ndarray) -> None:
+        """Host side of layer i's record: start the next layer's prefetch
+        from the prediction (gate checked as the reference does), then the
+        pool bookkeeping of the call."""
+        k = self.cfg.top_k
+        w = self.layers[i].mlp.switch_mlp
+        if self._pred_flags[i] and w.pred_gate():
+            w.start_prefetch((rec[20:20 + k].copy(),
+                              rec[36:36 + k].view(np.float32).copy()))
+        ids = rec[4:4 + k].astype(np.int64).reshape(1, 1, k)
+        if w.route(ids, None, start_prefetch=False) != "pool":
+            raise RuntimeError("decode call routed more experts than the "
+                               "pool has slots")
+        w.pool.sync_device()
+
+    def _serve_step(self, stamp: int) -> None:
+        """Follow the running step's layer records and serve parked layers
+        until the step's graph has completed."""
+        n = self.cfg.layers
+        svc = self.svc
+        log = svc.log
+        ht = self.host_times
+        nxt = 0
+        idle = 0
+        while True:
+            busy = False
+            while nxt < n and int(log[nxt, 0]) == stamp:
+                t0 = time.perf_counter()
+                self._on_record(nxt, log[nxt].copy())
+                ht["bookkeeping"] += time.perf_counter() - t0
+                nxt += 1
+                busy = True
+            pk = svc.pending_park(stamp)
+            if pk is not None and pk[0] < nxt:
+                t0 = time.perf_counter()
+                layer, ticket = pk
+                svc.serve(layer, ticket, self.layers[layer].mlp.switch_mlp.pool)
+                ht["park_serve"] += time.perf_counter() - t0
+                ht["parks"] += 1
+                busy = True
+            if busy:
+                idle = 0
+                continue
+            if nxt == n and self._ev_done.query():
+                break
+            idle += 1
+            if idle > 64:
+                time.sleep(0)       # let the prefetch thread run
+            if idle > 64 and self._ev_done.query() and nxt < n:
+                # the graph finished: every record it wrote is visible
+                if int(log[nxt, 0]) != stamp:
+                    raise RuntimeError(f"decode step ended without layer "
+                                       f"{nxt}'s record")
+
+    def _abort_step(self, stamp: int) -> None:
+        """After a host-side failure: release any parked layer without
+        fills, let the step finish and put the stores back in direct mode."""
+        t_end = time.perf_counter() + self.WAIT_S + 5
+        while not self._ev_done.query() and time.perf_counter() < t_end:
+            pk = self.svc.pending_park(stamp)
+            if pk is not None:
+                self.svc.abort(pk[1])
+            time.sleep(1e-4)
+        torch.cuda.current_stream(self.device).synchronize()
+        self.svc.stream.synchronize()
+        for pool in self._stores():
+            pool.store.deferred = False
 
     def _step_graph(self, token: torch.Tensor) -> torch.Tensor:
         n = self.cfg.layers
         if self.n_pos >= self.max_len:
             raise RuntimeError("KV cache full")
+        if self._graphs is not None and any(
+                self._pred_flags[i] != self._pred_on(i) for i in range(n)):
+            self._graphs = None     # a prediction gate closed: recapture
         if self._graphs is None:
-            self.flush()
             self._capture()
+        self._stamp += 1
+        stamp = self._stamp & 0x7FFFFF
+        if stamp == 0:
+            self._stamp += 1
+            stamp = 1
         ch = self.g_ctrl_host.numpy()
         ch[0] = self.n_pos
         for i in range(n):
             ch[1 + i] = int(bool(self.repeat_p) and self.n_pos > 0 and
                             self._rng.random() < self.repeat_p)
+        ch[n + 2] = stamp
         tok = token.reshape(1)
         if tok.dtype != torch.int32 or tok.device != self.device:
             tok = tok.to(device=self.device, dtype=torch.int32)
-        L.copy_many([self.g_ctrl.data_ptr(), self.g_ctrl.data_ptr() + 4 * (n + 1)],
-                    [self.g_ctrl_host.data_ptr(), tok.data_ptr()],
-                    [4 * (n + 1), 4])
-        # this step's device work is queued before the host replays the
-        # previous step: that replay's slot fills and table pushes run after
-        # it on the stream, and this step is judged by its own log
+        cur = torch.cuda.current_stream(self.device)
+        L.copy_many([self.g_ctrl.data_ptr(), self.g_ctrl.data_ptr() + 4 * (n + 1),
+                     self.g_ctrl.data_ptr() + 4 * (n + 2)],
+                    [self.g_ctrl_host.data_ptr(), tok.data_ptr(),
+                     self.g_ctrl_host.data_ptr() + 4 * (n + 2)],
+                    [4 * (n + 1), 4, 4])
         ht = self.host_times
         t0 = time.perf_counter()
-        self._launch(0)
+        for pool in self._stores():
+            pool.store.deferred = True
+        self._step_active = True
+        self._graphs.replay()
+        L._count(self._kernels_full)
+        self._ev_done.record(cur)
         t1 = time.perf_counter()
-        self.flush()
+        parks0 = ht["parks"]
+        try:
+            self._serve_step(stamp)
+        except BaseException:
+            self._step_active = False
+            self._abort_step(stamp)
+            raise
         t2 = time.perf_counter()
-        log = self._read_log()
+        self._step_active = False
+        for pool in self._stores():
+            pool.store.deferred = False
+        self.flush()                 # fills of layers that did not park
         t3 = time.perf_counter()
         ht["launch"] += t1 - t0
-        ht["bookkeeping"] += t2 - t1
-        ht["wait"] += t3 - t2
+        ht["serve"] += t2 - t1
+        ht["flush"] += t3 - t2
         ht["steps"] += 1
-        self._glu_timing(0)
-        lst = log[self._lst_off:self._lst_off + n]
-        t4 = time.perf_counter()
-        if self.pipeline and not (lst == self._UNMAPPED).any():
-            # bookkeeping (and the prefetch reads it starts) waits for the
-            # next call, where it overlaps that step's device work
-            self._pending = (log, 0, 0)
-        else:
-            self._pf_done = 0
-            self._prefetch_upto(log)
-            start = 0
-            while True:
-                r0 = time.perf_counter()
-                redo = self._replay(log, start)
-                r1 = time.perf_counter()
-                ht["miss_replay"] += r1 - r0
-                if redo is None:
-                    break
-                self._launch(redo)
-                r2 = time.perf_counter()
-                log = self._read_log()
-                ht["miss_relaunch"] += r2 - r1
-                ht["miss_wait"] += time.perf_counter() - r2
-                self._glu_timing(redo)
-                self._prefetch_upto(log)
-                if int(log[self._lst_off + redo]) != 0:
-                    raise RuntimeError(f"layer {redo} still unmapped after "
-                                       "its slots were filled")
-                start = redo + 1
-                rest = log[self._lst_off + start:self._lst_off + n]
-                if self.pipeline and not (rest == self._UNMAPPED).any():
-                    # the layers after the refilled one all ran on resident
-                    # experts: their bookkeeping waits for the next call,
-                    # like a miss-free step's
-                    self._pending = (log, start, self._pf_done)
-                    break
-            ht["miss_path"] += time.perf_counter() - t4
-            ht["miss_steps"] += 1
-        t5 = time.perf_counter()
+        ht["park_steps"] += int(ht["parks"] > parks0)
+        log = self.g_log_host.numpy()
+        st = int(log[n])
+        bad = [int(v) for v in log[:n] if int(v) != 0]
+        if st != 0 or bad:
+            self.g_status.zero_()
+            self.g_lstatus.zero_()
+            raise L.SlxError("device", st or bad[0], "decode step device error")
+        self._glu_timing()
         self.g_prev_ids.copy_(self.g_ids)
         self.n_pos += 1
         nxt = torch.empty(1, dtype=torch.int32, device=self.device)
         nxt.copy_(self.g_tok_out)
-        ht["tail"] += time.perf_counter() - t5
         return nxt
 
     @torch.no_grad()

@@ -100,22 +100,74 @@ class HbmSlotStore:
         self.bank = _lib.bank_struct(self.pool, n_slots, hidden, inter, bits,
                                      self.stride)
         self._dirty = True
+        # Deferred mode (the graph decoder, while a step runs): slot fills
+        # and table pushes are recorded instead of issued, because the device
+        # may be reading this pool's slots.  They are applied between steps
+        # (flush_pending) or handed to a parked layer kernel (take_pending).
+        self.deferred = False
+        self._pending: list = []        # (reader, raw, [(slot, expert)])
+        self._slot_table = None
 
     def slot_ptr(self, slot: int) -> int:
         return self.pool.data_ptr() + slot * self.stride
 
     def write(self, reader: ExpertReader, raw: dict, items) -> None:
         """Copy the experts of `items` [(slot, expert)] from a read result
-        into their slots."""
-        self.write_to(reader, raw, [(self.slot_ptr(s), e) for s, e in items])
+        into their slots (recorded for later in deferred mode)."""
         self._dirty = True
+        if self.deferred:
+            self._pending.append((reader, raw, list(items)))
+            return
+        self.write_to(reader, raw, [(self.slot_ptr(s), e) for s, e in items])
+
+    def take_pending(self, slot_table: np.ndarray) -> tuple[list, list]:
+        """Coalesced recorded fills: the last fill of each slot whose expert
+        still occupies that slot in `slot_table`, as [(slot, expert, raw,
+        reader)], plus every (reader, raw) the records referenced (each to be
+        released exactly once by the caller).  Clears the record."""
+        last: dict = {}
+        raws: dict = {}
+        for reader, raw, items in self._pending:
+            raws[id(raw)] = (reader, raw)
+            for slot, e in items:
+                last[slot] = (e, raw, reader)
+        self._pending = []
+        keep = [(slot, e, raw, rd) for slot, (e, raw, rd) in last.items()
+                if int(slot_table[e]) == slot]
+        return keep, list(raws.values())
+
+    def has_pending(self) -> bool:
+        return bool(self._pending) or self._dirty
+
+    def flush_pending(self, slot_table: np.ndarray, stream=None) -> int:
+        """Apply the recorded fills now, on `stream` (nothing may be reading
+        this pool's slots meanwhile), then push the table.  Returns the
+        number of experts packed."""
+        keep, raws = self.take_pending(slot_table)
+        by_raw: dict = {}
+        for slot, e, raw, rd in keep:
+            by_raw.setdefault(id(raw), (rd, raw, []))[2].append(
+                (self.slot_ptr(slot), e))
+        for rd, raw in raws:
+            ent = by_raw.get(id(raw))
+            if ent is not None:
+                self.write_to(rd, raw, ent[2], release=True, stream=stream)
+            else:
+                rd.release_raw(raw)
+        was, self.deferred = self.deferred, False
+        try:
+            self._dirty = True
+            self.sync_table(slot_table, stream=stream)
+        finally:
+            self.deferred = was
+        return len(keep)
 
     def write_to(self, reader: ExpertReader, raw: dict, items,
-                 release: bool = True) -> None:
+                 release: bool = True, stream=None) -> None:
         """Pack the experts of `items` [(device_ptr, expert)] from a read
         result: one host->device copy of the read's pinned region, one pack
         kernel.  With `release`, the region returns to the reader's arena
-        once the copy has run.  Ordered on the current stream."""
+        once the copy has run.  Ordered on `stream` (default: current)."""
         torch = self.torch
         if not items:
             if release:
@@ -123,7 +175,8 @@ class HbmSlotStore:
             return
         base, total = raw["__arena__"]
         staging = _staging(torch, self.device, total)
-        stream = torch.cuda.current_stream(self.device)
+        if stream is None:
+            stream = torch.cuda.current_stream(self.device)
         arena = reader.arena
         host0 = arena.base_ptr() + base
         self.L.copy_many([staging.data_ptr()], [host0], [total], stream)
@@ -146,13 +199,30 @@ class HbmSlotStore:
             ev.record(stream)
             reader.release_raw(raw, ev)
 
-    def sync_table(self, slot_table: np.ndarray) -> None:
-        """Push the host slot table (SENTINEL -> -1) to the device copy."""
+    def sync_table(self, slot_table: np.ndarray, stream=None) -> None:
+        """Push the host slot table (SENTINEL -> -1) to the device copy
+        (deferred mode: only remembered)."""
         if not self._dirty:
             return
+        if self.deferred:
+            self._slot_table = slot_table
+            return
+        torch = self.torch
         t = self._table_host.numpy()
         t[:] = slot_table.astype(np.int64).astype(np.int32)
-        self.table_dev.copy_(self._table_host, non_blocking=True)
+        if stream is None:
+            self.table_dev.copy_(self._table_host, non_blocking=True)
+        else:
+            with torch.cuda.stream(stream):
+                self.table_dev.copy_(self._table_host, non_blocking=True)
+        self._dirty = False
+
+    def table_words(self, slot_table: np.ndarray) -> np.ndarray:
+        """The device form of a host slot table (int32, -1 = absent)."""
+        return slot_table.astype(np.int64).astype(np.int32)
+
+    def mark_clean(self) -> None:
+        """The device table was installed another way (a parked kernel)."""
         self._dirty = False
 
     def mark_dirty(self) -> None:
