@@ -51,10 +51,9 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-PRESET = "qwen3moe_c2"
+WORKLOAD = "laguna_c5"
 SEED = 0
 PROMPT_TOKENS = 128
-BUDGET = 16 << 30
 SYNTH_ROOT = os.environ.get("STREAMLX_SYNTH_DIR",
                             os.path.join(tempfile.gettempdir(), "streamlx_synth"))
 METRIC = "decode_tok_s"
@@ -101,7 +100,7 @@ class Clocks:
             self.f = open(self.path, "w")
             self.p = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:   # noqa: BLE001 - clocks are best effort
             self.p = None
@@ -141,9 +140,10 @@ def measured_peak() -> tuple[float, str]:
         return 6650.0, "fallback"
 
 
-def traffic_from_profile() -> float | None:
-    """DRAM bytes per SwitchGLU launch pair from the committed ncu summary."""
-    p = os.path.join(ROOT, "profiles", "switchglu_decode_qwen3moe_c2.md")
+def traffic_from_profile(model: str) -> float | None:
+    """DRAM bytes per decode SwitchGLU launch from the committed ncu summary
+    of that model's layer shape."""
+    p = os.path.join(ROOT, "profiles", f"switchglu_decode_{model}.md")
     try:
         for line in open(p):
             if line.startswith("traffic_bytes_per_launch_pair:"):
@@ -153,63 +153,88 @@ def traffic_from_profile() -> float | None:
     return None
 
 
+SAMPLE_LAYERS = 4     # CPU timing sample: this many layers of each token
+
+
+def _oracle_token_seconds(o, tok: int, n_layers: int) -> float:
+    """Seconds of one decode token of the CPU oracle, measured on its first
+    ``n_layers`` layers (+ final norm and head) and scaled to every layer;
+    the head is timed once per call and not scaled."""
+    t0 = time.perf_counter()
+    o.step(tok, n_layers=n_layers)
+    t_sample = time.perf_counter() - t0
+    L = o.L
+    if n_layers >= L:
+        return t_sample
+    t0 = time.perf_counter()
+    o.step(tok, n_layers=0)                  # head only
+    t_head = time.perf_counter() - t0
+    return t_head + (t_sample - t_head) * L / n_layers
+
+
 def cpu_oracle_rate(d: str, budget_s: float, max_steps: int | None = None
                     ) -> tuple[float, int, int]:
-    """tok/s of the CPU oracle decoder (fp32 BLAS) on a bounded sample."""
+    """tok/s of the CPU oracle decoder (fp32 numpy BLAS) on a bounded
+    sample: tokens run through their first SAMPLE_LAYERS layers, scaled to
+    the whole model."""
     from oracle.model import OracleDecoder
-    o = OracleDecoder(d, max_len=64, exact=False)
+    o = OracleDecoder(d, max_len=512, exact=False)
     rng = np.random.default_rng(SEED)
-    tok = int(rng.integers(o.cfg["vocab"]))
-    logits, _ = o.step(tok)            # untimed warm-up (weight dequant)
-    tok = int(np.argmax(logits))
-    n, t0 = 0, time.perf_counter()
+    n_lay = min(SAMPLE_LAYERS, o.L)
+    o.step(int(rng.integers(o.cfg["vocab"])), n_layers=n_lay)   # warm-up
+    secs, n, t0 = 0.0, 0, time.perf_counter()
     while True:
-        logits, _ = o.step(tok)
-        tok = int(np.argmax(logits))
+        secs += _oracle_token_seconds(o, int(rng.integers(o.cfg["vocab"])),
+                                      n_lay)
         n += 1
-        el = time.perf_counter() - t0
-        if el > budget_s or (max_steps and n >= max_steps):
+        if time.perf_counter() - t0 > budget_s or \
+                (max_steps and n >= max_steps):
             break
     cores = len(os.sched_getaffinity(0))
-    return n / el, n, cores
+    return n / secs, n, cores
 
 
 def run_reference(args) -> None:
+    """The reference path restated on the CPU (the oracle decoder) on the
+    workload's checkpoint: each step is one decode token measured on its
+    first SAMPLE_LAYERS layers and scaled to the whole model."""
     rank, world, local = dist_env()
     if rank != 0:
         return
-    d = synth_dir(args.preset, SEED, 0, lambda: None)
+    preset = args.preset or WORKLOADS[args.workload][0]
+    d = synth_dir(preset, SEED, 0, lambda: None)
     from oracle.model import OracleDecoder
-    o = OracleDecoder(d, max_len=args.warmup + args.steps + 8, exact=False)
+    o = OracleDecoder(d, max_len=args.warmup + 2 * args.steps + 8,
+                      exact=False)
+    n_lay = min(SAMPLE_LAYERS, o.L)
     rng = np.random.default_rng(SEED)
-    tok = int(rng.integers(o.cfg["vocab"]))
     for _ in range(max(1, args.warmup)):
-        logits, _ = o.step(tok)
-        tok = int(np.argmax(logits))
-    budget_s = 180.0
-    n, t0 = 0, time.perf_counter()
+        o.step(int(rng.integers(o.cfg["vocab"])), n_layers=n_lay)
+    budget_s = 240.0
+    secs, n, t0 = 0.0, 0, time.perf_counter()
     while n < args.steps:
-        logits, _ = o.step(tok)
-        tok = int(np.argmax(logits))
+        secs += _oracle_token_seconds(o, int(rng.integers(o.cfg["vocab"])),
+                                      n_lay)
         n += 1
         if time.perf_counter() - t0 > budget_s:
             break
-    el = time.perf_counter() - t0
-    v = n / el
+    v = n / secs
     cores = len(os.sched_getaffinity(0))
-    sample = (f"{n} of {args.steps} decode tokens of the {args.preset} decoder "
-              f"(fp32 numpy, all experts dequantised per use), short context")
+    sample = (f"{n} of {args.steps} decode tokens of the {preset} decoder, "
+              f"each timed on its first {n_lay} of {o.L} layers (+ head) and "
+              f"scaled to all layers; fp32 numpy BLAS, experts dequantised "
+              f"per use")
     print(json.dumps({
-        "impl": "reference", "metric": METRIC, "value": round(v, 4),
+        "impl": "reference", "metric": METRIC, "value": round(v, 5),
         "unit": "tok/s", "n_gpus": world, "steps": n, "warmup": args.warmup,
-        "ms_per_step": round(1000 * el / max(n, 1), 2),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "ms_per_step": round(1000 * secs / max(n, 1), 2),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "u2/u4-affine codes, fp32 accumulate",
         "data": "synthetic (seeded)",
-        "config": {"workload": args.preset, "batch": 1},
-        "cpu_baseline": {"value": round(v, 4), "unit": "tok/s",
+        "config": {"workload": args.workload, "model": preset, "batch": 1},
+        "cpu_baseline": {"value": round(v, 5), "unit": "tok/s",
                          "cores": cores, "kind": "port", "sample": sample},
-        "e2e": {"value": round(v, 4), "unit": "tok/s",
+        "e2e": {"value": round(v, 5), "unit": "tok/s",
                 "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -475,9 +500,38 @@ def run_ep(args) -> None:
                 raise SystemExit(f"EP check failed: {bad}")
 
 
-def run_ours(args) -> None:
+WORKLOADS = {
+    # name: (preset, expert budget GiB or None = every expert resident and
+    #        sharded over the ranks)
+    "laguna_c5": ("laguna_c3", None),
+    "laguna_c3": ("laguna_c3", 7.5),
+    "qwen3moe_c2": ("qwen3moe_c2", 16.0),
+}
+
+
+def init_dist(world: int, local: int):
+    """Process group of the run (one rank without torchrun), NCCL on GPUs."""
+    import datetime
+
     import torch
     import torch.distributed as tdist
+    if tdist.is_initialized():
+        return tdist
+    if world == 1 and "MASTER_ADDR" not in os.environ:
+        import socket
+        sk = socket.socket()
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+        sk.close()
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port),
+                          RANK="0", WORLD_SIZE="1", LOCAL_RANK="0")
+    tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                             device_id=torch.device("cuda", local))
+    return tdist
+
+
+def run_ours(args) -> None:
+    import torch
 
     from streamlx_b200 import _lib as L
     from streamlx_b200 import ops, synth
@@ -486,22 +540,34 @@ def run_ours(args) -> None:
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    tdist = init_dist(world, local)
+    preset, budget_gib = WORKLOADS[args.workload]
+    if args.budget_gib is not None:
+        budget_gib = args.budget_gib
+    if args.policy:
+        os.environ["STREAMLX_EVICT"] = args.policy
+    if args.prefetch is not None:
+        os.environ["STREAMLX_PREFETCH"] = "1" if args.prefetch == "on" else "0"
+    sharded = budget_gib is None
+    if world > 1 and not sharded and not args.replicas:
+        raise SystemExit(f"{args.workload} streams experts through per-GPU "
+                         "pools; run it on one GPU or pass --replicas")
 
     def barrier():
         if world > 1:
             tdist.barrier()
 
-    d = synth_dir(args.preset, SEED, local, barrier)
-    cfg = synth.PRESETS[args.preset]
-    budget = int(args.budget_gib * (1 << 30))
+    d = synth_dir(preset, SEED, local, barrier)
+    cfg = synth.PRESETS[preset]
     t_load = time.time()
-    model, tok_, pools, reader = load_streaming_model(d, budget,
-                                                      k=cfg.top_k, device=dev)
+    if sharded:
+        model, tok_, pools, reader = load_streaming_model(
+            d, 0, k=cfg.top_k, device=dev, expert_parallel=True)
+    else:
+        model, tok_, pools, reader = load_streaming_model(
+            d, int(budget_gib * (1 << 30)), k=cfg.top_k, device=dev)
     t_load = time.time() - t_load
-    rng = np.random.default_rng(SEED + rank)
+    rng = np.random.default_rng(SEED)      # the same prompt on every rank
     prompt = rng.integers(0, cfg.vocab, args.prompt)
     total_steps = args.prompt + args.warmup + 2 * args.steps + 2
     if total_steps > model.max_len:
@@ -515,18 +581,18 @@ def run_ours(args) -> None:
         tok = model.step(tok)
     torch.cuda.synchronize()
     t_prompt = time.time() - t_prompt
-    for p in pools.values():
-        p.reset_stats()
-    reader.reset_stats()
+
+    def pool_counts():
+        st = aggregate_stats(pools)
+        return st["hits"], st["misses"], st["pf_used"]
 
     # ----------------------------------------------------- timed region --
     clocks = Clocks(local)
     for k_ in model.host_times:
         model.host_times[k_] = 0
-    ops.TIMING = []                 # eager-path launches (none expected)
     model.glu_times = []            # graph-path launches: per-layer events
     l0 = L.LAUNCHES[0]
-    model.flush()
+    c0 = pool_counts()
     barrier()
     torch.cuda.synchronize()
     clocks.start()
@@ -535,29 +601,32 @@ def run_ours(args) -> None:
     e0.record()
     for _ in range(args.steps):
         tok = model.step(tok)
-    model.flush()                   # the last step's deferred bookkeeping
     e1.record()
     torch.cuda.synchronize()
     barrier()
     clk = clocks.stop()
     launches = L.LAUNCHES[0] - l0
+    c1 = pool_counts()
     ht = dict(model.host_times)
     host_ms = {k_: round(1000 * v / max(ht["steps"], 1), 3)
                for k_, v in ht.items()
                if k_ not in ("steps", "parks", "park_steps")}
     host_ms["parks"] = ht["parks"]
     host_ms["steps_with_a_park"] = ht["park_steps"]
-    timing, ops.TIMING = ops.TIMING, None
     glu_ms, model.glu_times = model.glu_times, None
     ms = e0.elapsed_time(e1)
     t = torch.tensor([ms], device=dev)
     if world > 1:
         tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
     ms_max = float(t.item())
-    value = world * args.steps / (ms_max / 1000.0)
-    st = aggregate_stats(pools)
+    # batch-1 decode: every rank steps the same token (sharded experts) or
+    # its own replica (--replicas)
+    n_seq = world if (args.replicas and not sharded) else 1
+    value = n_seq * args.steps / (ms_max / 1000.0)
 
     # ------------------------------------ end to end (host token in/out) --
+    # the same number of steps right after, on the pools the timed loop
+    # left (each loop's pool traffic is reported)
     tok_host = int(tok.item())
     barrier()
     torch.cuda.synchronize()
@@ -568,28 +637,29 @@ def run_ours(args) -> None:
         t_in = torch.tensor([tok_host], dtype=torch.int32).pin_memory()
         out = model.step(t_in.to(dev, non_blocking=True))
         tok_host = int(out.item())
-    model.flush()
     f1.record()
     torch.cuda.synchronize()
+    c2 = pool_counts()
     t2 = torch.tensor([f0.elapsed_time(f1)], device=dev)
     if world > 1:
         tdist.all_reduce(t2, op=tdist.ReduceOp.MAX)
-    e2e_value = world * args.steps / (float(t2.item()) / 1000.0)
+    e2e_value = n_seq * args.steps / (float(t2.item()) / 1000.0)
 
     # --------------------------------------------------------- roofline --
-    durs = [a.elapsed_time(b) for a, b, *_ in timing] + list(glu_ms)
     H = cfg.hidden
     bpe = synth.expert_bytes(H, cfg.inter, cfg.expert_bits, 64)
     sh_b = synth.expert_bytes(H, cfg.shared_inter, cfg.trunk_bits, 64) \
         if cfg.shared_inter else 0
-    per_launch = cfg.top_k * bpe + sh_b + 2 * 2 * H
-    mean_ms = float(np.mean(durs)) if durs else float("nan")
+    # routed experts this rank computes per launch (all of them at N = 1)
+    units = cfg.top_k / (world if sharded else 1)
+    per_launch = units * bpe + sh_b + 2 * 2 * H
+    mean_ms = float(np.mean(glu_ms)) if glu_ms else float("nan")
     achieved = per_launch / (mean_ms / 1000.0) / 1e9
     peak, peak_kind = measured_peak()
-    traffic = traffic_from_profile()
+    traffic = traffic_from_profile(cfg.name)
 
     pre = None
-    if not args.no_prefill:
+    if not args.no_prefill and rank == 0 and world == 1:
         pre = prefill_measure(dev)
 
     cpu = None
@@ -597,51 +667,59 @@ def run_ours(args) -> None:
         rate, n, cores = cpu_oracle_rate(d, budget_s=args.cpu_seconds)
         cpu = {"value": round(rate, 4), "unit": "tok/s", "cores": cores,
                "kind": "port",
-               "sample": f"{n} decode tokens of the same {args.preset} checkpoint "
+               "sample": f"{n} decode tokens of the same {preset} checkpoint "
                          f"on the CPU oracle decoder (fp32 numpy BLAS)"}
 
-    if world > 1:
-        tdist.barrier()
+    if sharded and model.ep is not None:
+        model.ep.close()
+    barrier()
+    if world > 1 or tdist.is_initialized():
+        model._graphs = None
         tdist.destroy_process_group()
     if rank != 0:
         return
+    hits0 = (c1[0] - c0[0], c1[1] - c0[1])
+    hits1 = (c2[0] - c1[0], c2[1] - c1[1])
     res = {
         "metric": METRIC, "value": round(value, 3), "unit": "tok/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms_max / args.steps, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "u4-affine codes x bf16, fp32 accumulate",
+        "higher_is_better": True,
+        "scaling": "strong" if sharded else "weak", "vs_baseline": None,
+        "dtype": f"u{cfg.expert_bits}-affine codes x bf16, fp32 accumulate",
         "data": "synthetic (seeded random-init weights and prompt)",
-        "config": {"workload": args.preset, "layers": cfg.layers,
-                   "hidden": cfg.hidden, "experts": cfg.n_experts,
-                   "top_k": cfg.top_k, "shared_expert": True,
-                   "expert_budget_gib": args.budget_gib,
+        "config": {"workload": args.workload, "model": preset,
+                   "layers": cfg.layers, "hidden": cfg.hidden,
+                   "experts": cfg.n_experts, "top_k": cfg.top_k,
+                   "expert_bits": cfg.expert_bits,
+                   "shared_expert": bool(cfg.shared_inter),
+                   "experts_in_hbm": ("all, sharded over the GPUs" if sharded
+                                      else f"{budget_gib} GiB pools"),
                    "slots_per_layer": pools[0].n_slots,
+                   "evict": os.environ.get("STREAMLX_EVICT", "lru"),
+                   "prefetch": os.environ.get("STREAMLX_PREFETCH", "1") != "0",
                    "prompt_tokens": args.prompt, "batch": 1,
-                   "l2": "inputs larger than L2: ~0.9 GB of weights per step",
-                   "parallelism": f"replicas x{world}"},
+                   "l2": "inputs larger than L2: ~1 GB of weights per step",
+                   "parallelism": (f"expert parallel x{world}" if sharded
+                                   else f"replicas x{world}")},
         "e2e": {"value": round(e2e_value, 3), "unit": "tok/s",
                 "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
-        "roofline": {"kernel": "slx_switchglu decode (k_switchglu_fused: one cooperative launch per layer)",
+        "roofline": {"kernel": "decode SwitchGLU (k_switchglu_fused, one "
+                               "cooperative launch per layer)",
                      "bound": "hbm", "achieved": round(achieved, 1),
                      "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                      "frac": round(achieved / peak, 4),
                      "traffic": traffic,
-                     "traffic_source": "ncu DRAM bytes of the two-launch "
-                                       "form of the same SwitchGLU (same "
-                                       "tiles read); the fused launch was "
-                                       "not captured at steady state",
-                     "algorithmic_bytes_per_launch": per_launch,
-                     "launches_timed": len(durs),
-                     "sampling": "layers 3, 11, 19, 27, 35 of every step",
+                     "algorithmic_bytes_per_launch": int(per_launch),
+                     "launches_timed": len(glu_ms),
+                     "sampling": "layers 3, 11, 19, ... of every step",
                      "mean_launch_us": round(1000 * mean_ms, 2)},
         "gpu_launches": launches,
         "host_ms_per_step": host_ms,
         "clocks": clk,
-        "pool": {"miss_rate": round(st["miss_rate"], 5),
-                 "fetch_s": st["fetch_s"],
-                 "hits": st["hits"], "misses": st["misses"],
-                 "prefetch_used": st["pf_used"]},
+        "pool": {"timed_loop": {"hits": hits0[0], "misses": hits0[1]},
+                 "e2e_loop": {"hits": hits1[0], "misses": hits1[1]},
+                 "prefetch_used_timed": c1[2] - c0[2]},
         "setup_s": {"load": round(t_load, 1), "prompt_and_warmup":
                     round(t_prompt, 1)},
     }
@@ -658,10 +736,22 @@ def main():
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--preset", default=PRESET,
-                    help="synthetic model shape (parity/debug runs)")
+    ap.add_argument("--workload", default=WORKLOAD, choices=sorted(WORKLOADS),
+                    help="laguna_c5: the 117B-shaped decoder, every expert "
+                         "resident and sharded over the GPUs (default); "
+                         "laguna_c3: the same model streaming from 7.5 GiB "
+                         "pools; qwen3moe_c2: the Qwen3-MoE-shaped decoder "
+                         "with 16 GiB pools")
+    ap.add_argument("--preset", default=None,
+                    help="checkpoint preset of the reference arm (default: "
+                         "the workload's)")
     ap.add_argument("--prompt", type=int, default=PROMPT_TOKENS)
-    ap.add_argument("--budget-gib", type=float, default=BUDGET / (1 << 30))
+    ap.add_argument("--budget-gib", type=float, default=None,
+                    help="override the workload's expert budget")
+    ap.add_argument("--policy", choices=["lru", "s3fifo"], default=None)
+    ap.add_argument("--prefetch", choices=["on", "off"], default=None)
+    ap.add_argument("--replicas", action="store_true",
+                    help="pool workloads on N GPUs: N independent replicas")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true",

@@ -39,6 +39,9 @@ extern "C" {
 #define SLX_ERR_DEVICE_TIMEOUT (-6)  /* device: a bounded wait expired */
 #define SLX_ERR_SCRATCH (-7)         /* scratch buffer too small */
 #define SLX_ERR_IO (-8)              /* host file read failed or was short */
+#define SLX_ERR_RANGE (-9)           /* device: an operand outside the range
+                                        a kernel computes exactly (fp16
+                                        operands: see the kernel's entry) */
 
 #define SLX_GEMV_GLU 0
 #define SLX_GEMV_LINEAR 1
@@ -203,6 +206,67 @@ int slx_switchglu_serviced(const slx_expert_bank* bank,
                            void* scratch, size_t scratch_bytes,
                            int32_t* status, const slx_fill_service* svc,
                            void* stream);
+
+/* Expert-parallel decode over NVLink peer memory (no reference counterpart:
+ * the reference runs on one device).  Every rank runs the trunk and the
+ * router (identical results on every rank) and the SwitchGLU of the routed
+ * experts it owns (its slot table maps only those); the launch writes each
+ * owned unit's bf16 output rows into EVERY rank's receive block of this
+ * step and layer, then each of its CTAs adds 1 to every rank's counter of
+ * the layer (system-scope release).  slx_ep_combine_rmsnorm on each rank
+ * waits (bounded) until its counter of the stamp's parity reaches
+ * ((stamp + 1) / 2) * n_ranks * grid (the steps of that parity so far), sums the
+ * rows in unit order exactly as the single-GPU kernel does (so the result
+ * does not depend on n_ranks), adds the residual and applies the next
+ * RMSNorm.  Receive block layout per rank: [2 (stamp parity)][n_layers]
+ * [k + 1][hidden] bf16 (row k = the shared expert, written by every rank
+ * for itself); counters: uint32 [2][n_layers] (stamp parity), zero before
+ * the first step.  A rank can only count itself for step s + 1 at a layer
+ * after every rank has combined step s there, and parity-split counters keep
+ * those early counts out of the step-s wait.
+ * recv/count hold peer addresses (slx_ipc_open) except entry `rank`. */
+#define SLX_EP_MAX_RANKS 8
+
+typedef struct slx_ep_exchange {
+  int32_t rank, n_ranks;   /* n_ranks <= SLX_EP_MAX_RANKS */
+  int32_t layer, n_layers;
+  const int32_t* stamp;    /* device int32: step stamp, 1, 2, 3, ... */
+  void* recv[SLX_EP_MAX_RANKS];
+  uint32_t* count[SLX_EP_MAX_RANKS];
+  int32_t grid;            /* CTAs of the SwitchGLU launch (slx_ep_grid) */
+  int64_t wait_ns;         /* bound of the combine's wait */
+} slx_ep_exchange;
+
+/* CTAs of the single-launch decode SwitchGLU on the current device (every
+ * rank must agree). */
+int slx_ep_grid(void);
+
+/* slx_switchglu for one decode token in expert-parallel mode (above): the
+ * combined output is formed by slx_ep_combine_rmsnorm, `scores` is still
+ * required for the shared expert's presence only. */
+int slx_switchglu_ep(const slx_expert_bank* bank,
+                     const slx_shared_expert* shared, const void* x, int k,
+                     const int32_t* ids, const float* scores,
+                     const int32_t* slot_table, int n_table, void* scratch,
+                     size_t scratch_bytes, int32_t* status,
+                     const slx_ep_exchange* ep, void* stream);
+
+/* Wait for every rank's rows of this step and layer, then
+ * delta = bf16(sum_j scores[j] * row_j (+ shared row)), h_out = bf16(h_in +
+ * delta), y = RMSNorm(h_out) * weight (one token).  With ep->grid == 0 the
+ * wait is skipped (a warm-up launch). */
+int slx_ep_combine_rmsnorm(const slx_ep_exchange* ep, const float* scores,
+                           int k, int hidden, int has_shared,
+                           const void* h_in, const void* weight, float eps,
+                           void* h_out, void* y, int32_t* status,
+                           void* stream);
+
+/* CUDA IPC for the receive blocks: the handle (64 bytes) of the allocation
+ * holding dev_ptr and dev_ptr's offset inside it; open maps a peer's
+ * allocation (returns its base); close unmaps. */
+int slx_ipc_handle(const void* dev_ptr, void* handle64, int64_t* offset);
+int slx_ipc_open(const void* handle64, void** base);
+int slx_ipc_close(void* base);
 
 /* Device address of page-locked host memory (cudaHostGetDevicePointer):
  * the `log` and `park` words of slx_fill_service live in host memory that

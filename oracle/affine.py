@@ -154,6 +154,13 @@ def topk_ids(logits: np.ndarray, k: int) -> np.ndarray:
     return order[..., :k].astype(np.int32)
 
 
+def topk_margin(logits: np.ndarray, k: int) -> float:
+    """Smallest gap between logits that decides an ordered top-k: adjacent
+    pairs among the k + 1 largest (the order of the picks and the cut)."""
+    s = np.sort(np.asarray(logits, dtype=np.float64))[::-1][:k + 1]
+    return float(np.min(s[:-1] - s[1:])) if s.size > 1 else np.inf
+
+
 def softmax_rows(logits: np.ndarray) -> np.ndarray:
     z = logits.astype(np.float64)
     z = z - z.max(axis=-1, keepdims=True)

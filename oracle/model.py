@@ -60,6 +60,11 @@ class OracleDecoder:
         self.inv = TR.rope_inv_freq(c["head_dim"], c["rope_theta"])
         self._deq: dict = {}
         self.pos = 0
+        # smallest logit gap that decided each layer's routed / predicted
+        # ids at the last step (how far an input perturbation must move a
+        # logit to change the decision)
+        self.route_margin = np.full(self.L, np.inf)
+        self.pred_margin = np.full(self.L, np.inf)
 
     def deq(self, prefix: str, bits: int) -> np.ndarray:
         if prefix not in self._deq:
@@ -119,9 +124,11 @@ class OracleDecoder:
         """m [1, H] -> (combined [1, H], ids [k], scores [k])."""
         c = self.cfg
         p = f"model.layers.{layer}.mlp"
-        ids, sc, _ = A.router(m, self.t[f"{p}.gate.weight"],
-                              self.t[f"{p}.gate.bias"], c["top_k"],
-                              c["norm_topk_prob"], forced_ids=forced_ids)
+        ids, sc, lg = A.router(m, self.t[f"{p}.gate.weight"],
+                               self.t[f"{p}.gate.bias"], c["top_k"],
+                               c["norm_topk_prob"], forced_ids=forced_ids)
+        self.route_margin[layer] = (A.topk_margin(lg[0], c["top_k"])
+                                    if forced_ids is None else np.inf)
         y = np.stack([self.expert_fwd(m, self.expert(layer, int(e)))[0]
                       for e in ids[0]])[None]
         sh = None
@@ -131,16 +138,39 @@ class OracleDecoder:
             sh = self.expert_fwd(m, d)
         return A.moe_combine(y, sc, sh), ids[0], sc[0]
 
-    def step(self, token: int, forced: dict | None = None):
-        """One decode step; returns (logits [V], routed ids per layer).
-        forced: {layer: ids} for the temporal-reuse routing override."""
+    def predict_next(self, layer: int, m: np.ndarray):
+        """Next-layer routing prediction made at ``layer`` from its MoE input
+        m [1, H] (streamlx/integrate.py:60-88): the next layer's gate on
+        bf16(m * bf16(w_post(layer+1) / w_post(layer))).  Returns (ids [k],
+        scores [k])."""
+        c = self.cfg
+        wa = self.bf(f"model.layers.{layer}.post_attention_layernorm.weight")
+        wb = self.bf(f"model.layers.{layer + 1}.post_attention_layernorm"
+                     ".weight")
+        ratio = A.bf16_round(wb.astype(np.float32) / wa.astype(np.float32))
+        xr = A.bf16_round(m.astype(np.float32) * ratio)
+        p = f"model.layers.{layer + 1}.mlp"
+        ids, sc, lg = A.router(xr, self.t[f"{p}.gate.weight"],
+                               self.t[f"{p}.gate.bias"], c["top_k"],
+                               c["norm_topk_prob"])
+        self.pred_margin[layer] = A.topk_margin(lg[0], c["top_k"])
+        return ids[0], sc[0]
+
+    def step(self, token: int, forced: dict | None = None,
+             predict: bool = False, n_layers: int | None = None):
+        """One decode step; returns (logits [V], routed ids per layer), and
+        with ``predict`` also the next-layer predictions [(ids, scores) or
+        None per layer].  forced: {layer: ids} for the temporal-reuse
+        routing override.  ``n_layers`` runs only the first layers before
+        the final norm and head (a timing sample; logits then meaningless)."""
         c = self.cfg
         H, hd, nq, nkv = c["hidden"], c["head_dim"], c["heads"], c["kv_heads"]
         eps = c["rms_eps"]
         h = A.bf16_round(self.embed_row(token))
         delta = None
         routed = []
-        for i in range(self.L):
+        preds: list = []
+        for i in range(self.L if n_layers is None else min(n_layers, self.L)):
             p = f"model.layers.{i}"
             h, x = TR.add_rmsnorm(h, delta, self.bf(f"{p}.input_layernorm.weight"),
                                   eps)
@@ -163,9 +193,14 @@ class OracleDecoder:
                                   self.bf(f"{p}.post_attention_layernorm.weight"),
                                   eps)
             fi = None if forced is None else forced.get(i)
+            if predict:
+                preds.append(self.predict_next(i, m) if i + 1 < self.L
+                             else None)
             delta, ids, _ = self.moe(i, m, None if fi is None else fi[None])
             routed.append(ids)
         h, x = TR.add_rmsnorm(h, delta, self.bf("model.norm.weight"), eps)
         logits = self.mv(x, self.deq("lm_head", self.tbits))[0]
         self.pos += 1
+        if predict:
+            return logits, routed, preds
         return logits, routed

@@ -21,7 +21,9 @@ ERRORS = {
     -1: "SLX_ERR_INVALID", -2: "SLX_ERR_UNSUPPORTED", -3: "SLX_ERR_CUDA",
     -4: "SLX_ERR_OUT_OF_RANGE", -5: "SLX_ERR_UNMAPPED_EXPERT",
     -6: "SLX_ERR_DEVICE_TIMEOUT", -7: "SLX_ERR_SCRATCH", -8: "SLX_ERR_IO",
+    -9: "SLX_ERR_RANGE",
 }
+SLX_ERR_RANGE = -9
 GEMV_GLU, GEMV_LINEAR = 0, 1
 
 # every symbol the header declares (the CPU test checks they are exported)
@@ -38,7 +40,10 @@ EXPORTS = (
     "slx_set_switchglu_fused", "slx_switchglu_last_kernels",
     "slx_prefill_scratch_bytes", "slx_prefill_grouped",
     "slx_switchglu_serviced", "slx_host_device_ptr",
+    "slx_ep_grid", "slx_switchglu_ep", "slx_ep_combine_rmsnorm",
+    "slx_ipc_handle", "slx_ipc_open", "slx_ipc_close",
 )
+EP_MAX_RANKS = 8
 
 # slx_fill_service layout constants (include/streamlx_cuda.h)
 FILL_LOG_WORDS = 64
@@ -86,6 +91,14 @@ class slx_fill_service(C.Structure):
                 ("park", C.c_void_p), ("release", C.c_void_p),
                 ("desc", C.c_void_p), ("go", C.c_void_p),
                 ("wait_ns", C.c_int64)]
+
+
+class slx_ep_exchange(C.Structure):
+    _fields_ = [("rank", C.c_int32), ("n_ranks", C.c_int32),
+                ("layer", C.c_int32), ("n_layers", C.c_int32),
+                ("stamp", C.c_void_p),
+                ("recv", C.c_void_p * 8), ("count", C.c_void_p * 8),
+                ("grid", C.c_int32), ("wait_ns", C.c_int64)]
 
 
 class slx_router_head(C.Structure):
@@ -177,6 +190,21 @@ def lib() -> C.CDLL:
             C.POINTER(slx_expert_bank), C.POINTER(slx_shared_expert), vp,
             i32, vp, vp, vp, i32, vp, vp, sz, vp,
             C.POINTER(slx_fill_service), vp]
+        L.slx_ep_grid.restype = i32
+        L.slx_switchglu_ep.restype = i32
+        L.slx_switchglu_ep.argtypes = [
+            C.POINTER(slx_expert_bank), C.POINTER(slx_shared_expert), vp,
+            i32, vp, vp, vp, i32, vp, sz, vp, C.POINTER(slx_ep_exchange), vp]
+        L.slx_ep_combine_rmsnorm.restype = i32
+        L.slx_ep_combine_rmsnorm.argtypes = [
+            C.POINTER(slx_ep_exchange), vp, i32, i32, i32, vp, vp, C.c_float,
+            vp, vp, vp, vp]
+        L.slx_ipc_handle.restype = i32
+        L.slx_ipc_handle.argtypes = [vp, vp, C.POINTER(C.c_int64)]
+        L.slx_ipc_open.restype = i32
+        L.slx_ipc_open.argtypes = [vp, C.POINTER(vp)]
+        L.slx_ipc_close.restype = i32
+        L.slx_ipc_close.argtypes = [vp]
         L.slx_host_device_ptr.restype = i32
         L.slx_host_device_ptr.argtypes = [vp, C.POINTER(vp)]
         L.slx_prefill_grouped.restype = i32
@@ -310,6 +338,59 @@ def switchglu_serviced(bank: slx_expert_bank, x: torch.Tensor,
         status.data_ptr(), C.byref(svc), stream_ptr(stream))
     _check("slx_switchglu_serviced", rc)
     _count(1)
+
+
+def ep_grid() -> int:
+    n = int(lib().slx_ep_grid())
+    if n <= 0:
+        _check("slx_ep_grid", n)
+    return n
+
+
+def switchglu_ep(bank, x, ids, scores, slot_table, scratch, status, ep,
+                 shared=None, stream=None) -> None:
+    """One decode token's SwitchGLU in expert-parallel mode."""
+    k = ids.shape[-1]
+    rc = lib().slx_switchglu_ep(
+        C.byref(bank), C.byref(shared) if shared is not None else None,
+        x.data_ptr(), k, ids.data_ptr(), scores.data_ptr(),
+        slot_table.data_ptr(), int(slot_table.numel()), scratch.data_ptr(),
+        scratch.numel() * scratch.element_size(), status.data_ptr(),
+        C.byref(ep), stream_ptr(stream))
+    _check("slx_switchglu_ep", rc)
+    _count(1)
+
+
+def ep_combine_rmsnorm(ep, scores, k: int, hidden: int, has_shared: bool,
+                       h_in, weight, eps: float, h_out, y, status,
+                       stream=None) -> None:
+    rc = lib().slx_ep_combine_rmsnorm(
+        C.byref(ep), scores.data_ptr(), k, hidden, 1 if has_shared else 0,
+        h_in.data_ptr(), weight.data_ptr(), eps, h_out.data_ptr(),
+        y.data_ptr(), status.data_ptr(), stream_ptr(stream))
+    _check("slx_ep_combine_rmsnorm", rc)
+    _count(1)
+
+
+def ipc_handle(t: torch.Tensor) -> tuple[bytes, int]:
+    """(64-byte CUDA IPC handle of the allocation holding t, t's offset)."""
+    buf = (C.c_char * 64)()
+    off = C.c_int64(0)
+    rc = lib().slx_ipc_handle(t.data_ptr(), buf, C.byref(off))
+    _check("slx_ipc_handle", rc)
+    return bytes(buf), int(off.value)
+
+
+def ipc_open(handle: bytes) -> int:
+    out = C.c_void_p()
+    buf = (C.c_char * 64).from_buffer_copy(handle)
+    rc = lib().slx_ipc_open(buf, C.byref(out))
+    _check("slx_ipc_open", rc)
+    return int(out.value)
+
+
+def ipc_close(base: int) -> None:
+    _check("slx_ipc_close", lib().slx_ipc_close(base))
 
 
 def host_device_ptr(host_ptr: int) -> int:

@@ -1,5 +1,7 @@
 // extern "C" entry points of libstreamlx_cuda.so (declared in
 // include/streamlx_cuda.h).  Host-side argument checks, then the launchers.
+#include <cuda.h>
+
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -140,7 +142,125 @@ static int switchglu_impl(const slx_expert_bank* bank,
                           int T, int k, const int32_t* ids, const float* scores,
                           const int32_t* slot_table, int n_table, void* out,
                           void* scratch, size_t scratch_bytes, int32_t* status,
-                          void* stream, const slx_fill_service* svc);
+                          void* stream, const slx_fill_service* svc,
+                          const slx_ep_exchange* ep = nullptr);
+
+static bool ep_ok(const slx_ep_exchange* ep) {
+  if (!ep || ep->n_ranks < 1 || ep->n_ranks > SLX_EP_MAX_RANKS ||
+      ep->rank < 0 || ep->rank >= ep->n_ranks || ep->layer < 0 ||
+      ep->layer >= ep->n_layers || !ep->stamp || ep->grid < 0 ||
+      ep->wait_ns <= 0)
+    return false;
+  for (int r = 0; r < ep->n_ranks; ++r)
+    if (!ep->recv[r] || !ep->count[r] || !aligned16(ep->recv[r])) return false;
+  return true;
+}
+
+int slx_ep_grid(void) {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) !=
+          cudaSuccess)
+    return fail(SLX_ERR_CUDA, "slx_ep_grid: no device");
+  return n;
+}
+
+int slx_switchglu_ep(const slx_expert_bank* bank,
+                     const slx_shared_expert* shared, const void* x, int k,
+                     const int32_t* ids, const float* scores,
+                     const int32_t* slot_table, int n_table, void* scratch,
+                     size_t scratch_bytes, int32_t* status,
+                     const slx_ep_exchange* ep, void* stream) {
+  g_err.clear();
+  if (!ep_ok(ep)) return fail(SLX_ERR_INVALID, "switchglu_ep: bad exchange");
+  if (!scores || !slot_table)
+    return fail(SLX_ERR_INVALID, "switchglu_ep: scores and slot_table are "
+                "required");
+  if (ep->grid != slx_ep_grid())
+    return fail(SLX_ERR_INVALID, "switchglu_ep: grid %d != %d", ep->grid,
+                slx_ep_grid());
+  // out is not written in this mode; the scratch doubles as a dummy
+  return switchglu_impl(bank, shared, x, 1, k, ids, scores, slot_table,
+                        n_table, scratch, scratch, scratch_bytes, status,
+                        stream, nullptr, ep);
+}
+
+int slx_ep_combine_rmsnorm(const slx_ep_exchange* ep, const float* scores,
+                           int k, int hidden, int has_shared,
+                           const void* h_in, const void* weight, float eps,
+                           void* h_out, void* y, int32_t* status,
+                           void* stream) {
+  g_err.clear();
+  if (!ep_ok(ep)) return fail(SLX_ERR_INVALID, "ep_combine: bad exchange");
+  if (!scores || !h_in || !weight || !h_out || !y || k < 1 ||
+      !aligned16(h_in) || !aligned16(h_out) || !aligned16(y) ||
+      !aligned16(weight))
+    return fail(SLX_ERR_INVALID, "ep_combine: NULL/misaligned or k %d", k);
+  const int rc = slx::launch_ep_combine_rmsnorm(
+      *ep, scores, k, hidden, has_shared ? 1 : 0,
+      reinterpret_cast<const uint16_t*>(h_in),
+      reinterpret_cast<const uint16_t*>(weight), eps,
+      reinterpret_cast<uint16_t*>(h_out), reinterpret_cast<uint16_t*>(y),
+      status, reinterpret_cast<cudaStream_t>(stream));
+  return rc ? cuda_check(rc, "slx_ep_combine_rmsnorm") : SLX_OK;
+}
+
+int slx_ipc_handle(const void* dev_ptr, void* handle64, int64_t* offset) {
+  g_err.clear();
+  if (!dev_ptr || !handle64 || !offset)
+    return fail(SLX_ERR_INVALID, "ipc_handle: NULL");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(dev_ptr));
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(SLX_ERR_CUDA, "cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+  }
+  // the handle names the whole allocation: locate dev_ptr inside it (the
+  // driver call is reached through the runtime, so the library does not
+  // link the driver and still loads on machines without one)
+  using range_fn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+  if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault,
+                              &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess || !fn) {
+    cudaGetLastError();
+    return fail(SLX_ERR_CUDA, "cuMemGetAddressRange entry point not found");
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (reinterpret_cast<range_fn>(fn)(&base, &size, (CUdeviceptr)dev_ptr) !=
+      CUDA_SUCCESS)
+    return fail(SLX_ERR_CUDA, "cuMemGetAddressRange failed");
+  std::memcpy(handle64, &h, sizeof(h));
+  *offset = (int64_t)((CUdeviceptr)dev_ptr - base);
+  return SLX_OK;
+}
+
+int slx_ipc_open(const void* handle64, void** base) {
+  g_err.clear();
+  if (!handle64 || !base) return fail(SLX_ERR_INVALID, "ipc_open: NULL");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle64, sizeof(h));
+  const cudaError_t e =
+      cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(SLX_ERR_CUDA, "cudaIpcOpenMemHandle: %s", cudaGetErrorString(e));
+  }
+  return SLX_OK;
+}
+
+int slx_ipc_close(void* base) {
+  g_err.clear();
+  const cudaError_t e = cudaIpcCloseMemHandle(base);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(SLX_ERR_CUDA, "cudaIpcCloseMemHandle: %s",
+                cudaGetErrorString(e));
+  }
+  return SLX_OK;
+}
 
 int slx_switchglu(const slx_expert_bank* bank, const slx_shared_expert* shared,
                   const void* x, int T, int k, const int32_t* ids,
@@ -188,7 +308,8 @@ static int switchglu_impl(const slx_expert_bank* bank,
                           int T, int k, const int32_t* ids, const float* scores,
                           const int32_t* slot_table, int n_table, void* out,
                           void* scratch, size_t scratch_bytes, int32_t* status,
-                          void* stream, const slx_fill_service* svc) {
+                          void* stream, const slx_fill_service* svc,
+                          const slx_ep_exchange* ep) {
   if (!bank) return fail(SLX_ERR_INVALID, "slx_switchglu: bank is NULL");
   const int H = bank->hidden, I = bank->inter, bits = bank->bits;
   if (bits != 2 && bits != 4 && bits != 8)
@@ -285,21 +406,21 @@ static int switchglu_impl(const slx_expert_bank* bank,
   d.n_units = k + (Is > 0 ? 1 : 0);
   d.pdl = 1;
   int rc = SLX_ERR_UNSUPPORTED;
-  if ((g_fused || svc) && T == 1) {
+  if ((g_fused || svc || ep) && T == 1) {
     // one cooperative launch for both phases when the token's tiles fit
     d.tile_bytes = (int)slx::single_tile_bytes(I, bits);
     d.tile_bytes_sh = Is ? (int)slx::single_tile_bytes(Is, bits) : 0;
     d.a_bytes = (long long)slx::expert_a_bytes(H, I, bits);
     d.a_bytes_sh = Is ? (long long)slx::expert_a_bytes(H, Is, bits) : 0;
-    rc = slx::launch_switchglu_fused(a, d, gbar, bits, s, svc);
+    rc = slx::launch_switchglu_fused(a, d, gbar, bits, s, svc, ep);
     if (rc != SLX_ERR_UNSUPPORTED) {
       g_glu_kernels = rc ? 0 : 1;
       return rc ? cuda_check(rc, "slx_switchglu fused") : SLX_OK;
     }
   }
-  if (svc)
-    return fail(SLX_ERR_UNSUPPORTED, "switchglu_serviced: the token's tiles "
-                "do not fit the single-launch form");
+  if (svc || ep)
+    return fail(SLX_ERR_UNSUPPORTED, "switchglu (serviced / ep): the token's "
+                "tiles do not fit the single-launch form");
   g_glu_kernels = 0;
   rc = slx::launch_gemv(a, bits, s, /*pdl_secondary=*/true);
   if (rc) return cuda_check(rc, "slx_switchglu gate/up");

@@ -1,7 +1,7 @@
 // Shared device helpers for the streamlx B200 kernels (sm_100a).
 //
 // Everything here is hand-written PTX or plain CUDA: mbarrier + bulk-copy
-// (TMA engine, no multicast) staging, mma.sync bf16 fragments, and the
+// (TMA engine, one CTA per copy) staging, mma.sync bf16 fragments, and the
 // magic-number unpack of MLX-affine 2/4/8-bit codes into bf16 pairs.
 #pragma once
 

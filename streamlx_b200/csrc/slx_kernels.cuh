@@ -84,7 +84,13 @@ int launch_gemv(GemvArgs a, int bits, cudaStream_t stream, bool pdl_secondary);
 int launch_down(DownArgs a, int bits, cudaStream_t stream);
 int launch_switchglu_fused(const GemvArgs& a, const DownArgs& d, void* bar,
                            int bits, cudaStream_t stream,
-                           const slx_fill_service* svc = nullptr);
+                           const slx_fill_service* svc = nullptr,
+                           const slx_ep_exchange* ep = nullptr);
+int launch_ep_combine_rmsnorm(const slx_ep_exchange& ep, const float* scores,
+                              int k, int H, int has_shared,
+                              const uint16_t* h_in, const uint16_t* w,
+                              float eps, uint16_t* h_out, uint16_t* y,
+                              int32_t* status, cudaStream_t s);
 int launch_dequant_rows(const uint32_t* w, const uint16_t* s, const uint16_t* b,
                         int in, int bits, int gs, const int32_t* rows,
                         int nrows, int n_src_rows, void* out, int out_bf16,

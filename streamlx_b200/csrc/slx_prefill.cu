@@ -24,12 +24,19 @@
 // Exact affine arithmetic on fp16 tensor cores.  MLX affine 2-bit weights
 // are w = s*q + b per group of 64 (s, b bf16, q in 0..3).  s*q has at most
 // 8 + 2 significant bits, so it is EXACT in fp16 (11 bits) whenever
-// 2^-17 <= |s| and 3|s| <= 65504; the dequant warps produce it with one fp16
-// FMA on the magic-number expansion (1024 + q) * s - 1024 * s.  The bias
-// term b * sum(x over the group) rides on extra K columns: per group two
-// columns, weights (b, b), activations (hi, lo) with hi + lo = the fp32
-// group sum.  Activations enter as fp16 (bf16 values are exact in fp16 for
-// 2^-14 <= |x| < 65504; below that the rounding error is < 2^-25).  So each
+// 2^-17 <= |s| (its last bit >= the fp16 subnormal step 2^-24); the dequant
+// warps produce it with one fp16 FMA on the magic-number expansion
+// (1024 + q) * s - 1024 * s, whose addend 1024 * s must itself be finite:
+// |s| < 64.  The bias term b * sum(x over the group) rides on extra K
+// columns: per group two columns, weights (b, b), activations (hi, lo) with
+// hi + lo = the fp32 group sum; b is exact in fp16 for 2^-17 <= |b| <
+// 65504.  Activations and SwiGLU outputs enter as fp16 (bf16 values are
+// exact there for 2^-17 <= |x| < 65504; a smaller one is off by < 2^-25),
+// and a group sum must stay below 65504.  The kernels check every scale,
+// bias, activation and group sum against those bounds (s = 0 and b = 0 are
+// exact) and report SLX_ERR_RANGE instead of a wrong result; the host then
+// runs the call on the GEMV kernels, whose scale/bias arithmetic is fp32.
+// So each
 // output is sum_i s*q_i*x_i + b*sum x accumulated in fp32 -- the value MLX's
 // quantized matrix-vector product forms (scale * dot(q, x) + bias * sum(x))
 // -- and the rounding points are those of switch_forward: gate / up to bf16,
@@ -100,6 +107,8 @@ constexpr int kThreads = 448;
 constexpr int kDqThreads = 256;     // one weight row each
 constexpr int kDqDepth = 4;         // cp.async chunks in flight per thread
 constexpr int kTmemCols = 512;      // two 256-column accumulators
+constexpr float kF16Max = 65504.f;   // largest finite fp16
+constexpr float kTiny = 7.62939453125e-06f;  // 2^-17: smaller loses bits
 
 // Tuning (compile-time; the defaults are the shipped configuration).
 #ifndef SLX_PF_L2_PREFETCH
@@ -475,13 +484,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_ld16(tq + 128 + 64 * jg + cc, uv);
             tc_wait_ld();
             float h[16];
+            bool big = false;
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
               const float gt = round_bf16(__uint_as_float(gv[i]));
               const float up = round_bf16(__uint_as_float(uv[i]));
               h[i] = round_bf16(silu_f32(gt) * up);
               hs += h[i];
+              big |= !(fabsf(h[i]) < kF16Max);
             }
+            if (valid && (big || !(fabsf(hs) < kF16Max)))
+              set_status(a.status, SLX_ERR_RANGE);
             // 16 I rows 16w..16w+15 of the group fill positions 16w..16w+15
             // (permuted order): word j = (h[j], h[j+8]), units 2w and 2w+1
             uint32_t hw[8];
@@ -591,6 +604,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       uint32_t out[32];
       if (c < a.nG) {
+        {  // operand range of the exact fp16 affine form (see the top)
+          const float fs = fabsf(bf16_lo(sbw)), fb = fabsf(bf16_hi(sbw));
+          const bool bad = !(fs < 64.f) || (fs != 0.f && fs < kTiny) ||
+                           !(fb < kF16Max) || (fb != 0.f && fb < kTiny);
+          if (__any_sync(0xffffffffu, bad) && lane == 0)
+            set_status(a.status, SLX_ERR_RANGE);
+        }
         const __half s16 = __float2half_rn(bf16_lo(sbw));
         // this thread's row only: written here, read back at the bias chunk
         btab[c * kDqThreads + n] = __float2half_rn(bf16_hi(sbw));
@@ -659,19 +679,23 @@ __global__ void __launch_bounds__(256)
   }
   if (n >= bl.z) return;
   const int xr = pair_row[bl.y + n];
-  if (xr < 0 || xr >= n_rows) {
-    if (lane == 0) set_status(status, SLX_ERR_OUT_OF_RANGE);
-    return;
-  }
-  const uint16_t* xrow = x + (size_t)xr * H;
+  // a bad row index is reported and the pair's image row written as zeros,
+  // so its (skipped-in-spirit) output is deterministic
+  const bool row_ok = xr >= 0 && xr < n_rows;
+  if (!row_ok && lane == 0) set_status(status, SLX_ERR_OUT_OF_RANGE);
+  const uint16_t* xrow = x + (size_t)(row_ok ? xr : 0) * H;
   uint8_t* blk = img + (size_t)b * nC * kActB;
   const int u = lane & 7;            // 16-byte unit of the chunk row
   const int i = u >> 1, j0 = 4 * (u & 1);
+  bool big = false;
   for (int c0 = 0; c0 < nG; c0 += 4) {
     const int c = c0 + (lane >> 3);
     const uint16_t* src = xrow + 64 * c + 16 * i + j0;
-    const uint2 lo4 = *reinterpret_cast<const uint2*>(src);      // elements j0..j0+3
-    const uint2 hi4 = *reinterpret_cast<const uint2*>(src + 8);  // j0+8..j0+11
+    uint2 lo4 = make_uint2(0, 0), hi4 = make_uint2(0, 0);
+    if (row_ok) {
+      lo4 = *reinterpret_cast<const uint2*>(src);      // elements j0..j0+3
+      hi4 = *reinterpret_cast<const uint2*>(src + 8);  // j0+8..j0+11
+    }
     const uint32_t lw[4] = {lo4.x & 0xFFFFu, lo4.x >> 16, lo4.y & 0xFFFFu, lo4.y >> 16};
     const uint32_t hw[4] = {hi4.x & 0xFFFFu, hi4.x >> 16, hi4.y & 0xFFFFu, hi4.y >> 16};
     uint32_t o[4];
@@ -680,6 +704,7 @@ __global__ void __launch_bounds__(256)
     for (int k = 0; k < 4; ++k) {
       const float a0 = bf16_to_f32((uint16_t)lw[k]);
       const float a1 = bf16_to_f32((uint16_t)hw[k]);
+      big |= !(fabsf(a0) < kF16Max) || !(fabsf(a1) < kF16Max);
       s += a0 + a1;
       o[k] = (uint32_t)h_bits(__float2half_rn(a0)) |
              ((uint32_t)h_bits(__float2half_rn(a1)) << 16);
@@ -689,6 +714,7 @@ __global__ void __launch_bounds__(256)
     s += __shfl_xor_sync(0xffffffffu, s, 1);
     s += __shfl_xor_sync(0xffffffffu, s, 2);
     s += __shfl_xor_sync(0xffffffffu, s, 4);
+    big |= !(fabsf(s) < kF16Max);
     if (u == 0) {
       const __half hi = __float2half_rn(s);
       const __half lo = __float2half_rn(s - __half2float(hi));
@@ -699,6 +725,8 @@ __global__ void __launch_bounds__(256)
           (uint32_t)h_bits(hi) | ((uint32_t)h_bits(lo) << 16);
     }
   }
+  if (__any_sync(0xffffffffu, big) && lane == 0 && row_ok)
+    set_status(status, SLX_ERR_RANGE);
 }
 
 // ------------------------------------------------------------ launchers --

@@ -126,9 +126,51 @@ SLX_DEV TileInfo gemv_tile(const GemvArgs& a, int q, SlotCache& sc) {
 // act_scale (a power of two: exact); xsum[G] = sum of the group's 64
 // activations (the bias term of the affine identity).  One (group, tig)
 // task per thread, all units at once: a single round of global loads.
+// An activation the fp16 fragments cannot hold (|x * factor| >= 65504
+// would become inf; non-finite inputs) is reported as SLX_ERR_RANGE.
+constexpr float kF16Max = 65504.f;
+
+// The tensor cores lose low-order bits of a k16 sum when its products are
+// tiny (fp16-subnormal code operands times small activations: measured
+// 0.1-24% of bf16 outputs off by an ulp, falling to ~0.05% once the
+// activations are raised by 2^6..2^12).  So each activation vector enters
+// the fp16 fragments multiplied by a power of two 2^e chosen per vector
+// (its largest magnitude lands in [2^12, 2^13)), and the SwiGLU outputs by
+// the fixed kHScale; the fold divides by the same power of two, so the
+// arithmetic is exact up to that scaling.
+constexpr float kHScale = 64.f;       // 2^6 on the down projection's input
+constexpr float kHUnit = 262144.f;    // 2^24 / kHScale
+
+SLX_DEV float pow2f(int e) { return __int_as_float((127 + e) << 23); }
+
+// Exponent e for a vector whose largest |value| is m (0: e = 0).
+SLX_DEV int vec_exp(float m) {
+  if (!(m > 0.f) || !(m < 3.0e38f)) return 0;
+  int ex;
+  frexpf(m, &ex);                     // m = f * 2^ex, f in [0.5, 1)
+  int e = 13 - ex;                    // m * 2^e in [2^12, 2^13)
+  return e < -60 ? -60 : (e > 60 ? 60 : e);
+}
+
+// Largest |x| of n bf16 values (8 per 16-byte load), this thread's share.
+SLX_DEV float absmax_part(const uint16_t* x, int n, int t, int nt) {
+  float m = 0.f;
+  for (int c = 8 * t; c < n; c += 8 * nt) {
+    const uint4 v = *reinterpret_cast<const uint4*>(x + c);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      m = fmaxf(m, fmaxf(fabsf(bf16_lo(w[q])), fabsf(bf16_hi(w[q]))));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  return m;
+}
+
 template <int BITS>
 SLX_DEV void frag_task(const uint16_t* __restrict__ x, int G, int tig,
-                       uint32_t* frag, float* part) {
+                       uint32_t* frag, float* part, int32_t* status,
+                       float vscale) {
   const uint4* src = reinterpret_cast<const uint4*>(x + 64 * G + 16 * tig);
   const uint4 q0 = src[0], q1 = src[1];
   const uint32_t w8[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
@@ -138,8 +180,11 @@ SLX_DEV void frag_task(const uint16_t* __restrict__ x, int G, int tig,
     const int cl = col_lo(BITS, j), ch = col_hi(BITS, j);
     const float xl = (cl & 1) ? bf16_hi(w8[cl >> 1]) : bf16_lo(w8[cl >> 1]);
     const float xh = (ch & 1) ? bf16_hi(w8[ch >> 1]) : bf16_lo(w8[ch >> 1]);
-    frag[(G * 4 + tig) * 8 + j] =
-        pack_f16x2(xl * act_scale(BITS, cl), xh * act_scale(BITS, ch));
+    const float sl = xl * vscale * act_scale(BITS, cl);
+    const float sh = xh * vscale * act_scale(BITS, ch);
+    if (status && !(fabsf(sl) < kF16Max && fabsf(sh) < kF16Max))
+      set_status(status, SLX_ERR_RANGE);
+    frag[(G * 4 + tig) * 8 + j] = pack_f16x2(sl, sh);
     s += xl + xh;
   }
   part[G * 4 + tig] = s;
@@ -201,8 +246,8 @@ SLX_DEV void named_bar_consumers() {
 }
 
 // fold one group: acc += scale * sum(q*x) + bias * sum(x); sb = scale|bias
-SLX_DEV float fold(float acc, float d, uint32_t sb, float xs) {
-  acc = fmaf(bf16_lo(sb) * kSubnormalUnit, d, acc);
+SLX_DEV float fold(float acc, float d, uint32_t sb, float xs, float unit) {
+  acc = fmaf(bf16_lo(sb) * unit, d, acc);
   return fmaf(bf16_hi(sb), xs, acc);
 }
 
@@ -256,8 +301,11 @@ SLX_DEV void gemv_epilogue(const GemvArgs& a, const TileInfo& t,
   const int cl = col_lo(BITS, j), ch = col_hi(BITS, j);
   const float lo = __shfl_sync(0xffffffffu, hv, (cl & 7) * 4 + (cl >> 3));
   const float hi = __shfl_sync(0xffffffffu, hv, (ch & 7) * 4 + (ch >> 3));
-  const uint32_t word =
-      pack_f16x2(lo * act_scale(BITS, cl), hi * act_scale(BITS, ch));
+  const float slo = lo * (kHScale * act_scale(BITS, cl));
+  const float shi = hi * (kHScale * act_scale(BITS, ch));
+  if (!(fabsf(slo) < kF16Max && fabsf(shi) < kF16Max))
+    set_status(a.status, SLX_ERR_RANGE);
+  const uint32_t word = pack_f16x2(slo, shi);
   float hsum = hv;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) hsum += __shfl_xor_sync(0xffffffffu, hsum, o);
@@ -352,6 +400,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int mat = tig >> 1;
   const int sbl = mat * 16 + g + 8 * (tig & 1);  // this lane's SB word slot
   int cached_token = -1;
+  float vunit = kSubnormalUnit;
   SlotCache scache;
   for (int q = q_begin, i = 0; q < q_end; ++q, ++i) {
     const int st = i % NS;
@@ -359,8 +408,19 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (t.token != cached_token) {
       named_bar_consumers();
       const uint16_t* xr = a.x + (size_t)t.token * a.in;
+      // per-token scale: the consumers' max |x| meets in frag[] (rebuilt
+      // right after, and nobody reads the old fragments any more)
+      const float m = absmax_part(xr, a.in, ct, kNW * 32);
+      if (lane == 0) reinterpret_cast<float*>(frag)[cw] = m;
+      named_bar_consumers();
+      float mm = 0.f;
+      for (int w = 0; w < kNW; ++w)
+        mm = fmaxf(mm, reinterpret_cast<const float*>(frag)[w]);
+      const int ve = vec_exp(mm);
+      vunit = pow2f(24 - ve);
+      named_bar_consumers();
       for (int p = ct; p < 4 * nG; p += kNW * 32)
-        frag_task<BITS>(xr, p >> 2, p & 3, frag, part);
+        frag_task<BITS>(xr, p >> 2, p & 3, frag, part, a.status, pow2f(ve));
       named_bar_consumers();
       frag_sums(part, xsum, nG, ct, kNW * 32);
       named_bar_consumers();
@@ -393,11 +453,11 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         const float v = mat == 0 ? ((tig & 1) ? d0[2] : d0[0])
                                  : ((tig & 1) ? d1[2] : d1[0]);
-        acc = fold(acc, v, SB[G * 32 + sbl], xsum[G]);
+        acc = fold(acc, v, SB[G * 32 + sbl], xsum[G], vunit);
         if (two) {
           const float v2 = mat == 0 ? ((tig & 1) ? e0[2] : e0[0])
                                     : ((tig & 1) ? e1[2] : e1[0]);
-          acc = fold(acc, v2, SB[G2 * 32 + sbl], xsum[G2]);
+          acc = fold(acc, v2, SB[G2 * 32 + sbl], xsum[G2], vunit);
         }
       }
     }
@@ -438,9 +498,11 @@ SLX_DEV float down_unit_groups(const uint8_t* S, int in, int cw, int g,
     float d[4], e[4] = {0.f, 0.f, 0.f, 0.f};
     group_mma<BITS>(S, RB, swz, G, g, tig, b, d);
     if (two) group_mma<BITS>(S, RB, swz, G2, g, tig, b2, e);
-    acc = fold(acc, (tig & 1) ? d[2] : d[0], SB[G * 16 + rrow], xs[G]);
+    acc = fold(acc, (tig & 1) ? d[2] : d[0], SB[G * 16 + rrow], xs[G],
+               kHUnit);
     if (two)
-      acc = fold(acc, (tig & 1) ? e[2] : e[0], SB[G2 * 16 + rrow], xs[G2]);
+      acc = fold(acc, (tig & 1) ? e[2] : e[0], SB[G2 * 16 + rrow], xs[G2],
+                 kHUnit);
   }
   return acc;
 }
@@ -679,6 +741,11 @@ static int num_sms() {
 constexpr int kFusedSmemMax = 220 * 1024;
 constexpr int kFW = 16;                   // compute warps
 constexpr int kFThreads = 32 * (kFW + 1);
+
+// barrier of the fused kernel's compute warps only
+SLX_DEV void named_bar_fused() {
+  asm volatile("bar.sync 2, %0;" ::"n"(kFW * 32) : "memory");
+}
 constexpr int kFMaxA = 8;                 // gate/up tiles per CTA
 constexpr int kFMaxB = 64;                // down tiles per CTA
 constexpr int kFMaxUnits = 64;
@@ -705,6 +772,14 @@ struct FusedArgs {
   int32_t* svc_go;
   int32_t* svc_table;
   long long svc_wait_ns;
+  // expert parallelism (slx_ep_exchange): the per-unit bf16 rows of the
+  // units this rank owns go to every rank's receive block, then every CTA
+  // counts itself on every rank's counter of this layer; ids without a slot
+  // here belong to another rank (not an error)
+  int ep_on, ep_rank, ep_nranks, ep_layer, ep_layers;
+  const int32_t* ep_stamp;
+  uint16_t* ep_recv[SLX_EP_MAX_RANKS];
+  unsigned int* ep_count[SLX_EP_MAX_RANKS];
 };
 
 SLX_DEV unsigned long long ld_acquire_u64(const unsigned long long* p) {
@@ -891,7 +966,49 @@ SLX_DEV float down_group(const uint8_t* S, int in, int G, int g, int tig,
   float dd[4];
   group_mma<BITS>(S, RB, swz, G, g, tig, b, dd);
   (void)nG;
-  return fold(0.f, (tig & 1) ? dd[2] : dd[0], SB[G * 16 + rrow], xs[G]);
+  return fold(0.f, (tig & 1) ? dd[2] : dd[0], SB[G * 16 + rrow], xs[G],
+              kHUnit);
+}
+
+// Rows row0..row0+15 of unit j (lanes 0..15 hold them) into the receive
+// block of this step and layer: a routed unit to every rank, the shared
+// expert (unit k, computed by every rank) to this rank only.
+SLX_DEV void ep_write_rows(const FusedArgs& f, const DownArgs& d, int j,
+                           int row0, float y, int lane) {
+  const uint32_t b = lane < kRows ? (uint32_t)f32_to_bf16(y) : 0u;
+  uint32_t w[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int src = (lane & 1) * 8 + 2 * q;
+    const uint32_t lo = __shfl_sync(0xffffffffu, b, src);
+    const uint32_t hi = __shfl_sync(0xffffffffu, b, src + 1);
+    w[q] = lo | (hi << 16);
+  }
+  if (lane >= 2) return;
+  const int stamp = *f.ep_stamp;
+  const size_t block = ((size_t)(stamp & 1) * f.ep_layers + f.ep_layer) *
+                       (size_t)(d.k + 1) * d.H;
+  const size_t off = block + (size_t)j * d.H + row0 + 8 * lane;
+  const uint4 v = make_uint4(w[0], w[1], w[2], w[3]);
+  if (j >= d.k) {
+    *reinterpret_cast<uint4*>(f.ep_recv[f.ep_rank] + off) = v;
+    return;
+  }
+  for (int r = 0; r < f.ep_nranks; ++r)
+    *reinterpret_cast<uint4*>(f.ep_recv[r] + off) = v;
+}
+
+// This CTA's rows are written (every thread's stores are ordered before
+// thread 0's by the preceding barrier): count the CTA on every rank.
+SLX_DEV void ep_signal(const FusedArgs& f) {
+  if (threadIdx.x != 0) return;
+  const int stamp = *f.ep_stamp;
+  const int slot = (stamp & 1) * f.ep_layers + f.ep_layer;
+  __threadfence_system();
+  for (int r = 0; r < f.ep_nranks; ++r)
+    asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(
+                     f.ep_count[r] + slot)
+                 : "memory");
 }
 
 template <int BITS>
@@ -913,6 +1030,8 @@ __global__ void __launch_bounds__(kFThreads, 1)
   float* redB = reinterpret_cast<float*>(smem + f.off_redb);  // [tiles][nGmax][16]
   uint8_t* stB = smem + f.off_stage_b;
   int* meta = reinterpret_cast<int*>(smem + f.off_meta);      // A tile valid + B unit valid
+  __shared__ float s_vmax[kFW];
+  __shared__ float s_vunit;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G_ = gridDim.x, bid = blockIdx.x;
   const int nG = tile_ng(a.in);
@@ -956,7 +1075,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
       SlotCache c;
       const TileInfo t = gemv_tile(a, qa0 + lane, c);
       meta[lane] = t.valid;
-      if (!t.valid) set_status(a.status, SLX_ERR_UNMAPPED_EXPERT);
+      if (!t.valid && !f.ep_on) set_status(a.status, SLX_ERR_UNMAPPED_EXPERT);
       gemv_issue<BITS>(a, t, stA + (size_t)lane * f.stage_a, &fullA[lane], pol);
     }
   }
@@ -978,7 +1097,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
         src = d.shared + d.a_bytes_sh + (size_t)rb * d.tile_bytes_sh;
       }
       if (s < U) meta[kFMaxA + j] = valid;
-      if (!valid) set_status(d.status, SLX_ERR_UNMAPPED_EXPERT);
+      if (!valid && !f.ep_on) set_status(d.status, SLX_ERR_UNMAPPED_EXPERT);
       if (valid) {
         mbar_arrive_expect_tx(&fullB[s], bytes);
         bulk_g2s(stB + (size_t)s * f.stage_b, src, bytes, &fullB[s], pol);
@@ -990,12 +1109,20 @@ __global__ void __launch_bounds__(kFThreads, 1)
   if (warp == 0) {
     if (!f.b_late) issue_b();
   } else {
-    // ---- activation fragments of the token ----
+    // ---- activation fragments of the token (per-token scale first) ----
     const int ct = threadIdx.x - 32;
+    const float m = absmax_part(a.x, a.in, ct, kFW * 32);
+    if (lane == 0) s_vmax[warp - 1] = m;
+    named_bar_fused();
+    float mm = 0.f;
+    for (int w = 0; w < kFW; ++w) mm = fmaxf(mm, s_vmax[w]);
+    const int ve = vec_exp(mm);
+    if (ct == 0) s_vunit = pow2f(24 - ve);
     for (int p = ct; p < 4 * nG; p += kFW * 32)
-      frag_task<BITS>(a.x, p >> 2, p & 3, frag, part);
+      frag_task<BITS>(a.x, p >> 2, p & 3, frag, part, a.status, pow2f(ve));
   }
   __syncthreads();
+  const float vunit = s_vunit;
   if (warp > 0) frag_sums(part, xsum, nG, threadIdx.x - 32, kFW * 32);
   __syncthreads();
   SLX_TRACE_POINT(0, 1);
@@ -1031,11 +1158,11 @@ __global__ void __launch_bounds__(kFThreads, 1)
           }
           const float v = mat == 0 ? ((tig & 1) ? d0[2] : d0[0])
                                    : ((tig & 1) ? d1[2] : d1[0]);
-          acc = fold(acc, v, SB[G * 32 + sbl], xsum[G]);
+          acc = fold(acc, v, SB[G * 32 + sbl], xsum[G], vunit);
           if (two) {
             const float v2 = mat == 0 ? ((tig & 1) ? e0[2] : e0[0])
                                       : ((tig & 1) ? e1[2] : e1[0]);
-            acc = fold(acc, v2, SB[G2 * 32 + sbl], xsum[G2]);
+            acc = fold(acc, v2, SB[G2 * 32 + sbl], xsum[G2], vunit);
           }
         }
       }
@@ -1059,7 +1186,10 @@ __global__ void __launch_bounds__(kFThreads, 1)
   __syncthreads();
   SLX_TRACE_POINT(0, 7);
   pdl_launch_dependents();
-  if (nb == 0) return;
+  if (nb == 0) {
+    if (f.ep_on) ep_signal(f);
+    return;
+  }
 
   // ---- phase B: fragments of every unit, then (unit, group) tasks ----
   {
@@ -1127,14 +1257,23 @@ __global__ void __launch_bounds__(kFThreads, 1)
       if (lane < kRows)
         for (int G = 0; G < ng; ++G) v += redB[((size_t)s * nGmax + G) * kRows + lane];
       const float y = meta[kFMaxA + j] ? round_bf16(v) : 0.f;
+      if (f.ep_on) {
+        if (meta[kFMaxA + j]) ep_write_rows(f, d, j, row0, y, lane);
+        continue;
+      }
       if (!d.scores) {
         if (lane < kRows)
           d.out[(size_t)j * d.H + row0 + lane] = f32_to_bf16(y);
       } else {
-        y_out += (j < d.k) ? d.scores[j] * y : y;
+        y_out = (j < d.k) ? fmaf(d.scores[j], y, y_out) : y_out + y;
       }
     }
-    if (d.scores && lane < kRows) d.out[row0 + lane] = f32_to_bf16(y_out);
+    if (d.scores && !f.ep_on && lane < kRows)
+      d.out[row0 + lane] = f32_to_bf16(y_out);
+  }
+  if (f.ep_on) {
+    __syncthreads();
+    ep_signal(f);
   }
   SLX_TRACE_POINT(0, 10);
 }
@@ -1213,12 +1352,25 @@ static int launch_fused_t(FusedArgs f, cudaStream_t stream) {
 
 int launch_switchglu_fused(const GemvArgs& a, const DownArgs& d, void* bar,
                            int bits, cudaStream_t stream,
-                           const slx_fill_service* svc) {
+                           const slx_fill_service* svc,
+                           const slx_ep_exchange* ep) {
   if (a.T != 1 || d.T != 1) return SLX_ERR_UNSUPPORTED;
   FusedArgs f = {};
   f.a = a;
   f.d = d;
   f.bar = reinterpret_cast<unsigned long long*>(bar);
+  if (ep) {
+    f.ep_on = 1;
+    f.ep_rank = ep->rank;
+    f.ep_nranks = ep->n_ranks;
+    f.ep_layer = ep->layer;
+    f.ep_layers = ep->n_layers;
+    f.ep_stamp = ep->stamp;
+    for (int r = 0; r < ep->n_ranks; ++r) {
+      f.ep_recv[r] = reinterpret_cast<uint16_t*>(ep->recv[r]);
+      f.ep_count[r] = ep->count[r];
+    }
+  }
   if (svc) {
     f.svc_on = 1;
     f.svc_layer = svc->layer;

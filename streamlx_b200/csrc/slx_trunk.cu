@@ -89,6 +89,127 @@ __global__ void __launch_bounds__(kNormThreads) k_add_rmsnorm(
   }
 }
 
+// Expert-parallel combine (slx_ep_exchange): wait until every rank has
+// counted every CTA of its SwitchGLU launch for this step and layer, then
+// delta = bf16(sum_j fma(score_j, row_j) (+ shared row)) -- the same fp32
+// operations in the same unit order as the single-GPU fused kernel -- and
+// the residual add + RMSNorm of k_add_rmsnorm on it (same arithmetic).
+__global__ void __launch_bounds__(kNormThreads) k_ep_combine_rmsnorm(
+    const slx_ep_exchange ep, const float* scores, int k, int H,
+    int has_shared, const uint16_t* h_in, const uint16_t* w, float eps,
+    uint16_t* h_out, uint16_t* y, int32_t* status) {
+  __shared__ float red[32];
+  __shared__ int s_ok;
+  pdl_launch_dependents();
+  pdl_wait_primary();
+  const int stamp = *ep.stamp;
+  if (threadIdx.x == 0) {
+    s_ok = 1;
+    if (ep.grid > 0) {
+      // counters per (stamp parity, layer): this parity's steps so far,
+      // each counted by every CTA of every rank
+      const unsigned int want = (unsigned int)((stamp + 1) >> 1) *
+                                (unsigned int)(ep.n_ranks * ep.grid);
+      const unsigned int* cnt =
+          ep.count[ep.rank] + (stamp & 1) * ep.n_layers + ep.layer;
+      const uint64_t t0 = globaltimer_ns();
+      for (uint32_t i = 0;; ++i) {
+        unsigned int v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];"
+                     : "=r"(v) : "l"(cnt) : "memory");
+        if ((int)(v - want) >= 0) break;
+        if ((i & 63u) == 0 && globaltimer_ns() - t0 > (uint64_t)ep.wait_ns) {
+          set_status(status, SLX_ERR_DEVICE_TIMEOUT);
+          s_ok = 0;
+          break;
+        }
+        if (i > 256) __nanosleep(64);
+      }
+    }
+  }
+  __syncthreads();
+  const uint16_t* blk =
+      reinterpret_cast<const uint16_t*>(ep.recv[ep.rank]) +
+      ((size_t)(stamp & 1) * ep.n_layers + ep.layer) * (size_t)(k + 1) * H;
+  uint4 v[kNormMaxChunks];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < kNormMaxChunks; ++j) {
+    const int c = (j * kNormThreads + threadIdx.x) * 8;
+    if (c >= H) break;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (s_ok) {
+      for (int u = 0; u < k; ++u) {
+        const float sc = scores[u];
+        const uint4 r = __ldcg(reinterpret_cast<const uint4*>(
+            blk + (size_t)u * H + c));
+        const uint32_t rw[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          acc[2 * q] = fmaf(sc, bf16_lo(rw[q]), acc[2 * q]);
+          acc[2 * q + 1] = fmaf(sc, bf16_hi(rw[q]), acc[2 * q + 1]);
+        }
+      }
+      if (has_shared) {
+        const uint4 r = __ldcg(reinterpret_cast<const uint4*>(
+            blk + (size_t)k * H + c));
+        const uint32_t rw[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          acc[2 * q] = acc[2 * q] + bf16_lo(rw[q]);
+          acc[2 * q + 1] = acc[2 * q + 1] + bf16_hi(rw[q]);
+        }
+      }
+    }
+    uint4 a = *reinterpret_cast<const uint4*>(h_in + c);
+    uint32_t* pa = reinterpret_cast<uint32_t*>(&a);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float dlo = round_bf16(acc[2 * q]), dhi = round_bf16(acc[2 * q + 1]);
+      const float lo = round_bf16(bf16_lo(pa[q]) + dlo);
+      const float hi = round_bf16(bf16_hi(pa[q]) + dhi);
+      pa[q] = (uint32_t)f32_to_bf16(lo) | ((uint32_t)f32_to_bf16(hi) << 16);
+    }
+    *reinterpret_cast<uint4*>(h_out + c) = a;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float lo = bf16_lo(pa[q]), hi = bf16_hi(pa[q]);
+      ss += lo * lo + hi * hi;
+    }
+    v[j] = a;
+  }
+  ss = breduce(ss, red, [](float a, float b) { return a + b; });
+  const float inv = rsqrtf(ss / (float)H + eps);
+#pragma unroll
+  for (int j = 0; j < kNormMaxChunks; ++j) {
+    const int c = (j * kNormThreads + threadIdx.x) * 8;
+    if (c >= H) break;
+    const uint4 wv = *reinterpret_cast<const uint4*>(w + c);
+    const uint32_t* pa = reinterpret_cast<const uint32_t*>(&v[j]);
+    const uint32_t* pw = reinterpret_cast<const uint32_t*>(&wv);
+    uint4 o;
+    uint32_t* po = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint16_t lo = f32_to_bf16(bf16_lo(pa[q]) * inv * bf16_lo(pw[q]));
+      const uint16_t hi = f32_to_bf16(bf16_hi(pa[q]) * inv * bf16_hi(pw[q]));
+      po[q] = (uint32_t)lo | ((uint32_t)hi << 16);
+    }
+    *reinterpret_cast<uint4*>(y + c) = o;
+  }
+}
+
+int launch_ep_combine_rmsnorm(const slx_ep_exchange& ep, const float* scores,
+                              int k, int H, int has_shared,
+                              const uint16_t* h_in, const uint16_t* w,
+                              float eps, uint16_t* h_out, uint16_t* y,
+                              int32_t* status, cudaStream_t s) {
+  if (H % 8 || H > 8 * kNormThreads * kNormMaxChunks) return SLX_ERR_UNSUPPORTED;
+  return launch_k(k_ep_combine_rmsnorm, dim3(1), dim3(kNormThreads), 0, s, ep,
+                  scores, k, H, has_shared, h_in, w, eps, h_out, y, status) ==
+                 cudaSuccess ? SLX_OK : SLX_ERR_CUDA;
+}
+
 // qkv row layout: [nq*hd | nkv*hd | nkv*hd].  Per head: RMSNorm over hd with
 // q_norm / k_norm, then rotate-half RoPE at pos[t]; q written back in place,
 // k and v appended to the caches at row pos[t].

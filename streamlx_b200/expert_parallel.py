@@ -23,7 +23,7 @@ contiguous id blocks) fully resident, and a layer call is
     each rank computes only the pairs whose expert it owns, combines them
     (score-weighted, fp32), and one all-reduce sums the partial outputs.
 
-No collective needs TMA or multicast loads: rows land in this GPU's memory
+No collective needs TMA or cluster-broadcast loads: rows land in this GPU's memory
 through NCCL before any kernel reads them.
 """
 
@@ -190,3 +190,80 @@ def load_local_experts(model_dir: str, layer: int, n_experts: int,
     pool.begin_call()
     pool.ensure(list(range(e0, e1)))
     return pool
+
+
+# ----------------------------------------------------------------------
+# Expert-parallel decode over NVLink peer memory (slx_ep_exchange)
+
+
+class EpExchange:
+    """Receive blocks and counters of the expert-parallel decoder on one
+    rank, with every peer's mapped through CUDA IPC.
+
+    Layout (include/streamlx_cuda.h, slx_ep_exchange): recv bf16
+    [2][n_layers][k + 1][hidden], counters uint32 [2][n_layers].  The
+    SwitchGLU launch of each rank writes its owned units' rows into every
+    rank's block and counts its CTAs on every rank's counter; each rank's
+    combine kernel waits on its own counter.  The handles are exchanged with
+    one all_gather_object over the process group (any backend)."""
+
+    def __init__(self, n_layers: int, k: int, hidden: int, device,
+                 group=None, wait_s: float = 10.0):
+        from . import _lib as L
+        self.L = L
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if self.world > L.EP_MAX_RANKS:
+            raise ValueError(f"{self.world} ranks > {L.EP_MAX_RANKS}")
+        self.n_layers, self.k, self.hidden = n_layers, k, hidden
+        self.device = device
+        self.grid = L.ep_grid()
+        self.wait_ns = int(wait_s * 1e9)
+        self.recv = torch.zeros(2 * n_layers * (k + 1) * hidden,
+                                dtype=torch.bfloat16, device=device)
+        self.count = torch.zeros(max(64, 2 * n_layers), dtype=torch.int32,
+                                 device=device)
+        torch.cuda.synchronize(device)
+        mine = (L.ipc_handle(self.recv), L.ipc_handle(self.count), self.grid)
+        allh = [None] * self.world
+        dist.all_gather_object(allh, mine, group=group)
+        grids = {g[2] for g in allh}
+        if len(grids) != 1:
+            raise RuntimeError(f"ranks disagree on the SwitchGLU grid: {grids}")
+        self._opened: list[int] = []
+        self.recv_ptr: list[int] = []
+        self.count_ptr: list[int] = []
+        for r, ((hr, offr), (hc, offc), _) in enumerate(allh):
+            if r == self.rank:
+                self.recv_ptr.append(self.recv.data_ptr())
+                self.count_ptr.append(self.count.data_ptr())
+                continue
+            br = L.ipc_open(hr)
+            self._opened.append(br)
+            bc = br if hc == hr else L.ipc_open(hc)
+            if bc != br:
+                self._opened.append(bc)
+            self.recv_ptr.append(br + offr)
+            self.count_ptr.append(bc + offc)
+        dist.barrier(group=group)
+
+    def struct(self, layer: int, stamp_ptr: int, warmup: bool = False):
+        L = self.L
+        recv = (C_VOID * 8)(*(self.recv_ptr + [0] * (8 - self.world)))
+        count = (C_VOID * 8)(*(self.count_ptr + [0] * (8 - self.world)))
+        return L.slx_ep_exchange(self.rank, self.world, layer, self.n_layers,
+                                 stamp_ptr, recv, count,
+                                 0 if warmup else self.grid, self.wait_ns)
+
+    def close(self) -> None:
+        for b in self._opened:
+            try:
+                self.L.ipc_close(b)
+            except Exception:   # noqa: BLE001 - best effort at teardown
+                pass
+        self._opened = []
+
+
+import ctypes as _ctypes  # noqa: E402
+
+C_VOID = _ctypes.c_void_p

@@ -446,14 +446,23 @@ class IdTokenizer:
 def load_streaming_model(model_dir: str, budget_bytes: int, k: int = 8,
                          trust_remote_code: bool = False,
                          tokenizer_config: dict | None = None,
-                         resident: str | None = None, device=None):
+                         resident: str | None = None, device=None,
+                         expert_parallel: bool = False, ep_group=None):
     """Build the decoder with every MoE layer pool-backed.  Returns
-    ``(model, tokenizer, pools, reader)`` (integrate.py:397-473)."""
+    ``(model, tokenizer, pools, reader)`` (integrate.py:397-473).
+
+    ``expert_parallel``: one process per GPU under torch.distributed; this
+    rank keeps only its block of every layer's experts, all resident (the
+    budget is not used), and decode steps exchange the experts' outputs
+    over NVLink peer memory (no reference counterpart)."""
     from .model import SynthDecoder
     index = SafetensorsIndex(model_dir)
     reader = ExpertReader(index)
     model = SynthDecoder.from_checkpoint(model_dir, index, device=device)
     moe_layers = list(range(model.cfg.layers))
+    if expert_parallel:
+        return _load_expert_parallel(model, model_dir, index, reader,
+                                     moe_layers, ep_group)
     bpe = {i: index.layer_expert_bytes(i) for i in moe_layers}
     n_exp = {i: index.switch_triples(i)["gate_proj"]["weight"].shape[0]
              for i in moe_layers}
@@ -491,6 +500,32 @@ def load_streaming_model(model_dir: str, budget_bytes: int, k: int = 8,
         rb = sum(n_exp[i] * bpe[i] for i in res_layers) / 2**30
         print(f"[streamlx] {len(res_layers)} fully-resident MoE layers "
               f"({rb:.1f} GiB); {len(streamed)} streamed", file=sys.stderr)
+    return model, IdTokenizer(), pools, reader
+
+
+def _load_expert_parallel(model, model_dir, index, reader, moe_layers,
+                          group):
+    import torch.distributed as dist
+
+    from .expert_parallel import local_range
+    rank = dist.get_rank(group)
+    world = dist.get_world_size(group)
+    pools: dict = {}
+    for i in moe_layers:
+        n_exp = index.switch_triples(i)["gate_proj"]["weight"].shape[0]
+        e0, e1 = local_range(n_exp, world, rank)
+        pool = StreamingSwitchMLP(model_dir, i, max(1, e1 - e0), index=index,
+                                  reader=reader, device=model.device)
+        for a in range(e0, e1, 32):
+            pool.begin_call()
+            pool.ensure(list(range(a, min(a + 32, e1))))
+        pool.sync_device()
+        model.layers[i].mlp.switch_mlp = StreamingSwitchGLU(
+            pool, model.layers[i].mlp.shared_struct())
+        pools[i] = pool
+    for pool in pools.values():
+        pool.flush_hook = model.flush
+    model.enable_expert_parallel(group)
     return model, IdTokenizer(), pools, reader
 
 

@@ -167,6 +167,7 @@ class SynthDecoder:
                            "park_serve": 0.0, "flush": 0.0, "steps": 0,
                            "parks": 0, "park_steps": 0}
         self._step_active = False
+        self.ep = None              # EpExchange when experts are sharded
         # temporal-reuse routing override of the workloads: per (token,
         # layer) a seeded coin decides whether the previous token's expert
         # set is kept (applied identically to the CPU oracle)
@@ -212,6 +213,18 @@ class SynthDecoder:
         self._graphs = None          # links changed: capture again
         return linked
 
+    def enable_expert_parallel(self, group=None, wait_s: float = 10.0):
+        """Shard the experts over the ranks of a process group: this rank's
+        pools hold only its experts, and each decode step exchanges the
+        owned experts' output rows over NVLink peer memory
+        (expert_parallel.EpExchange).  Graph decode only."""
+        from .expert_parallel import EpExchange
+        self.ep = EpExchange(self.cfg.layers, self.cfg.top_k, self.cfg.hidden,
+                             self.device, group=group, wait_s=wait_s)
+        self.use_graphs = True
+        self._graphs = None
+        return self.ep
+
     # -------------------------------------------------------------- decode --
 
     def reset(self) -> None:
@@ -238,8 +251,8 @@ class SynthDecoder:
         the pool bookkeeping in step and serves layers that park on a miss
         (_step_graph).  Otherwise the step runs layer by layer with one host
         sync on the routed ids per layer (_step_eager)."""
-        if self.use_graphs and all(
-                hasattr(la.mlp.switch_mlp, "route") for la in self.layers):
+        if self.ep is not None or (self.use_graphs and all(
+                hasattr(la.mlp.switch_mlp, "route") for la in self.layers)):
             return self._step_graph(token)
         self.flush()
         return self._step_eager(token)
@@ -372,13 +385,23 @@ class SynthDecoder:
         blk = la.mlp
         w = blk.switch_mlp
         eps = cfg.rms_eps
+        stamp = self.g_ctrl.data_ptr() + 4 * (n + 2)
         if i == 0:
             L.dequant_rows(self.embed, H, bits, self.g_ctrl[n + 1:n + 2], 1,
                            cfg.vocab, self.g_emb, self.g_status)
-            h_in, d_in = self.g_emb, None
+            L.add_rmsnorm_out(self.g_emb, None, la.w_in, eps, self.g_s[i],
+                              self.x)
+        elif self.ep is not None:
+            # the previous layer's experts, combined from every rank's rows
+            L.ep_combine_rmsnorm(
+                self.ep.struct(i - 1, stamp, warmup=not serviced),
+                self.g_scores[i - 1], k, H,
+                self.layers[i - 1].mlp.switch_mlp.shared is not None,
+                self.g_m[i - 1], la.w_in, eps, self.g_s[i], self.x,
+                self.g_status)
         else:
-            h_in, d_in = self.g_m[i - 1], self.g_d[i - 1]
-        L.add_rmsnorm_out(h_in, d_in, la.w_in, eps, self.g_s[i], self.x)
+            L.add_rmsnorm_out(self.g_m[i - 1], self.g_d[i - 1], la.w_in, eps,
+                              self.g_s[i], self.x)
         L.qlinear(la.w_qkv, la.n_qkv, H, bits, self.x, self.qkv,
                   self.g_status)
         L.qk_norm_rope_cache(self.qkv, cfg.heads, cfg.kv_heads, cfg.head_dim,
@@ -412,8 +435,13 @@ class SynthDecoder:
         timed = self._glu_timed(i)
         if timed:
             L.event_record_external(ev[0])
-        if serviced:
-            stamp = self.g_ctrl.data_ptr() + 4 * (n + 2)
+        if serviced and self.ep is not None:
+            L.switchglu_ep(pool.store.bank, xm, self.g_ids[i],
+                           self.g_scores[i], pool.store.table_dev,
+                           self.g_glu_scratch, self.g_lstatus[i:i + 1],
+                           self.ep.struct(i, stamp),
+                           shared=sh[0] if sh else None)
+        elif serviced:
             svc = self.svc.svc(i, stamp,
                                self.g_pf_ids[i] if pred else None,
                                self.g_pf_scores[i] if pred else None)
@@ -432,11 +460,20 @@ class SynthDecoder:
         if timed:
             L.event_record_external(ev[1])
 
-    def _record_tail(self) -> None:
+    def _record_tail(self, serviced: bool = True) -> None:
         cfg = self.cfg
         n = cfg.layers
-        L.add_rmsnorm_out(self.g_m[n - 1], self.g_d[n - 1], self.norm,
-                          cfg.rms_eps, self.g_fin, self.x)
+        if self.ep is not None:
+            stamp = self.g_ctrl.data_ptr() + 4 * (n + 2)
+            L.ep_combine_rmsnorm(
+                self.ep.struct(n - 1, stamp, warmup=not serviced),
+                self.g_scores[n - 1], cfg.top_k, cfg.hidden,
+                self.layers[n - 1].mlp.switch_mlp.shared is not None,
+                self.g_m[n - 1], self.norm, cfg.rms_eps, self.g_fin, self.x,
+                self.g_status)
+        else:
+            L.add_rmsnorm_out(self.g_m[n - 1], self.g_d[n - 1], self.norm,
+                              cfg.rms_eps, self.g_fin, self.x)
         L.qlinear(self.w_lm, cfg.vocab, cfg.hidden, cfg.trunk_bits, self.x,
                   self.logits, self.g_status)
         L.argmax(self.logits, self.g_tok_out)
@@ -465,7 +502,7 @@ class SynthDecoder:
         with torch.cuda.stream(s):
             for i in range(n):
                 self._record_layer(i, serviced=False)
-            self._record_tail()
+            self._record_tail(serviced=False)
         s.synchronize()
         self._pred_flags = [self._pred_on(i) for i in range(n)]
         prev_pdl = L.set_pdl(self.pdl)
@@ -626,7 +663,10 @@ class SynthDecoder:
         t1 = time.perf_counter()
         parks0 = ht["parks"]
         try:
-            self._serve_step(stamp)
+            if self.ep is not None:
+                self._ev_done.synchronize()     # resident shards: no service
+            else:
+                self._serve_step(stamp)
         except BaseException:
             self._step_active = False
             self._abort_step(stamp)

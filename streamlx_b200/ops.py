@@ -157,5 +157,40 @@ def prefill_grouped(bank, x2d: torch.Tensor, pair_row, slots, counts, *,
     if need == 0:
         raise L.SlxError("slx_prefill_scratch_bytes", -2, "unsupported shape")
     sc = scratch(need, dev, tag="prefill")
-    L.prefill_grouped(bank, x2d, pr, bl, out, sc, _status(dev), out_row=orow)
+    st = _status_word(dev, "prefill")
+    L.prefill_grouped(bank, x2d, pr, bl, out, sc, st, out_row=orow)
+    code = int(st.item())           # one sync per prefill call
+    if code == 0:
+        return out
+    st.zero_()
+    if code != L.SLX_ERR_RANGE:
+        raise L.SlxError("slx_prefill_grouped", code, "device-side error")
+    # an operand outside the tensor-core kernel's exact fp16 range: the
+    # call runs on the GEMV kernels instead (fp32 scale/bias arithmetic)
+    seg = np.repeat(np.asarray(slots, dtype=np.int32),
+                    np.asarray(counts, dtype=np.int64))
+    rows = torch.as_tensor(np.asarray(pair_row, dtype=np.int64), device=dev)
+    xs = x2d[rows].contiguous()
+    sid = torch.as_tensor(seg, device=dev).reshape(-1, 1)
+    y = switchglu(bank, xs, sid, 1, inter=bank.inter,
+                  status=st).reshape(-1, H)
+    code = int(st.item())
+    if code != 0:
+        st.zero_()
+        raise L.SlxError("prefill (GEMV path)", code,
+                         "an activation is outside the fp16 range (|x| >= "
+                         "65504) of the expert kernels")
+    dst = torch.as_tensor(np.asarray(out_row if out_row is not None
+                                     else np.arange(P), dtype=np.int64),
+                          device=dev)
+    out[dst] = y
     return out
+
+
+def _status_word(device, tag: str) -> torch.Tensor:
+    key = ("status", tag, device)
+    t = _scratch.get(key)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=device)
+        _scratch[key] = t
+    return t

@@ -61,6 +61,12 @@ class SynthConfig:
     zipf_s: float = 1.0              # router logit bias: popularity ~ 1/(rank+1)^s
     repeat_p: float = 0.0            # harness-side routing override (temporal reuse)
     weight_std: float = 0.02
+    # "normal": N(0, weight_std) weights quantized with the min/max affine
+    # scheme; "codes": the routed experts' codes, scales and biases drawn
+    # directly (numpy, identical on every machine, ~1 GB/s) with the
+    # statistics of quantized N(0, weight_std) groups -- for the large
+    # 2-bit models, whose expert bytes dominate the checkpoint
+    expert_init: str = "normal"
     extra: dict = field(default_factory=dict)
 
     @property
@@ -109,6 +115,14 @@ PRESETS: dict[str, SynthConfig] = {
                              expert_bits=2, trunk_bits=4, heads=24,
                              kv_heads=4, head_dim=128, vocab=151936,
                              zipf_s=1.1, repeat_p=0.6),
+    # the 117B-shaped decoder cut to 4 layers and a 4096-token vocabulary
+    # (expert shapes, top-k, routing statistics unchanged): trace tests
+    "laguna_c3_4l": SynthConfig(name="laguna_c3_4l", hidden=2560, layers=4,
+                                n_experts=256, top_k=10, inter=1024,
+                                expert_bits=2, trunk_bits=4, heads=24,
+                                kv_heads=4, head_dim=128, vocab=4096,
+                                zipf_s=1.1, repeat_p=0.6,
+                                expert_init="codes"),
     # small decoders for parity tests
     "tiny_dec": SynthConfig(name="tiny_dec", hidden=512, layers=3,
                             n_experts=16, top_k=4, inter=512, shared_inter=512,
@@ -120,6 +134,30 @@ PRESETS: dict[str, SynthConfig] = {
                              head_dim=128, vocab=1024, zipf_s=1.1,
                              repeat_p=0.6),
 }
+
+
+def random_codes(rng: np.random.Generator, lead: tuple, out: int, inp: int,
+                 bits: int, gs: int, std: float):
+    """Quantized weights drawn directly: uniform codes, and per group a
+    scale ~ (range of gs N(0, std) samples) / (2^bits - 1) and a bias near
+    -(2^bits - 1) / 2 * scale, so s*q + b is centred with the spread of the
+    quantized normal weights.  Returns (int32 words [..., out, inp*bits/32],
+    bf16 scales, bf16 biases) as numpy arrays (bf16 as uint16 bits)."""
+    import ml_dtypes
+    shape = (*lead, out, inp * bits // 32)
+    n = int(np.prod(shape))
+    words = rng.bit_generator.random_raw((n + 1) // 2).view(np.int32)[:n] \
+        .reshape(shape)
+    g = inp // gs
+    nb = (1 << bits) - 1
+    spread = 2.0 * std * np.sqrt(2.0 * np.log(gs))      # ~ max - min
+    scale = (spread / nb) * (0.85 + 0.3 * rng.random((*lead, out, g),
+                                                    dtype=np.float32))
+    bias = -0.5 * nb * scale * (0.9 + 0.2 * rng.random((*lead, out, g),
+                                                     dtype=np.float32))
+    s16 = scale.astype(ml_dtypes.bfloat16).view(np.uint16)
+    b16 = bias.astype(ml_dtypes.bfloat16).view(np.uint16)
+    return words, s16, b16
 
 
 def expert_bytes(hidden: int, inter: int, bits: int, gs: int) -> int:
@@ -208,10 +246,9 @@ class _ShardWriter:
             arr = t.cpu().numpy()
         else:
             arr = np.ascontiguousarray(t)
-        b = arr.tobytes()
-        if len(b) != n:
-            raise RuntimeError(f"{name}: {len(b)} bytes, header says {n}")
-        self.f.write(b)
+        if arr.nbytes != n:
+            raise RuntimeError(f"{name}: {arr.nbytes} bytes, header says {n}")
+        self.f.write(memoryview(arr.reshape(-1)).cast("B"))
         self.i += 1
 
     def close(self) -> None:
@@ -309,10 +346,18 @@ def write_model(out_dir: str, cfg: SynthConfig, seed: int = 0,
             w.put(f"{p}.mlp.gate.bias",
                   zipf_bias(cfg.n_experts, cfg.zipf_s, seed * 7919 + L))
             E, I = cfg.n_experts, cfg.inter
+            nrng = np.random.default_rng(seed * 1_000_003 + L * 7 + 1)
             for nm, o, i in (("gate_proj", I, H), ("up_proj", I, H),
                              ("down_proj", H, I)):
-                qput(w, f"{p}.mlp.switch_mlp.{nm}", randn(E, o, i, std=std),
-                     cfg.expert_bits)
+                pre = f"{p}.mlp.switch_mlp.{nm}"
+                if cfg.expert_init == "codes":
+                    for arr, part in zip(random_codes(nrng, (E,), o, i,
+                                                      cfg.expert_bits, gs,
+                                                      std),
+                                         ("weight", "scales", "biases")):
+                        w.put(f"{pre}.{part}", arr)
+                else:
+                    qput(w, pre, randn(E, o, i, std=std), cfg.expert_bits)
             if cfg.shared_inter:
                 Is = cfg.shared_inter
                 for nm, o, i in (("gate_proj", Is, H), ("up_proj", Is, H),

@@ -106,13 +106,15 @@ def predictions(ids, E, agree, seed):
 class GateStub:
     """Stands in for the next layer's router: returns (inds, scores)."""
 
-    def __init__(self, pi, ps, layer, clock):
+    def __init__(self, pi, ps, layer, clock, score_dtype=BF16):
         self.pi, self.ps, self.layer, self.clock = pi, ps, layer, clock
+        self.score_dtype = score_dtype
 
     def __call__(self, x):
         t = self.clock["t"]
         return (self.pi[t, self.layer][None, None, :].astype(np.uint32),
-                self.ps[t, self.layer][None, None, :].astype(BF16))
+                self.ps[t, self.layer][None, None, :].astype(
+                    self.score_dtype))
 
 
 # ------------------------------------------------------------ patching --
@@ -236,7 +238,7 @@ def norm_weights(L, H, seed):
 
 
 def run_decode(model_dir, n_slots, ids, pi, ps, policy, prefetch, topm, H,
-               x_seed=5):
+               x_seed=5, score_dtype=BF16):
     os.environ["STREAMLX_EVICT"] = policy
     os.environ["STREAMLX_PREFILL"] = "sweep"
     ref_pool.StreamingSwitchMLP._PF_TOPM = topm
@@ -250,7 +252,8 @@ def run_decode(model_dir, n_slots, ids, pi, ps, policy, prefetch, topm, H,
     nw = norm_weights(L, H, 11)
     if prefetch:
         for l in range(L - 1):
-            wr[l]._pf_next = (pools[l + 1], GateStub(pi, ps, l + 1, clock),
+            wr[l]._pf_next = (pools[l + 1],
+                              GateStub(pi, ps, l + 1, clock, score_dtype),
                               nw[l], nw[l + 1])
     rng = np.random.default_rng(x_seed)
     snaps = [[] for _ in range(L)]
@@ -300,15 +303,102 @@ def main():
         raise SystemExit("name the reference checkout with --reference or "
                          "STREAMLX_REFERENCE")
     load_reference(args.reference)
-    only = set(args.only.split(",")) if args.only else {"core", "residency"}
+    only = set(args.only.split(",")) if args.only else {"core", "residency",
+                                                        "c3trace"}
     tmp = tempfile.mkdtemp(prefix="slx_golden_")
     try:
         if "core" in only:
             _main(tmp)
         if "residency" in only:
             _residency(tmp)
+        if "c3trace" in only:
+            _c3trace(tmp)
     finally:
         shutil.rmtree(tmp, ignore_errors=True)
+
+
+C3_TRACE = dict(preset="laguna_c3_4l", seed=11, tokens=48, slots=64,
+                topm=7, token_seed=5, repeat_seed=12345)
+
+
+def _c3trace(tmp):
+    """Decode trace of the 117B-shaped decoder cut to 4 layers: the CPU
+    oracle decodes a fixed token sequence (routing, next-layer predictions,
+    the temporal-reuse coin drawn as the decoder draws it, logits), and the
+    reference's own pool code replays those ids and predictions with 64 LRU
+    slots per layer and prefetch top-m 7 (streamlx/integrate.py:234-298,
+    streamlx/pool.py:117-280)."""
+    from oracle.model import OracleDecoder
+    c = C3_TRACE
+    cfg = synth.PRESETS[c["preset"]]
+    d = synth.write_model(os.path.join(tmp, "c3"), cfg, seed=c["seed"])
+    T, L, k = c["tokens"], cfg.layers, cfg.top_k
+    toks = np.random.default_rng(c["token_seed"]).integers(0, cfg.vocab, T)
+    coin = np.random.default_rng(c["repeat_seed"])
+    o = OracleDecoder(d, max_len=T + 4)
+    ids = np.zeros((T, L, k), np.int32)
+    pi = np.full((T, L, k), -1, np.int32)
+    ps = np.zeros((T, L, k), np.float32)
+    logits = np.zeros((T, cfg.vocab), np.uint16)
+    rmargin = np.zeros((T, L), np.float64)
+    pmargin = np.full((T, L), np.inf)
+    prev = None
+    for t in range(T):
+        forced = {}
+        for i in range(L):
+            if cfg.repeat_p and t > 0 and coin.random() < cfg.repeat_p:
+                forced[i] = prev[i]
+        lg, routed, preds = o.step(int(toks[t]), forced=forced, predict=True)
+        logits[t] = BF16_BITS(lg)
+        rmargin[t] = o.route_margin
+        for i in range(L - 1):
+            pmargin[t, i + 1] = o.pred_margin[i]
+        for i in range(L):
+            ids[t, i] = routed[i]
+            if preds[i] is not None:
+                # prediction made at layer i is for layer i + 1
+                pi[t, i + 1], ps[t, i + 1] = preds[i]
+        prev = [r.copy() for r in routed]
+        print(f"[c3trace] token {t + 1}/{T}", flush=True)
+    # the trace needs the reference's bookkeeping, not its expert outputs:
+    # the stand-in's gather_qmm returns zeros of the right shape here
+    import mlx.core as mxc
+    full_qmm = mxc.gather_qmm
+
+    def shape_only_qmm(x, w, scales, biases, rhs_indices=None, **kw):
+        x = np.asarray(x)
+        idx = np.asarray(rhs_indices)
+        batch = np.broadcast_shapes(x.shape[:-2], idx.shape)
+        return np.zeros(batch + (x.shape[-2], w.shape[-2]), dtype=BF16)
+
+    mxc.gather_qmm = shape_only_qmm
+    try:
+        # the decoder orders a prediction by its fp32 scores
+        snaps, pools, err, pfr = run_decode(d, c["slots"], ids, pi, ps, "lru",
+                                            True, c["topm"], cfg.hidden,
+                                            score_dtype=np.float32)
+    finally:
+        mxc.gather_qmm = full_qmm
+    assert err is None, err
+    arrays = {"tokens": toks.astype(np.int32), "ids": ids, "pred_ids": pi,
+              "pred_scores": ps, "logits_bf16": logits,
+              "route_margin": rmargin, "pred_margin": pmargin}
+    p0 = pools[0]
+    for l, sn in enumerate(snaps):
+        for k2, v in pack_snaps(sn, p0.n_slots, p0.n_small,
+                                p0.n_main).items():
+            arrays[f"L{l}_{k2}"] = v
+    np.savez_compressed(os.path.join(HERE, "c3_trace.npz"), **arrays)
+    meta = dict(c, counters=list(COUNTERS), pf_rank=pfr,
+                final_stats=[{k3: v for k3, v in p.stats.items()
+                              if k3 not in ("fetch_s", "sweep_fetch_s")}
+                             for p in pools])
+    with open(os.path.join(HERE, "c3_trace.json"), "w") as f:
+        json.dump(meta, f, indent=1, sort_keys=True)
+
+
+def BF16_BITS(a):
+    return np.asarray(a, dtype=np.float32).astype(BF16).view(np.uint16)
 
 
 def _residency(tmp):

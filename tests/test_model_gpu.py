@@ -33,11 +33,17 @@ def tiny(tmp_path_factory):
             for name in ("tiny_dec", "tiny_dec2")}
 
 
-def _margin_ok(logits: np.ndarray, ids: np.ndarray, k: int) -> bool:
-    """Routing is well conditioned when the k-th and (k+1)-th logits differ
-    by more than the bf16 noise of the router input."""
-    s = np.sort(logits)[::-1]
-    return (s[k - 1] - s[k]) > 2e-3
+# Logit tolerances of the free-running decoder against the fp64 oracle.
+# Max-abs is the workload's 2e-2.  Rel-L2 stops at 5e-3, not the 1e-3 of a
+# single layer: the two pipelines round at the same points, but a SwiGLU
+# activation whose exact value sits within ~1e-6 of a bf16 rounding
+# boundary can round either way (the tensor cores' k16 sums are accurate to
+# ~1e-6 relative, not fp32's 1e-7), and one flipped activation moves the
+# down projection's bf16 outputs by an ulp in ~10% of their elements; over
+# three layers the logits settle at rel-L2 2.5-3.4e-3 (measured every step
+# on both decoders), max-abs one logit ulp (7.8e-3).
+LOGIT_MAX_ABS = 2e-2
+LOGIT_REL = 5e-3
 
 
 @pytest.mark.parametrize("path", ["graph", "eager"])
@@ -60,7 +66,7 @@ def test_decoder_matches_oracle(tiny, name, slots, path, monkeypatch):
     oracle = OracleDecoder(d)
     rng = np.random.default_rng(0)
     seq = rng.integers(0, cfg.vocab, 24)
-    worst_rel, agree, total = 0.0, 0, 0
+    worst_rel = 0.0
     prev = {}
     for t, tk in enumerate(seq):
         model.step(torch.tensor([int(tk)], dtype=torch.int32,
@@ -73,16 +79,14 @@ def test_decoder_matches_oracle(tiny, name, slots, path, monkeypatch):
                                                                 prev.get(i))}
         want_logits, ids_cpu = oracle.step(int(tk), forced=forced)
         for i in range(cfg.layers):
-            total += 1
-            agree += int(np.array_equal(np.sort(ids_gpu[i]),
-                                        np.sort(ids_cpu[i])))
+            # the same experts in the same order, every layer and step
+            assert np.array_equal(ids_gpu[i], ids_cpu[i]), (t, i, ids_gpu[i],
+                                                            ids_cpu[i])
         prev = {i: ids_gpu[i] for i in range(cfg.layers)}
         rel = A.rel_l2(got_logits, want_logits)
         worst_rel = max(worst_rel, rel)
-        assert np.max(np.abs(got_logits - want_logits)) <= 2e-2 * max(
-            1.0, float(np.max(np.abs(want_logits)))), t
-    assert worst_rel <= 1e-2, worst_rel
-    assert agree >= total - 2, (agree, total)
+        assert np.max(np.abs(got_logits - want_logits)) <= LOGIT_MAX_ABS, t
+    assert worst_rel <= LOGIT_REL, worst_rel
     st = aggregate_stats(pools)
     assert st["misses"] > 0 and st["evictions"] > 0      # the pool streamed
     assert st["hits"] + st["misses"] == 24 * cfg.layers * cfg.top_k
