@@ -65,6 +65,9 @@ class OracleDecoder:
         # logit to change the decision)
         self.route_margin = np.full(self.L, np.inf)
         self.pred_margin = np.full(self.L, np.inf)
+        self.route_own = [None] * self.L
+        self.own_margin = np.full(self.L, np.inf)
+        self.route_scores = [None] * self.L
 
     def deq(self, prefix: str, bits: int) -> np.ndarray:
         if prefix not in self._deq:
@@ -129,6 +132,11 @@ class OracleDecoder:
                                c["norm_topk_prob"], forced_ids=forced_ids)
         self.route_margin[layer] = (A.topk_margin(lg[0], c["top_k"])
                                     if forced_ids is None else np.inf)
+        # the router's own ordered pick and its margin even when the ids
+        # are forced, and the combine weights used
+        self.route_own[layer] = A.topk_ids(lg, c["top_k"])[0]
+        self.own_margin[layer] = A.topk_margin(lg[0], c["top_k"])
+        self.route_scores[layer] = sc[0]
         y = np.stack([self.expert_fwd(m, self.expert(layer, int(e)))[0]
                       for e in ids[0]])[None]
         sh = None

@@ -33,17 +33,19 @@ def tiny(tmp_path_factory):
             for name in ("tiny_dec", "tiny_dec2")}
 
 
-# Logit tolerances of the free-running decoder against the fp64 oracle.
-# Max-abs is the workload's 2e-2.  Rel-L2 stops at 5e-3, not the 1e-3 of a
-# single layer: the two pipelines round at the same points, but a SwiGLU
-# activation whose exact value sits within ~1e-6 of a bf16 rounding
-# boundary can round either way (the tensor cores' k16 sums are accurate to
-# ~1e-6 relative, not fp32's 1e-7), and one flipped activation moves the
-# down projection's bf16 outputs by an ulp in ~10% of their elements; over
-# three layers the logits settle at rel-L2 2.5-3.4e-3 (measured every step
-# on both decoders), max-abs one logit ulp (7.8e-3).
+# Logit tolerances of the free-running decoder against the fp64 oracle:
+# max-abs 2e-2, and rel-L2 1e-3 or, where the bf16 pipeline itself cannot
+# get that close, F32_FACTOR times the distance an fp32-accumulating
+# restatement of the same pipeline (oracle exact=False, forced onto the same
+# routing) has from the fp64 one.  Both round at the same points; a value
+# whose exact result sits near a bf16 rounding boundary rounds either way
+# under fp32 accumulation, one flipped SwiGLU activation moves ~10% of the
+# down projection's bf16 outputs by an ulp, and later roundings compound
+# it.  On these decoders the fp32 restatement reaches 2.8-2.9e-3 over 24
+# steps (max-abs one logit ulp, 7.8e-3), the GPU 2.5-3.4e-3.
 LOGIT_MAX_ABS = 2e-2
-LOGIT_REL = 5e-3
+LOGIT_REL = 1e-3
+F32_FACTOR = 1.5
 
 
 @pytest.mark.parametrize("path", ["graph", "eager"])
@@ -64,9 +66,10 @@ def test_decoder_matches_oracle(tiny, name, slots, path, monkeypatch):
         model.layers[i].mlp.switch_mlp.record_sink = s
         sinks.append(s)
     oracle = OracleDecoder(d)
+    fp32 = OracleDecoder(d, exact=False)
     rng = np.random.default_rng(0)
     seq = rng.integers(0, cfg.vocab, 24)
-    worst_rel = 0.0
+    worst_rel = worst_rel32 = 0.0
     prev = {}
     for t, tk in enumerate(seq):
         model.step(torch.tensor([int(tk)], dtype=torch.int32,
@@ -83,10 +86,13 @@ def test_decoder_matches_oracle(tiny, name, slots, path, monkeypatch):
             assert np.array_equal(ids_gpu[i], ids_cpu[i]), (t, i, ids_gpu[i],
                                                             ids_cpu[i])
         prev = {i: ids_gpu[i] for i in range(cfg.layers)}
-        rel = A.rel_l2(got_logits, want_logits)
-        worst_rel = max(worst_rel, rel)
-        assert np.max(np.abs(got_logits - want_logits)) <= LOGIT_MAX_ABS, t
-    assert worst_rel <= LOGIT_REL, worst_rel
+        lf, _ = fp32.step(int(tk), forced=dict(enumerate(ids_cpu)))
+        want = A.bf16_round(want_logits)
+        worst_rel = max(worst_rel, A.rel_l2(got_logits, want))
+        worst_rel32 = max(worst_rel32, A.rel_l2(A.bf16_round(lf), want))
+        assert np.max(np.abs(got_logits - want)) <= LOGIT_MAX_ABS, t
+    assert worst_rel <= max(LOGIT_REL, F32_FACTOR * worst_rel32), \
+        (worst_rel, worst_rel32)
     st = aggregate_stats(pools)
     assert st["misses"] > 0 and st["evictions"] > 0      # the pool streamed
     assert st["hits"] + st["misses"] == 24 * cfg.layers * cfg.top_k
