@@ -77,8 +77,11 @@ size_t slx_switchglu_scratch_bytes(int T, int k, int inter, int shared_inter) {
   const size_t u = (size_t)T * k, ng = inter / 64, ngs = shared_inter / 64;
   // the first 256 bytes: grid-barrier words of the fused decode kernel (at
   // a fixed place, so calls of any shape sharing one scratch agree on them)
+  // then the split area of the one-launch decode path (T == 1): per CTA
+  // boundary, the rows of a down item that straddles it (slx_qgemv.cu)
   return 256 + align256(u * ng * 128) + align256(u * ng * 16) +
-         align256((size_t)T * ngs * 128) + align256((size_t)T * ngs * 16);
+         align256((size_t)T * ngs * 128) + align256((size_t)T * ngs * 16) +
+         align256(slx::split_area_bytes(k + (shared_inter > 0 ? 1 : 0)));
 }
 
 size_t slx_expert_tiled_bytes(int hidden, int inter, int bits) {
@@ -350,6 +353,8 @@ static int switchglu_impl(const slx_expert_bank* bank,
   uint32_t* hfrag_sh = reinterpret_cast<uint32_t*>(sp);
   sp += align256((size_t)T * ngs * 128);
   float* hpart_sh = reinterpret_cast<float*>(sp);
+  sp += align256((size_t)T * ngs * 16);
+  void* split = sp;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
 
   slx::GemvArgs a = {};
@@ -412,7 +417,7 @@ static int switchglu_impl(const slx_expert_bank* bank,
     d.tile_bytes_sh = Is ? (int)slx::single_tile_bytes(Is, bits) : 0;
     d.a_bytes = (long long)slx::expert_a_bytes(H, I, bits);
     d.a_bytes_sh = Is ? (long long)slx::expert_a_bytes(H, Is, bits) : 0;
-    rc = slx::launch_switchglu_fused(a, d, gbar, bits, s, svc, ep);
+    rc = slx::launch_switchglu_fused(a, d, gbar, split, bits, s, svc, ep);
     if (rc != SLX_ERR_UNSUPPORTED) {
       g_glu_kernels = rc ? 0 : 1;
       return rc ? cuda_check(rc, "slx_switchglu fused") : SLX_OK;
@@ -548,9 +553,16 @@ int slx_dequant_rows(const slx_qmat* w, int in_features, int bits,
   return rc ? cuda_check(rc, "slx_dequant_rows") : SLX_OK;
 }
 
+// Router scratch: [T, E] logits, then (one token) the E logit bounds of
+// the many-SM form, then the T tickets.
+static size_t router_bound_bytes(int T, int n_experts) {
+  return T == 1 ? align256((size_t)n_experts * 4) : 0;
+}
+
 size_t slx_router_scratch_bytes(int T, int n_experts) {
   if (T < 0 || n_experts < 0) return 0;
-  return align256((size_t)T * n_experts * 4) + align256((size_t)T * 4);
+  return align256((size_t)T * n_experts * 4) + router_bound_bytes(T, n_experts) +
+         align256((size_t)T * 4);
 }
 
 int slx_router_topk(const void* x, const void* ratio, const void* w_gate,
@@ -586,8 +598,12 @@ int slx_router_topk(const void* x, const void* ratio, const void* w_gate,
   a.out_ids = out_ids;
   a.out_scores = out_scores;
   a.logits = reinterpret_cast<float*>(scratch);
+  a.bound = T == 1 ? reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(scratch) +
+                                               align256((size_t)T * E * 4))
+                   : nullptr;
   a.tickets = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(scratch) +
-                                         align256((size_t)T * E * 4));
+                                         align256((size_t)T * E * 4) +
+                                         router_bound_bytes(T, E));
   a.status = status;
   const int rc = slx::launch_router(a, reinterpret_cast<cudaStream_t>(stream));
   return rc ? cuda_check(rc, "slx_router_topk") : SLX_OK;
@@ -634,8 +650,13 @@ int slx_router_topk_multi(const slx_router_head* heads, int n_heads,
     a[i].out_ids = h.out_ids;
     a[i].out_scores = h.out_scores;
     a[i].logits = reinterpret_cast<float*>(h.scratch);
+    a[i].bound = T == 1 ? reinterpret_cast<float*>(
+                              reinterpret_cast<uint8_t*>(h.scratch) +
+                              align256((size_t)T * E * 4))
+                        : nullptr;
     a[i].tickets = reinterpret_cast<int32_t*>(
-        reinterpret_cast<uint8_t*>(h.scratch) + align256((size_t)T * E * 4));
+        reinterpret_cast<uint8_t*>(h.scratch) + align256((size_t)T * E * 4) +
+        router_bound_bytes(T, E));
     a[i].status = status;
   }
   const int rc = slx::launch_router_heads(a, n_heads,
@@ -802,9 +823,13 @@ extern "C" int slx_router_topk_noalloc(
     }
     base = g_noalloc_addr[dev];
   }
-  // slx_router_topk puts the tickets right after the 256-aligned logits;
-  // start the logits so that the tickets land on the fixed ticket words.
-  const size_t logit_bytes = align256((size_t)T * E * 4);
+  // slx_router_topk puts the tickets right after the 256-aligned logits
+  // (and, for one token, the logit bounds); start the logits so that the
+  // tickets land on the fixed ticket words.
+  const size_t logit_bytes =
+      align256((size_t)T * E * 4) + router_bound_bytes(T, E);
+  if (logit_bytes > kNoAllocTicketOff)
+    return fail(SLX_ERR_SCRATCH, "router_noalloc: E %d too large", E);
   unsigned char* scr = (unsigned char*)base + kNoAllocTicketOff - logit_bytes;
   return slx_router_topk(x, ratio, w_gate, bias, T, H, E, k, norm_topk, force,
                          forced_ids, out_ids, out_scores, scr,

@@ -120,6 +120,28 @@ SLX_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes,
       : "memory");
 }
 
+// Same without an L2 policy (data that other CTAs read too).
+SLX_DEV void bulk_g2s_plain(void* dst, const void* src, uint32_t bytes,
+                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Generic-proxy global writes before async-proxy (bulk copy) accesses.
+SLX_DEV void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Start reading [src, src + bytes) from DRAM into L2 (no completion to
+// wait for).  src and bytes: 16-byte aligned / multiple of 16.
+SLX_DEV void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes)
+               : "memory");
+}
+
 // ------------------------------------------------------------------ PDL ---
 //
 // Every kernel of the library lets its dependent grid launch at once

@@ -212,14 +212,6 @@ SLX_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memo
 template <int N>
 SLX_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 SLX_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-SLX_DEV void bulk_g2s_plain(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-      ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
-}
-SLX_DEV void bulk_prefetch_l2(const void* src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
 // Byte offset of fp16 position pos of row n inside a 128-byte-swizzled chunk.
 SLX_DEV int sw_off(int n, int pos) {
   return n * kRowB + ((((pos >> 3) ^ (n & 7))) << 4) + ((pos & 7) << 1);

@@ -754,9 +754,10 @@ struct FusedArgs {
   GemvArgs a;
   DownArgs d;
   unsigned long long* bar;  // arrival counter (only grows)
-  int off_frag, off_part, off_xsum, off_reda, off_stage_a;
+  int off_frag, off_part, off_xsum, off_reda, off_stage_a, off_x;
   int off_bfrag, off_bpart, off_bxsum, off_redb, off_stage_b, off_meta;
   int stage_a, stage_b;  // bytes per A / B tile slot
+  int bfrag_bulk;        // phase-B fragments by bulk copy
   int b_late;            // down tiles share the gate/up slots: request them
                          // once phase A is done (they load during the barrier)
   // in-kernel slot fill of graph-launched decode (slx_fill_service); off
@@ -780,6 +781,10 @@ struct FusedArgs {
   const int32_t* ep_stamp;
   uint16_t* ep_recv[SLX_EP_MAX_RANKS];
   unsigned int* ep_count[SLX_EP_MAX_RANKS];
+  // split area of the scratch: per CTA boundary, the bf16 rows of the units
+  // of an item that straddles it, and one epoch flag per unit
+  float* split_y;          // [kSplitMaxGrid][n_units][16]
+  unsigned* split_flag;    // [kSplitMaxGrid][n_units]
 };
 
 SLX_DEV unsigned long long ld_acquire_u64(const unsigned long long* p) {
@@ -796,12 +801,16 @@ SLX_DEV void red_release_add_u64(unsigned long long* p, unsigned long long v) {
 // [n * nblocks, (n + 1) * nblocks) on entry (the earlier launches are
 // complete), add one each with a release reduction (no reply to wait for,
 // unlike a returning atomic), and wait until it reaches (n + 1) * nblocks.
+// `epoch` (optional) receives target / nblocks: a number no earlier barrier
+// on this counter produced.
 SLX_DEV bool grid_barrier(unsigned long long* cnt, int nblocks,
                           int32_t* status,
-                          unsigned long long limit_ns = kWaitLimitNs) {
+                          unsigned long long limit_ns = kWaitLimitNs,
+                          unsigned long long* epoch = nullptr) {
   const unsigned long long nb = (unsigned long long)nblocks;
   const unsigned long long v = ld_acquire_u64(cnt);
   const unsigned long long target = v - v % nb + nb;
+  if (epoch) *epoch = target / nb;
   red_release_add_u64(cnt, 1ull);
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 0; ld_acquire_u64(cnt) < target; ++i) {
@@ -829,7 +838,11 @@ SLX_DEV int ld_volatile_s32(const int32_t* p) {
   return v;
 }
 
-SLX_DEV void svc_write_log(const FusedArgs& f, const GemvArgs& a, int need) {
+// Off the hot path (out of line keeps the decode kernel's code compact: a
+// one-CTA-per-SM kernel runs each code line once, so every instruction-cache
+// line it touches costs a miss).
+__device__ __noinline__ void svc_write_log(const FusedArgs& f, const GemvArgs& a,
+                                           int need) {
   volatile int32_t* L = f.svc_log;
   if (!L) return;
   const int stamp = ld_volatile_s32(f.svc_stamp);
@@ -848,7 +861,7 @@ SLX_DEV void svc_write_log(const FusedArgs& f, const GemvArgs& a, int need) {
 // Every thread of every CTA calls this after the CTA agreed that some routed
 // id of this launch has no slot.
 template <int BITS>
-SLX_DEV void svc_fill(const FusedArgs& f, const GemvArgs& a) {
+__device__ __noinline__ void svc_fill(const FusedArgs& f, const GemvArgs& a) {
   __shared__ int s_ok;
   __shared__ __align__(16) slx_fill_item s_item;
   __shared__ int s_nitems;
@@ -952,28 +965,75 @@ SLX_DEV void svc_fill(const FusedArgs& f, const GemvArgs& a) {
   asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
-// One 64-column group of a 16-row down tile: per-row partial (lanes with
-// tig < 2 hold rows g and g + 8).
+// Up to four 64-column groups G0..G0+n-1 of a 16-row down tile, folded in
+// group order: per-row partial (lanes with tig < 2 hold rows g and g + 8).
+// The groups' fragment loads and MMAs are independent, so they overlap.
 template <int BITS>
-SLX_DEV float down_group(const uint8_t* S, int in, int G, int g, int tig,
-                         int rrow, const uint32_t* fr, const float* xs) {
+SLX_DEV float down_quad(const uint8_t* S, int in, int G0, int n, int g,
+                        int tig, int rrow, const uint32_t* fr, const float* xs) {
   const int RB = tile_rb(in, BITS);
   const bool swz = tile_swizzled(in, BITS);
-  const int nG = tile_ng(in);
   const uint32_t* SB = reinterpret_cast<const uint32_t*>(S + 16 * RB);
-  uint32_t b[8];
-  load_frag(fr, G, tig, b);
-  float dd[4];
-  group_mma<BITS>(S, RB, swz, G, g, tig, b, dd);
-  (void)nG;
-  return fold(0.f, (tig & 1) ? dd[2] : dd[0], SB[G * 16 + rrow], xs[G],
-              kHUnit);
+  // groups past the unit's last one (n < 4) repeat its last group, weight 0
+  int G[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) G[q] = G0 + (q < n ? q : n - 1);
+  uint32_t b[4][8];
+  float dd[4][4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) load_frag(fr, G[q], tig, b[q]);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) group_mma<BITS>(S, RB, swz, G[q], g, tig, b[q], dd[q]);
+  float acc = 0.f;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float a = fold(acc, (tig & 1) ? dd[q][2] : dd[q][0], SB[G[q] * 16 + rrow],
+                         xs[G[q]], kHUnit);
+    acc = q < n ? a : acc;
+  }
+  return acc;
+}
+
+// gemv_issue in pieces of about kBulkPiece bytes: the copy engine keeps
+// several bulk copies in flight per SM, so a few medium copies stream from
+// DRAM faster than one large one (measured: 24 MB over 148 SMs in 25.6 KB
+// copies ~3.6 TB/s, in 12.8 KB copies ~4.7 TB/s).
+constexpr int kBulkPiece = 12800;
+SLX_DEV void issue_pieces(const uint8_t* src, uint8_t* dst, int bytes,
+                          uint64_t* bar, uint64_t pol) {
+  mbar_arrive_expect_tx(bar, bytes);
+  const int n = (bytes + kBulkPiece - 1) / kBulkPiece;
+  const int piece = ((bytes + n - 1) / n + 15) & ~15;
+  for (int o = 0; o < bytes; o += piece)
+    bulk_g2s(dst + o, src + o, bytes - o < piece ? bytes - o : piece, bar, pol);
+}
+
+// Tile q of a one-token launch, with the routed units' slots already looked
+// up (slot[u] < 0: no slot).
+SLX_DEV TileInfo fused_tile(const GemvArgs& a, int q, const int* slot) {
+  TileInfo t{};
+  const int tpu = a.I / kRows;
+  const int routed = a.k * tpu;
+  if (q < routed) {
+    const int u = q / tpu, s = slot[u];
+    t.valid = t.valid1 = s >= 0;
+    t.unit = u;
+    t.ti = q % tpu;
+    t.src = a.bank + (size_t)(s < 0 ? 0 : s) * a.slot_stride +
+            (size_t)t.ti * a.tile_bytes;
+    return t;
+  }
+  t.valid = t.valid1 = 1;
+  t.unit = -1;  // the token's shared expert
+  t.ti = q - routed;
+  t.src = a.shared + (size_t)t.ti * a.tile_bytes;
+  return t;
 }
 
 // Rows row0..row0+15 of unit j (lanes 0..15 hold them) into the receive
 // block of this step and layer: a routed unit to every rank, the shared
 // expert (unit k, computed by every rank) to this rank only.
-SLX_DEV void ep_write_rows(const FusedArgs& f, const DownArgs& d, int j,
+__device__ __noinline__ void ep_write_rows(const FusedArgs& f, const DownArgs& d, int j,
                            int row0, float y, int lane) {
   const uint32_t b = lane < kRows ? (uint32_t)f32_to_bf16(y) : 0u;
   uint32_t w[4];
@@ -1011,6 +1071,59 @@ SLX_DEV void ep_signal(const FusedArgs& f) {
                  : "memory");
 }
 
+// Phase-B fragments of the units a CTA touches, by plain loads (when the
+// units' rows do not line up for one bulk copy).  Every thread calls this.
+__device__ __noinline__ void load_bfrag_lsu(const DownArgs& d, uint32_t* bfrag,
+                                            float* bpart, int U, int nGmax,
+                                            int nGr, int nGs, int qb0, int nbt) {
+  const int w0 = qb0 % U;
+  auto touched = [&](int j) { return nbt >= U || (j - w0 + U) % U < nbt; };
+  const int pu = nGmax * 8;  // uint4 per unit
+  const int total = U * pu;
+  uint4* bf4 = reinterpret_cast<uint4*>(bfrag);
+  for (int base = threadIdx.x; base < total; base += 4 * kFThreads) {
+    uint4 v[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int p = base + r * kFThreads;
+      v[r] = make_uint4(0u, 0u, 0u, 0u);
+      if (p < total) {
+        const int j = p / pu, o = p % pu;
+        const bool sh = j >= d.k;
+        if (touched(j) && o < (sh ? nGs : nGr) * 8)
+          v[r] = __ldcg(reinterpret_cast<const uint4*>(
+                            sh ? d.hfrag_sh : d.hfrag + (size_t)j * d.unit_frag_words) +
+                        o);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int p = base + r * kFThreads;
+      if (p < total) bf4[p] = v[r];
+    }
+  }
+  for (int p = threadIdx.x; p < U * nGmax; p += kFThreads) {
+    const int j = p / nGmax, G = p % nGmax;
+    const bool sh = j >= d.k;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (touched(j) && G < (sh ? nGs : nGr))
+      v = __ldcg(reinterpret_cast<const float4*>(
+                     sh ? d.hpart_sh : d.hpart + (size_t)j * d.unit_part_floats) +
+                 G);
+    reinterpret_cast<float4*>(bpart)[p] = v;
+  }
+}
+
+// Phase B splits the token's (16-row item, unit) down tiles evenly over the
+// CTAs, item-major: CTA b owns tiles [NB b / G, NB (b + 1) / G).  An item
+// whose tiles straddle CTAs is combined by the CTA that owns its last unit:
+// the other parts leave their units' bf16 rows in the scratch's split area
+// (slot = the first CTA boundary inside the item) and a flag per unit that
+// holds the launch's barrier epoch, so no word ever needs resetting.
+SLX_DEV int split_slot(int item, int U, int NB, int G) {
+  return (int)((((long long)item * U + 1) * G + NB - 1) / NB);
+}
+
 template <int BITS>
 __global__ void __launch_bounds__(kFThreads, 1)
     k_switchglu_fused(const __grid_constant__ FusedArgs f) {
@@ -1019,19 +1132,26 @@ __global__ void __launch_bounds__(kFThreads, 1)
   const DownArgs& d = f.d;
   uint64_t* fullA = reinterpret_cast<uint64_t*>(smem);
   uint64_t* fullB = fullA + kFMaxA;
+  uint64_t* fullX = fullB + kFMaxB;  // the token's activations
+  uint64_t* fullF = fullX + 1;       // phase-B fragments
   uint32_t* frag = reinterpret_cast<uint32_t*>(smem + f.off_frag);
   float* part = reinterpret_cast<float*>(smem + f.off_part);
   float* xsum = reinterpret_cast<float*>(smem + f.off_xsum);
-  float* redA = reinterpret_cast<float*>(smem + f.off_reda);  // [kFMaxA][kFW][32]
+  uint16_t* xs = reinterpret_cast<uint16_t*>(smem + f.off_x);
+  float* redA = reinterpret_cast<float*>(smem + f.off_reda);  // [na][kFW][32]
   uint8_t* stA = smem + f.off_stage_a;
   uint32_t* bfrag = reinterpret_cast<uint32_t*>(smem + f.off_bfrag);
   float* bpart = reinterpret_cast<float*>(smem + f.off_bpart);
   float* bxsum = reinterpret_cast<float*>(smem + f.off_bxsum);
-  float* redB = reinterpret_cast<float*>(smem + f.off_redb);  // [tiles][nGmax][16]
+  float* redB = reinterpret_cast<float*>(smem + f.off_redb);  // [tiles][nq][16]
   uint8_t* stB = smem + f.off_stage_b;
-  int* meta = reinterpret_cast<int*>(smem + f.off_meta);      // A tile valid + B unit valid
+  int* meta = reinterpret_cast<int*>(smem + f.off_meta);      // A tile valid + unit valid
   __shared__ float s_vmax[kFW];
   __shared__ float s_vunit;
+  __shared__ int s_slot[kFMaxUnits];
+  __shared__ float s_score[kFMaxUnits];  // combine weight per unit (shared: 1)
+  __shared__ int s_need;
+  __shared__ unsigned s_epoch;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G_ = gridDim.x, bid = blockIdx.x;
   const int nG = tile_ng(a.in);
@@ -1040,65 +1160,74 @@ __global__ void __launch_bounds__(kFThreads, 1)
   const int qa0 = (int)((long long)a.n_tiles * bid / G_);
   const int na = (int)((long long)a.n_tiles * (bid + 1) / G_) - qa0;
   const int U = d.n_units;
-  const int qb0 = (int)((long long)d.n_items * bid / G_);
-  const int nb = (int)((long long)d.n_items * (bid + 1) / G_) - qb0;
-  const int nbt = nb * U;  // down tiles of this CTA
+  const int NB = d.n_items * U;
+  const int qb0 = (int)((long long)NB * bid / G_);
+  const int nbt = (int)((long long)NB * (bid + 1) / G_) - qb0;  // down tiles here
   const int nGr = tile_ng(d.I), nGs = d.Is ? tile_ng(d.Is) : 0;
   const int nGmax = nGr > nGs ? nGr : nGs;
+  const int nq = (nGmax + 3) >> 2;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kFMaxA; ++i) mbar_init(&fullA[i], 1);
     for (int i = 0; i < kFMaxB; ++i) mbar_init(&fullB[i], 1);
+    mbar_init(fullX, 1);
+    mbar_init(fullF, 1);
     fence_mbar_init();
   }
   __syncthreads();
   pdl_wait_primary();
   SLX_TRACE_POINT(0, 0);
+  SLX_TRACE_SMID(0);
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(fullX, a.in * 2);
+    bulk_g2s_plain(xs, a.x, a.in * 2, fullX);
+  }
 
-  if (f.svc_on) {
-    __shared__ int s_need;
-    if (threadIdx.x == 0) {
-      int need = 0;
-      for (int j = 0; j < a.k; ++j)
-        need |= lookup_slot(a.ids, j, a.slot_table, a.n_table, a.n_slots) < 0;
-      s_need = need;
-      if (bid == 0) svc_write_log(f, a, need);
+  // slots of the routed experts, one lane each; s_need: one has none
+  auto lookup_slots = [&]() {
+    if (warp == 0) {
+      unsigned miss = 0u;
+      for (int j0 = 0; j0 < a.k; j0 += 32) {
+        const int j = j0 + lane;
+        int sl = -1;
+        if (j < a.k) {
+          sl = lookup_slot(a.ids, j, a.slot_table, a.n_table, a.n_slots);
+          s_slot[j] = sl;
+        }
+        miss |= __ballot_sync(0xffffffffu, j < a.k && sl < 0);
+      }
+      if (lane == 0) s_need = miss != 0u;
     }
     __syncthreads();
-    if (s_need) svc_fill<BITS>(f, a);
-  }
-
-  if (warp == 0) {
-    // ---- every weight request of this CTA, up front ----
-    const uint64_t pol = l2_evict_first_policy();
-    if (lane < na) {
-      SlotCache c;
-      const TileInfo t = gemv_tile(a, qa0 + lane, c);
-      meta[lane] = t.valid;
-      if (!t.valid && !f.ep_on) set_status(a.status, SLX_ERR_UNMAPPED_EXPERT);
-      gemv_issue<BITS>(a, t, stA + (size_t)lane * f.stage_a, &fullA[lane], pol);
+  };
+  lookup_slots();
+  if (f.svc_on) {
+    if (bid == 0 && threadIdx.x == 0) svc_write_log(f, a, s_need);
+    if (s_need) {  // the same verdict in every CTA (same ids, same table)
+      svc_fill<BITS>(f, a);
+      lookup_slots();
     }
   }
+
+  // source of this CTA's down tile s (null: the unit has no slot)
+  auto b_src = [&](int s, int& bytes) -> const uint8_t* {
+    const int sg = qb0 + s, item = sg / U, j = sg % U;
+    if (j >= d.k) {
+      bytes = d.tile_bytes_sh;
+      return d.shared + d.a_bytes_sh + (size_t)item * d.tile_bytes_sh;
+    }
+    bytes = d.tile_bytes;
+    const int slot = s_slot[j];
+    if (slot < 0) return nullptr;
+    return d.bank + (size_t)slot * d.slot_stride + d.a_bytes +
+           (size_t)item * d.tile_bytes;
+  };
   auto issue_b = [&]() {
     const uint64_t pol = l2_evict_first_policy();
     for (int s = lane; s < nbt; s += 32) {
-      const int q = qb0 + s / U, j = s % U;
-      const int rb = q;  // one token: item = 16-row block of H
-      const bool shared = j >= d.k;
-      const int bytes = shared ? d.tile_bytes_sh : d.tile_bytes;
-      const uint8_t* src;
-      bool valid = true;
-      if (!shared) {
-        const int slot = lookup_slot(d.ids, j, d.slot_table, d.n_table, d.n_slots);
-        valid = slot >= 0;
-        src = d.bank + (size_t)(valid ? slot : 0) * d.slot_stride + d.a_bytes +
-              (size_t)rb * d.tile_bytes;
-      } else {
-        src = d.shared + d.a_bytes_sh + (size_t)rb * d.tile_bytes_sh;
-      }
-      if (s < U) meta[kFMaxA + j] = valid;
-      if (!valid && !f.ep_on) set_status(d.status, SLX_ERR_UNMAPPED_EXPERT);
-      if (valid) {
+      int bytes = 0;
+      const uint8_t* src = b_src(s, bytes);
+      if (src) {
         mbar_arrive_expect_tx(&fullB[s], bytes);
         bulk_g2s(stB + (size_t)s * f.stage_b, src, bytes, &fullB[s], pol);
       } else {
@@ -1107,11 +1236,37 @@ __global__ void __launch_bounds__(kFThreads, 1)
     }
   };
   if (warp == 0) {
-    if (!f.b_late) issue_b();
+    // ---- every weight request of this CTA, up front ----
+    const uint64_t pol = l2_evict_first_policy();
+    if (lane < na) {
+      const TileInfo t = fused_tile(a, qa0 + lane, s_slot);
+      meta[lane] = t.valid;
+      if (!t.valid && !f.ep_on) set_status(a.status, SLX_ERR_UNMAPPED_EXPERT);
+      if (t.valid)
+        issue_pieces(t.src, stA + (size_t)lane * f.stage_a, a.tile_bytes, &fullA[lane], pol);
+      else
+        mbar_arrive(&fullA[lane]);
+    }
+    for (int j = lane; j < U; j += 32) {
+      meta[kFMaxA + j] = j >= d.k || s_slot[j] >= 0;
+      s_score[j] = (d.scores && j < d.k) ? d.scores[j] : 1.f;
+    }
+    if (!f.b_late) {
+      issue_b();
+    } else {
+      // the down tiles share the gate/up stages: start their DRAM reads now
+      // into L2, the copies into shared memory follow once phase A is done
+      for (int s = lane; s < nbt; s += 32) {
+        int bytes = 0;
+        const uint8_t* src = b_src(s, bytes);
+        if (src) bulk_prefetch_l2(src, bytes);
+      }
+    }
   } else {
     // ---- activation fragments of the token (per-token scale first) ----
     const int ct = threadIdx.x - 32;
-    const float m = absmax_part(a.x, a.in, ct, kFW * 32);
+    mbar_wait(fullX, 0, a.status);
+    const float m = absmax_part(xs, a.in, ct, kFW * 32);
     if (lane == 0) s_vmax[warp - 1] = m;
     named_bar_fused();
     float mm = 0.f;
@@ -1119,7 +1274,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
     const int ve = vec_exp(mm);
     if (ct == 0) s_vunit = pow2f(24 - ve);
     for (int p = ct; p < 4 * nG; p += kFW * 32)
-      frag_task<BITS>(a.x, p >> 2, p & 3, frag, part, a.status, pow2f(ve));
+      frag_task<BITS>(xs, p >> 2, p & 3, frag, part, a.status, pow2f(ve));
   }
   __syncthreads();
   const float vunit = s_vunit;
@@ -1133,9 +1288,18 @@ __global__ void __launch_bounds__(kFThreads, 1)
     const int g = lane >> 2, tig = lane & 3;
     const int mat = tig >> 1;
     const int sbl = mat * 16 + g + 8 * (tig & 1);
+#ifdef SLX_TRACE
+    int tr_seen = 0;
+#endif
     for (int i = 0; i < na; ++i) {
       const bool ok = mbar_wait(&fullA[i], 0, a.status);
       if (i < 3) SLX_TRACE_POINT(0, 2 + i);
+#ifdef SLX_TRACE
+      if (threadIdx.x == 32 && nbt > 0 && !f.b_late) {
+        if (!(tr_seen & 1) && mbar_try_wait(&fullB[0], 0)) { SLX_TRACE_POINT(1, 8); tr_seen |= 1; }
+        if (!(tr_seen & 2) && mbar_try_wait(&fullB[nbt - 1], 0)) { SLX_TRACE_POINT(1, 9); tr_seen |= 2; }
+      }
+#endif
       const uint8_t* S = stA + (size_t)i * f.stage_a;
       float acc = 0.f;
       if (ok && meta[i]) {
@@ -1174,102 +1338,173 @@ __global__ void __launch_bounds__(kFThreads, 1)
   // one warp per tile: reduce the 16 partials, SwiGLU, write fragments
   if (warp > 0 && warp - 1 < na) {
     const int i = warp - 1;
-    SlotCache c;
-    TileInfo t = gemv_tile(a, qa0 + i, c);
+    TileInfo t = fused_tile(a, qa0 + i, s_slot);
     t.valid = t.valid1 = meta[i];
     gemv_epilogue<BITS, kFW>(a, t, redA + (size_t)i * kFW * 32, lane);
   }
-  if (warp == 0 && f.b_late) issue_b();  // the A slots are free now
+  if (warp == 0 && f.b_late) issue_b();  // the A stages are free now
+  // the SwiGLU fragments are read by other CTAs' bulk copies
+  fence_proxy_async_global();
   __syncthreads();
   SLX_TRACE_POINT(0, 6);
-  if (threadIdx.x == 0) grid_barrier(f.bar, G_, a.status);
+#ifdef SLX_TRACE
+  if (threadIdx.x == 32 && nbt > 0 && !f.b_late) {
+    if (mbar_try_wait(&fullB[nbt - 1], 0)) SLX_TRACE_POINT(1, 10);
+    else SLX_TRACE_POINT(1, 11);
+  }
+#endif
+  if (threadIdx.x == 0) {
+    unsigned long long ep = 0;
+    grid_barrier(f.bar, G_, a.status, kWaitLimitNs, &ep);
+    s_epoch = (unsigned)ep;
+  }
   __syncthreads();
   SLX_TRACE_POINT(0, 7);
   pdl_launch_dependents();
-  if (nb == 0) {
+  if (nbt == 0) {
     if (f.ep_on) ep_signal(f);
     return;
   }
+  const unsigned epoch = s_epoch;
 
-  // ---- phase B: fragments of every unit, then (unit, group) tasks ----
-  {
-    const int ct = threadIdx.x;
-    const int pu = nGmax * 8;  // uint4 per unit
-    for (int p = ct; p < U * pu; p += kFThreads) {
-      const int j = p / pu, o = p % pu;
-      const bool shared = j >= d.k;
-      if (o < (shared ? nGs : nGr) * 8) {
-        const uint32_t* src = shared ? d.hfrag_sh
-                                     : d.hfrag + (size_t)j * d.unit_frag_words;
-        reinterpret_cast<uint4*>(bfrag)[p] =
-            __ldcg(reinterpret_cast<const uint4*>(src) + o);
+  // ---- phase B: fragments of the units (bulk copies from L2) ----
+  if (f.bfrag_bulk) {
+    if (threadIdx.x == 0) {
+      fence_proxy_async_global();
+      const uint32_t fr = (uint32_t)d.k * nGr * 128, pr = (uint32_t)d.k * nGr * 16;
+      const uint32_t fs = (uint32_t)nGs * 128, ps = (uint32_t)nGs * 16;
+      mbar_arrive_expect_tx(fullF, fr + pr + fs + ps);
+      bulk_g2s_plain(bfrag, d.hfrag, fr, fullF);
+      bulk_g2s_plain(bpart, d.hpart, pr, fullF);
+      if (fs) {
+        bulk_g2s_plain(bfrag + (size_t)d.k * nGmax * 32, d.hfrag_sh, fs, fullF);
+        bulk_g2s_plain(bpart + (size_t)d.k * nGmax * 4, d.hpart_sh, ps, fullF);
       }
     }
-    for (int p = ct; p < U * nGmax; p += kFThreads) {
-      const int j = p / nGmax, G = p % nGmax;
-      const bool shared = j >= d.k;
-      if (G < (shared ? nGs : nGr)) {
-        const float* src = shared ? d.hpart_sh
-                                  : d.hpart + (size_t)j * d.unit_part_floats;
-        reinterpret_cast<float4*>(bpart)[p] =
-            __ldcg(reinterpret_cast<const float4*>(src) + G);
-      }
-    }
+    mbar_wait(fullF, 0, d.status);
+    SLX_TRACE_POINT(1, 0);
+  } else {
+    load_bfrag_lsu(d, bfrag, bpart, U, nGmax, nGr, nGs, qb0, nbt);
+    SLX_TRACE_POINT(1, 1);
   }
   __syncthreads();
+  SLX_TRACE_POINT(1, 2);
   frag_sums(bpart, bxsum, U * nGmax, threadIdx.x, kFThreads);
   __syncthreads();
   SLX_TRACE_POINT(0, 8);
+  // ---- phase B: (tile, group quad) tasks ----
   if (warp > 0) {
     const int cw = warp - 1;
     const int g = lane >> 2, tig = lane & 3;
     const int rrow = g + 8 * (tig & 1);
-    const int ntask = nbt * nGmax;
-    // the down tiles were requested at the start: wait for them once
-    bool ok = true;
-    for (int s = 0; s < nbt; ++s) ok &= mbar_wait(&fullB[s], 0, d.status);
-    SLX_TRACE_POINT(0, 11);
+    const int ntask = nbt * nq;
     for (int task = cw; task < ntask; task += kFW) {
-      const int s = task / nGmax, G = task % nGmax;
-      const int j = s % U;
+      const int s = task / nq, gq = task % nq;
+      const int j = (qb0 + s) % U;
       const int in = j >= d.k ? d.Is : d.I;
+      const int ng = tile_ng(in);
+      const int G0 = 4 * gq;
+      const bool ok = mbar_wait(&fullB[s], 0, d.status);
+      if (task == cw) SLX_TRACE_POINT(0, 11);
       float v = 0.f;
-      if (G < tile_ng(in) && ok && meta[kFMaxA + j])
-        v = down_group<BITS>(stB + (size_t)s * f.stage_b, in, G, g, tig,
-                             rrow, bfrag + (size_t)j * nGmax * 32,
-                             bxsum + (size_t)j * nGmax);
-      if (tig < 2) redB[((size_t)s * nGmax + G) * kRows + rrow] = v;
+      if (G0 < ng && ok && meta[kFMaxA + j])
+        v = down_quad<BITS>(stB + (size_t)s * f.stage_b, in, G0,
+                            ng - G0 < 4 ? ng - G0 : 4, g, tig, rrow,
+                            bfrag + (size_t)j * nGmax * 32,
+                            bxsum + (size_t)j * nGmax);
+      if (tig < 2) redB[((size_t)s * nq + gq) * kRows + rrow] = v;
+      if (task == cw) SLX_TRACE_POINT(1, 3);
     }
+    SLX_TRACE_POINT(1, 4);
   }
   __syncthreads();
   SLX_TRACE_POINT(0, 9);
-  // one warp per item: bf16 per unit, score weights, combine in unit order
-  if (warp < nb) {
-    const int it = warp;
-    const int q = qb0 + it;
-    const int row0 = q * kRows;
-    float y_out = 0.f;  // lane < 16: row lane
-    for (int j = 0; j < U; ++j) {
-      const int s = it * U + j;
-      const int in = j >= d.k ? d.Is : d.I;
-      const int ng = tile_ng(in);
+  // ---- per item: bf16 per unit, score weights, combine in unit order ----
+  const int i_first = qb0 / U, i_last = (qb0 + nbt - 1) / U;
+  for (int i = i_first + warp; i <= i_last; i += kFW + 1) {
+    const int j_lo = i * U < qb0 ? qb0 - i * U : 0;
+    const int j_hi = (i + 1) * U > qb0 + nbt ? qb0 + nbt - i * U : U;
+    const int row0 = i * kRows;
+    auto unit_y = [&](int j) {  // lane < 16: row lane of unit j
+      const int s = i * U + j - qb0;
       float v = 0.f;
       if (lane < kRows)
-        for (int G = 0; G < ng; ++G) v += redB[((size_t)s * nGmax + G) * kRows + lane];
-      const float y = meta[kFMaxA + j] ? round_bf16(v) : 0.f;
-      if (f.ep_on) {
-        if (meta[kFMaxA + j]) ep_write_rows(f, d, j, row0, y, lane);
-        continue;
+        for (int gq = 0; gq < nq; ++gq) v += redB[((size_t)s * nq + gq) * kRows + lane];
+      return meta[kFMaxA + j] ? round_bf16(v) : 0.f;
+    };
+    if (f.ep_on) {
+      for (int j = j_lo; j < j_hi; ++j)
+        if (meta[kFMaxA + j]) ep_write_rows(f, d, j, row0, unit_y(j), lane);
+      continue;
+    }
+    if (!d.scores) {
+      for (int j = j_lo; j < j_hi; ++j) {
+        const float y = unit_y(j);
+        if (lane < kRows) d.out[(size_t)j * d.H + row0 + lane] = f32_to_bf16(y);
       }
-      if (!d.scores) {
-        if (lane < kRows)
-          d.out[(size_t)j * d.H + row0 + lane] = f32_to_bf16(y);
-      } else {
-        y_out = (j < d.k) ? fmaf(d.scores[j], y, y_out) : y_out + y;
+      continue;
+    }
+    float y_out = 0.f;  // lane < 16: row lane
+    if (j_lo == 0 && j_hi == U) {
+      for (int j = 0; j < U; ++j) {
+        const float y = unit_y(j);
+        y_out = (j < d.k) ? fmaf(s_score[j], y, y_out) : y_out + y;
+      }
+      if (lane < kRows) d.out[row0 + lane] = f32_to_bf16(y_out);
+      continue;
+    }
+    // the item straddles CTAs
+    const int slot = split_slot(i, U, NB, G_);
+    float* ys = f.split_y + (size_t)slot * U * kRows;
+    unsigned* fl = f.split_flag + (size_t)slot * U;
+    for (int j = j_lo; j < j_hi; ++j) {
+      const float y = unit_y(j);
+      if (lane < kRows) ys[j * kRows + lane] = y;
+    }
+    __threadfence();
+    __syncwarp();
+    SLX_TRACE_POINT(1, 5);
+    if (j_hi < U) {
+      if (lane == 0)
+        for (int j = j_lo; j < j_hi; ++j)
+          asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(fl + j), "r"(epoch)
+                       : "memory");
+      continue;
+    }
+    // this CTA owns the item's last unit: wait for the other parts (one
+    // lane per flag), combine
+    {
+      const uint64_t t0 = globaltimer_ns();
+      for (uint32_t it = 0;; ++it) {
+        bool mine = true;
+        for (int j = lane; j < j_lo; j += 32) {
+          unsigned v;
+          asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(fl + j) : "memory");
+          mine &= v == epoch;
+        }
+        if (__all_sync(0xffffffffu, mine)) break;
+        bool late = (it & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs;
+        late = __shfl_sync(0xffffffffu, late, 0);
+        if (late) {
+          if (lane == 0) set_status(d.status, SLX_ERR_DEVICE_TIMEOUT);
+          break;
+        }
       }
     }
-    if (d.scores && !f.ep_on && lane < kRows)
-      d.out[row0 + lane] = f32_to_bf16(y_out);
+    __syncwarp();
+    SLX_TRACE_POINT(1, 6);
+    for (int j0 = 0; j0 < U; j0 += 16) {  // the loads of 16 units at once
+      float yv[16];
+#pragma unroll
+      for (int q = 0; q < 16; ++q)
+        yv[q] = (j0 + q < U && lane < kRows) ? __ldcg(ys + (j0 + q) * kRows + lane) : 0.f;
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        const int j = j0 + q;
+        if (j < U) y_out = (j < d.k) ? fmaf(s_score[j], yv[q], y_out) : y_out + yv[q];
+      }
+    }
+    if (lane < kRows) d.out[row0 + lane] = f32_to_bf16(y_out);
   }
   if (f.ep_on) {
     __syncthreads();
@@ -1279,34 +1514,57 @@ __global__ void __launch_bounds__(kFThreads, 1)
 }
 
 // Shared-memory layout of the fused kernel for one problem, or 0 if it
-// does not fit one CTA per SM.
+// does not fit one CTA per SM.  Preferred: gate/up stages and down stages
+// side by side (every copy requested at the start), the phase-B fragments
+// reusing the gate/up stages; else the down tiles reuse the gate/up stages
+// once phase A is done (b_late), their DRAM reads started as L2 prefetches.
 template <int BITS>
 static int fused_layout(FusedArgs& f, int grid) {
   const GemvArgs& a = f.a;
   const DownArgs& d = f.d;
   const int nG = tile_ng(a.in);
-  const int na_max = (a.n_tiles + grid - 1) / grid;
-  const int nb_max = (d.n_items + grid - 1) / grid;
   const int U = d.n_units;
-  if (na_max > kFMaxA || nb_max * U > kFMaxB || U > kFMaxUnits) return 0;
+  const int na_max = (a.n_tiles + grid - 1) / grid;
+  const int nb_max = (d.n_items * U + grid - 1) / grid;
+  if (na_max > kFMaxA || nb_max > kFMaxB || U > kFMaxUnits || a.k > kFMaxUnits)
+    return 0;
   const int nGr = tile_ng(d.I), nGs = d.Is ? tile_ng(d.Is) : 0;
   const int nGmax = nGr > nGs ? nGr : nGs;
+  const int nq = (nGmax + 3) / 4;
   auto al = [](int v) { return (v + 127) & ~127; };
-  int o = (kFMaxA + kFMaxB) * 8;
+  int o = (kFMaxA + kFMaxB + 2) * 8;
+  o = al(o); f.off_x = o;       o += a.in * 2;
   o = al(o); f.off_frag = o;    o += nG * 32 * 4;
   o = al(o); f.off_part = o;    o += nG * 4 * 4;
   o = al(o); f.off_xsum = o;    o += nG * 4;
-  o = al(o); f.off_reda = o;    o += kFMaxA * kFW * 32 * 4;
+  o = al(o); f.off_reda = o;    o += na_max * kFW * 32 * 4;
   o = al(o); f.off_meta = o;    o += (kFMaxA + kFMaxUnits) * 4;
-  o = al(o); f.off_bfrag = o;   o += U * nGmax * 32 * 4;
-  o = al(o); f.off_bpart = o;   o += U * nGmax * 4 * 4;
-  o = al(o); f.off_bxsum = o;   o += U * nGmax * 4;
-  o = al(o); f.off_redb = o;    o += nb_max * U * nGmax * kRows * 4;
+  o = al(o); f.off_redb = o;    o += nb_max * nq * kRows * 4;
+  const int bf = al(U * nGmax * 32 * 4), bp = al(U * nGmax * 4 * 4),
+            bx = al(U * nGmax * 4);
   f.stage_a = al((int)pair_tile_bytes(a.in, BITS));
   const int tb = d.tile_bytes > d.tile_bytes_sh ? d.tile_bytes : d.tile_bytes_sh;
   f.stage_b = al(tb);
-  o = al(o); f.off_stage_a = o;
-  const int bytes_a = na_max * f.stage_a, bytes_b = nb_max * U * f.stage_b;
+  const int bytes_a = na_max * f.stage_a, bytes_b = nb_max * f.stage_b;
+  // the routed units' SwiGLU fragments arrive in one bulk copy when their
+  // rows have the fragment buffer's stride
+  f.bfrag_bulk = nGr == nGmax && d.unit_frag_words == nGr * 32 &&
+                 d.unit_part_floats == nGr * 4;
+  o = al(o);
+  if (bf + bp + bx <= bytes_a && o + bytes_a + bytes_b <= kFusedSmemMax) {
+    f.b_late = 0;
+    f.off_stage_a = o;
+    f.off_bfrag = o;
+    f.off_bpart = o + bf;
+    f.off_bxsum = o + bf + bp;
+    f.off_stage_b = o + bytes_a;
+    return o + bytes_a + bytes_b;
+  }
+  f.off_bfrag = o;
+  f.off_bpart = o + bf;
+  f.off_bxsum = o + bf + bp;
+  o += bf + bp + bx;
+  f.off_stage_a = o;
   if (o + bytes_a + bytes_b <= kFusedSmemMax) {
     f.b_late = 0;
     f.off_stage_b = o + bytes_a;
@@ -1332,7 +1590,7 @@ static int launch_fused_t(FusedArgs f, cudaStream_t stream) {
       return SLX_ERR_CUDA;
     max_grid = per_sm >= 1 ? num_sms() : 0;
   }
-  if (max_grid <= 0) return SLX_ERR_UNSUPPORTED;
+  if (max_grid <= 0 || max_grid > kSplitMaxGrid) return SLX_ERR_UNSUPPORTED;
   const int grid = max_grid;
   const int bytes = fused_layout<BITS>(f, grid);
   if (bytes <= 0 || bytes > kFusedSmemMax) return SLX_ERR_UNSUPPORTED;
@@ -1341,24 +1599,38 @@ static int launch_fused_t(FusedArgs f, cudaStream_t stream) {
   cfg.blockDim = dim3(kFThreads);
   cfg.dynamicSmemBytes = bytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
+  // as a PDL secondary the launch's set-up overlaps the preceding kernel;
+  // the kernel waits (griddepcontrol.wait) before it reads anything
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k_switchglu_fused<BITS>, f) == cudaSuccess
-             ? SLX_OK : SLX_ERR_CUDA;
+  static int pdl_ok = 1;  // cleared if the driver refuses the combination
+  cfg.numAttrs = (pdl_ok && pdl_enabled()) ? 2 : 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_switchglu_fused<BITS>, f);
+  if (e != cudaSuccess && cfg.numAttrs == 2) {
+    (void)cudaGetLastError();
+    pdl_ok = 0;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, k_switchglu_fused<BITS>, f);
+  }
+  return e == cudaSuccess ? SLX_OK : SLX_ERR_CUDA;
 }
 
 int launch_switchglu_fused(const GemvArgs& a, const DownArgs& d, void* bar,
-                           int bits, cudaStream_t stream,
+                           void* split, int bits, cudaStream_t stream,
                            const slx_fill_service* svc,
                            const slx_ep_exchange* ep) {
-  if (a.T != 1 || d.T != 1) return SLX_ERR_UNSUPPORTED;
+  if (a.T != 1 || d.T != 1 || !split) return SLX_ERR_UNSUPPORTED;
   FusedArgs f = {};
   f.a = a;
   f.d = d;
   f.bar = reinterpret_cast<unsigned long long*>(bar);
+  f.split_flag = reinterpret_cast<unsigned*>(split);
+  f.split_y = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(split) +
+                                       split_flag_bytes(d.n_units));
   if (ep) {
     f.ep_on = 1;
     f.ep_rank = ep->rank;

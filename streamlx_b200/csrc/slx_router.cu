@@ -106,115 +106,16 @@ SLX_DEV float logit_bound(float s, float a, float logit, int depth) {
          1e-30f;
 }
 
-__global__ void __cluster_dims__(kRouterCluster, 1, 1)
-    __launch_bounds__(kRouterThreads, 1) k_router(const RouterLaunch L) {
-  namespace cg = cooperative_groups;
-  __shared__ __align__(16) float s_x[kRouterMaxH];
-  __shared__ float s_logit[kMaxExperts];   // cluster rank 0: the logits
-  __shared__ float s_bound[kMaxExperts];   // and their bounds (0 = exact)
-  __shared__ uint8_t s_gone[kMaxExperts];  // picked ids beyond the registers
-  __shared__ int s_cand[kMaxExperts];      // rows to recompute exactly
-  __shared__ int s_ncand;
-  __shared__ int s_cert;
-  cg::cluster_group cluster = cg::this_cluster();
-  const int rank = (int)cluster.block_rank();
-  const int head = blockIdx.x / kRouterCluster;
-  const RouterArgs& a = head ? L.h[1] : L.h[0];
-  const int t = blockIdx.y;
+// Ranking and outputs of one (head, token) from the logits and bounds in
+// shared memory (s_x: the token's staged activations, for the exact
+// recompute).  Every thread of the CTA calls this.
+__device__ __noinline__ void rank_and_write(const RouterArgs& a, int t,
+                                            const float* s_x, float* s_logit,
+                                            float* s_bound, uint8_t* s_gone,
+                                            int* s_cand, int& s_ncand,
+                                            int& s_cert) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int E = a.E, H = a.H, k = a.k;
-  const int epc = (E + kRouterCluster - 1) / kRouterCluster;
-  const int e_lo = rank * epc, e_hi = min(E, e_lo + epc);
-  // adds along one logit: the lane's chain, the 8-way tree, the butterfly
-  const int depth = (H + 255) / 256 + 3 + 5;
-  SLX_TRACE_POINT(0, 0);
-  pdl_launch_dependents();
-
-  // this warp's first row pair: gate rows are weights, in flight before
-  // the wait on the kernel that produced x
-  const int ea0 = e_lo + warp, eb0 = ea0 + kRouterWarps;
-  uint4 wa[kRouterBatch], wb[kRouterBatch];
-#pragma unroll
-  for (int i = 0; i < kRouterBatch; ++i) {
-    const int c = i * 256 + lane * 8;
-    wa[i] = (ea0 < e_hi && c < H)
-                ? __ldg(reinterpret_cast<const uint4*>(a.w + (size_t)ea0 * H + c))
-                : make_uint4(0, 0, 0, 0);
-    wb[i] = (eb0 < e_hi && c < H)
-                ? __ldg(reinterpret_cast<const uint4*>(a.w + (size_t)eb0 * H + c))
-                : make_uint4(0, 0, 0, 0);
-  }
-  pdl_wait_primary();
-  // stage x (times the ratio, rounded to bf16, for the predictor) as fp32
-  const uint16_t* xr = a.x + (size_t)t * H;
-  for (int c = threadIdx.x * 8; c < H; c += kRouterThreads * 8) {
-    const uint4 xv = *reinterpret_cast<const uint4*>(xr + c);
-    const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
-    uint32_t rw[4] = {0, 0, 0, 0};
-    if (a.ratio) {
-      const uint4 rv = *reinterpret_cast<const uint4*>(a.ratio + c);
-      rw[0] = rv.x; rw[1] = rv.y; rw[2] = rv.z; rw[3] = rv.w;
-    }
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      float x0 = bf16_lo(xw[q]), x1 = bf16_hi(xw[q]);
-      if (a.ratio) {
-        x0 = round_bf16(x0 * bf16_lo(rw[q]));
-        x1 = round_bf16(x1 * bf16_hi(rw[q]));
-      }
-      s_x[c + 2 * q] = x0;
-      s_x[c + 2 * q + 1] = x1;
-    }
-  }
-  __syncthreads();
-  SLX_TRACE_POINT(0, 1);
-  float* leader_logit = cluster.map_shared_rank(s_logit, 0);
-  float* leader_bound = cluster.map_shared_rank(s_bound, 0);
-  for (int ea = ea0; ea < e_hi; ea += 2 * kRouterWarps) {
-    const int eb = ea + kRouterWarps;
-    const bool hb = eb < e_hi;
-    float sA[8] = {0, 0, 0, 0, 0, 0, 0, 0}, aA[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    float sB[8] = {0, 0, 0, 0, 0, 0, 0, 0}, aB[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int base = 0; base < H; base += 256 * kRouterBatch) {
-      if (base > 0 || ea != ea0) {
-#pragma unroll
-        for (int i = 0; i < kRouterBatch; ++i) {
-          const int c = base + i * 256 + lane * 8;
-          wa[i] = c < H ? __ldg(reinterpret_cast<const uint4*>(
-                              a.w + (size_t)ea * H + c))
-                        : make_uint4(0, 0, 0, 0);
-          wb[i] = (hb && c < H) ? __ldg(reinterpret_cast<const uint4*>(
-                                      a.w + (size_t)eb * H + c))
-                                : make_uint4(0, 0, 0, 0);
-        }
-      }
-#pragma unroll
-      for (int i = 0; i < kRouterBatch; ++i) {
-        const int c = base + i * 256 + lane * 8;
-        if (c < H) {
-          dot8(s_x + c, wa[i], sA, aA);
-          dot8(s_x + c, wb[i], sB, aB);
-        }
-      }
-    }
-    const float ssa = warp_sum_f32(sum8(sA)), asa = warp_sum_f32(sum8(aA));
-    const float ssb = warp_sum_f32(sum8(sB)), asb = warp_sum_f32(sum8(aB));
-    if (lane == 0) {
-      const float la = a.bias ? ssa + a.bias[ea] : ssa;
-      leader_logit[ea] = la;
-      leader_bound[ea] = logit_bound(ssa, asa, la, depth);
-      if (hb) {
-        const float lb = a.bias ? ssb + a.bias[eb] : ssb;
-        leader_logit[eb] = lb;
-        leader_bound[eb] = logit_bound(ssb, asb, lb, depth);
-      }
-    }
-  }
-  SLX_TRACE_POINT(0, 2);
-  cluster.sync();  // every logit and bound is in rank 0's shared memory
-  SLX_TRACE_POINT(0, 3);
-  if (rank != 0) return;
-
   const bool forced = a.force && a.force[t];
   int id1 = -1, id2 = -1;  // rank `lane` and rank `lane + 32`
   // k rounds of a warp-wide (max key, min id) over the experts (only the
@@ -400,6 +301,227 @@ __global__ void __cluster_dims__(kRouterCluster, 1, 1)
   SLX_TRACE_AT(0, 6, slx::globaltimer_ns());
 }
 
+__global__ void __cluster_dims__(kRouterCluster, 1, 1)
+    __launch_bounds__(kRouterThreads, 1) k_router(const RouterLaunch L) {
+  namespace cg = cooperative_groups;
+  __shared__ __align__(16) float s_x[kRouterMaxH];
+  __shared__ float s_logit[kMaxExperts];   // cluster rank 0: the logits
+  __shared__ float s_bound[kMaxExperts];   // and their bounds (0 = exact)
+  __shared__ uint8_t s_gone[kMaxExperts];  // picked ids beyond the registers
+  __shared__ int s_cand[kMaxExperts];      // rows to recompute exactly
+  __shared__ int s_ncand;
+  __shared__ int s_cert;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int head = blockIdx.x / kRouterCluster;
+  const RouterArgs& a = head ? L.h[1] : L.h[0];
+  const int t = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int E = a.E, H = a.H;
+  const int epc = (E + kRouterCluster - 1) / kRouterCluster;
+  const int e_lo = rank * epc, e_hi = min(E, e_lo + epc);
+  // adds along one logit: the lane's chain, the 8-way tree, the butterfly
+  const int depth = (H + 255) / 256 + 3 + 5;
+  SLX_TRACE_POINT(0, 0);
+  pdl_launch_dependents();
+
+  // this warp's first row pair: gate rows are weights, in flight before
+  // the wait on the kernel that produced x
+  const int ea0 = e_lo + warp, eb0 = ea0 + kRouterWarps;
+  uint4 wa[kRouterBatch], wb[kRouterBatch];
+#pragma unroll
+  for (int i = 0; i < kRouterBatch; ++i) {
+    const int c = i * 256 + lane * 8;
+    wa[i] = (ea0 < e_hi && c < H)
+                ? __ldg(reinterpret_cast<const uint4*>(a.w + (size_t)ea0 * H + c))
+                : make_uint4(0, 0, 0, 0);
+    wb[i] = (eb0 < e_hi && c < H)
+                ? __ldg(reinterpret_cast<const uint4*>(a.w + (size_t)eb0 * H + c))
+                : make_uint4(0, 0, 0, 0);
+  }
+  pdl_wait_primary();
+  // stage x (times the ratio, rounded to bf16, for the predictor) as fp32
+  const uint16_t* xr = a.x + (size_t)t * H;
+  for (int c = threadIdx.x * 8; c < H; c += kRouterThreads * 8) {
+    const uint4 xv = *reinterpret_cast<const uint4*>(xr + c);
+    const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+    uint32_t rw[4] = {0, 0, 0, 0};
+    if (a.ratio) {
+      const uint4 rv = *reinterpret_cast<const uint4*>(a.ratio + c);
+      rw[0] = rv.x; rw[1] = rv.y; rw[2] = rv.z; rw[3] = rv.w;
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float x0 = bf16_lo(xw[q]), x1 = bf16_hi(xw[q]);
+      if (a.ratio) {
+        x0 = round_bf16(x0 * bf16_lo(rw[q]));
+        x1 = round_bf16(x1 * bf16_hi(rw[q]));
+      }
+      s_x[c + 2 * q] = x0;
+      s_x[c + 2 * q + 1] = x1;
+    }
+  }
+  __syncthreads();
+  SLX_TRACE_POINT(0, 1);
+  float* leader_logit = cluster.map_shared_rank(s_logit, 0);
+  float* leader_bound = cluster.map_shared_rank(s_bound, 0);
+  for (int ea = ea0; ea < e_hi; ea += 2 * kRouterWarps) {
+    const int eb = ea + kRouterWarps;
+    const bool hb = eb < e_hi;
+    float sA[8] = {0, 0, 0, 0, 0, 0, 0, 0}, aA[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    float sB[8] = {0, 0, 0, 0, 0, 0, 0, 0}, aB[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int base = 0; base < H; base += 256 * kRouterBatch) {
+      if (base > 0 || ea != ea0) {
+#pragma unroll
+        for (int i = 0; i < kRouterBatch; ++i) {
+          const int c = base + i * 256 + lane * 8;
+          wa[i] = c < H ? __ldg(reinterpret_cast<const uint4*>(
+                              a.w + (size_t)ea * H + c))
+                        : make_uint4(0, 0, 0, 0);
+          wb[i] = (hb && c < H) ? __ldg(reinterpret_cast<const uint4*>(
+                                      a.w + (size_t)eb * H + c))
+                                : make_uint4(0, 0, 0, 0);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kRouterBatch; ++i) {
+        const int c = base + i * 256 + lane * 8;
+        if (c < H) {
+          dot8(s_x + c, wa[i], sA, aA);
+          dot8(s_x + c, wb[i], sB, aB);
+        }
+      }
+    }
+    const float ssa = warp_sum_f32(sum8(sA)), asa = warp_sum_f32(sum8(aA));
+    const float ssb = warp_sum_f32(sum8(sB)), asb = warp_sum_f32(sum8(aB));
+    if (lane == 0) {
+      const float la = a.bias ? ssa + a.bias[ea] : ssa;
+      leader_logit[ea] = la;
+      leader_bound[ea] = logit_bound(ssa, asa, la, depth);
+      if (hb) {
+        const float lb = a.bias ? ssb + a.bias[eb] : ssb;
+        leader_logit[eb] = lb;
+        leader_bound[eb] = logit_bound(ssb, asb, lb, depth);
+      }
+    }
+  }
+  SLX_TRACE_POINT(0, 2);
+  cluster.sync();  // every logit and bound is in rank 0's shared memory
+  SLX_TRACE_POINT(0, 3);
+  if (rank != 0) return;
+
+  rank_and_write(a, t, s_x, s_logit, s_bound, s_gone, s_cand, s_ncand, s_cert);
+}
+
+// One-token form over many SMs: CTA c of a head owns kWideRows gate rows,
+// brought into shared memory by one bulk copy issued before the kernel
+// waits on its predecessor (the gate is immutable); four warps per row each
+// take a quarter of the columns.  Each CTA leaves its rows' logits and
+// bounds in the head's scratch and takes a ticket; the CTA that takes the
+// last one ranks the head (rank_and_write) and puts the ticket back to 0.
+constexpr int kWideRows = 4;
+constexpr int kWideSplit = kRouterWarps / kWideRows;  // warps per row
+
+struct WideLaunch {
+  RouterArgs h[2];
+  float* bound[2];  // [E] per head
+  int n_heads, ctas_per_head;
+};
+
+__global__ void __launch_bounds__(kRouterThreads, 1)
+    k_router_wide(const __grid_constant__ WideLaunch L) {
+  extern __shared__ __align__(128) uint8_t wsm[];  // the CTA's gate rows (bf16)
+  __shared__ __align__(16) float s_x[kRouterMaxH];
+  __shared__ float s_logit[kMaxExperts];
+  __shared__ float s_bound[kMaxExperts];
+  __shared__ uint8_t s_gone[kMaxExperts];
+  __shared__ int s_cand[kMaxExperts];
+  __shared__ int s_ncand, s_cert, s_last;
+  __shared__ float s_part[kWideRows][kWideSplit][2];
+  __shared__ __align__(8) uint64_t s_bar;
+  const int head = blockIdx.x / L.ctas_per_head, cb = blockIdx.x % L.ctas_per_head;
+  const RouterArgs& a = head ? L.h[1] : L.h[0];
+  float* gbound = L.bound[head];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int E = a.E, H = a.H;
+  const int e0 = cb * kWideRows;
+  const int nr = E - e0 < kWideRows ? E - e0 : kWideRows;
+  const uint16_t* rows = reinterpret_cast<const uint16_t*>(wsm);
+  if (threadIdx.x == 0) {
+    mbar_init(&s_bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(&s_bar, (uint32_t)nr * H * 2);
+    bulk_g2s_plain(wsm, a.w + (size_t)e0 * H, (uint32_t)nr * H * 2, &s_bar);
+  }
+  pdl_launch_dependents();
+  pdl_wait_primary();
+  const uint16_t* xr = a.x;  // one token
+  for (int c = threadIdx.x * 8; c < H; c += kRouterThreads * 8) {
+    const uint4 xv = *reinterpret_cast<const uint4*>(xr + c);
+    const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+    uint32_t rw[4] = {0, 0, 0, 0};
+    if (a.ratio) {
+      const uint4 rv = *reinterpret_cast<const uint4*>(a.ratio + c);
+      rw[0] = rv.x; rw[1] = rv.y; rw[2] = rv.z; rw[3] = rv.w;
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float x0 = bf16_lo(xw[q]), x1 = bf16_hi(xw[q]);
+      if (a.ratio) {
+        x0 = round_bf16(x0 * bf16_lo(rw[q]));
+        x1 = round_bf16(x1 * bf16_hi(rw[q]));
+      }
+      s_x[c + 2 * q] = x0;
+      s_x[c + 2 * q + 1] = x1;
+    }
+  }
+  __syncthreads();
+  const bool ok = mbar_wait(&s_bar, 0, a.status);
+  // row r, column quarter q: eight fp32 chains per lane, then the tree
+  const int r = warp / kWideSplit, q = warp % kWideSplit;
+  const int Hq = H / kWideSplit;
+  float sv[8] = {0, 0, 0, 0, 0, 0, 0, 0}, av[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (ok && r < nr)
+    for (int c = q * Hq + lane * 8; c < (q + 1) * Hq; c += 256)
+      dot8(s_x + c, *reinterpret_cast<const uint4*>(rows + (size_t)r * H + c), sv, av);
+  const float ss = warp_sum_f32(sum8(sv)), as = warp_sum_f32(sum8(av));
+  if (lane == 0) {
+    s_part[r][q][0] = ss;
+    s_part[r][q][1] = as;
+  }
+  __syncthreads();
+  // adds along one logit: the lane's chain, the 8-way tree, the butterfly,
+  // the quarters
+  const int depth = (Hq + 255) / 256 + 3 + 5 + 2;
+  if (threadIdx.x < nr) {
+    const int rr = threadIdx.x, e = e0 + rr;
+    const float S = (s_part[rr][0][0] + s_part[rr][1][0]) + (s_part[rr][2][0] + s_part[rr][3][0]);
+    const float A = (s_part[rr][0][1] + s_part[rr][1][1]) + (s_part[rr][2][1] + s_part[rr][3][1]);
+    const float l = a.bias ? S + a.bias[e] : S;
+    a.logits[e] = l;
+    gbound[e] = logit_bound(S, A, l, depth);
+    __threadfence();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int old = ticket_acq_rel(a.tickets);
+    s_last = old == L.ctas_per_head - 1;
+    if (s_last) *reinterpret_cast<volatile int32_t*>(a.tickets) = 0;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  for (int e = threadIdx.x; e < E; e += kRouterThreads) {
+    s_logit[e] = __ldcg(a.logits + e);
+    s_bound[e] = __ldcg(gbound + e);
+  }
+  __syncthreads();
+  rank_and_write(a, 0, s_x, s_logit, s_bound, s_gone, s_cand, s_ncand, s_cert);
+}
+
 int launch_router_heads(const RouterArgs* heads, int n_heads,
                         cudaStream_t stream) {
   if (n_heads < 1 || n_heads > 2) return SLX_ERR_INVALID;
@@ -414,6 +536,28 @@ int launch_router_heads(const RouterArgs* heads, int n_heads,
   }
   if (a.T <= 0) return SLX_OK;
   if (a.T > 65535) return SLX_ERR_INVALID;
+  if (a.T == 1 && a.H % (8 * kWideSplit) == 0 && heads[0].bound &&
+      (n_heads < 2 || heads[1].bound)) {
+    WideLaunch W = {};
+    W.h[0] = heads[0];
+    W.h[1] = n_heads > 1 ? heads[1] : heads[0];
+    W.bound[0] = heads[0].bound;
+    W.bound[1] = W.h[1].bound;
+    W.n_heads = n_heads;
+    W.ctas_per_head = (a.E + kWideRows - 1) / kWideRows;
+    const int smem = kWideRows * a.H * 2;
+    static bool attr = false;
+    if (!attr) {
+      if (cudaFuncSetAttribute(k_router_wide,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               kWideRows * kRouterMaxH * 2) != cudaSuccess)
+        return SLX_ERR_CUDA;
+      attr = true;
+    }
+    return launch_k(k_router_wide, dim3(W.ctas_per_head * n_heads),
+                    dim3(kRouterThreads), smem, stream, W) == cudaSuccess
+               ? SLX_OK : SLX_ERR_CUDA;
+  }
   RouterLaunch L = {};
   L.h[0] = heads[0];
   L.h[1] = n_heads > 1 ? heads[1] : heads[0];

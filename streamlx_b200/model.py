@@ -497,16 +497,17 @@ class SynthDecoder:
                     [self.g_ctrl.numel() * 4])
         s = torch.cuda.Stream(device=self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
-        # one eager pass on the side stream initialises every launcher
-        # (function attributes, lazy module loads) outside the capture
-        with torch.cuda.stream(s):
-            for i in range(n):
-                self._record_layer(i, serviced=False)
-            self._record_tail(serviced=False)
-        s.synchronize()
-        self._pred_flags = [self._pred_on(i) for i in range(n)]
         prev_pdl = L.set_pdl(self.pdl)
         try:
+            # one eager pass on the side stream initialises every launcher
+            # (function attributes, lazy module loads, the launch-attribute
+            # choices) outside the capture
+            with torch.cuda.stream(s):
+                for i in range(n):
+                    self._record_layer(i, serviced=False)
+                self._record_tail(serviced=False)
+            s.synchronize()
+            self._pred_flags = [self._pred_on(i) for i in range(n)]
             full = torch.cuda.CUDAGraph()
             c0 = L.LAUNCHES[0]
             with torch.cuda.graph(full, stream=s,

@@ -237,9 +237,10 @@ def test_qlinear_parity(dev, shape):
     check_close(bf16_np(y), A.qmv(x, deq))
 
 
+@pytest.mark.parametrize("T", [6, 1])    # 1: the many-SM one-token form
 @pytest.mark.parametrize("mode", ["plain", "ratio", "forced"])
-def test_router_parity(dev, mode):
-    T, H, E, k = 6, 2560, 256, 10
+def test_router_parity(dev, mode, T):
+    H, E, k = 2560, 256, 10
     rng = np.random.default_rng(5)
     x = A.bf16_round(rng.standard_normal((T, H)).astype(np.float32))
     wg = A.bf16_round((rng.standard_normal((E, H)) / np.sqrt(H))
@@ -253,7 +254,7 @@ def test_router_parity(dev, mode):
         xin = A.bf16_round(x * ratio)
     force = forced = None
     if mode == "forced":
-        force = np.array([1, 0, 1, 0, 0, 1], dtype=np.int32)
+        force = np.array([1, 0, 1, 0, 0, 1][:T], dtype=np.int32)
         forced = np.stack([rng.choice(E, k, replace=False)
                            for _ in range(T)]).astype(np.int32)
     ids_w, sc_w, _ = A.router(xin, A.bf16_to_bits(wg), bias, k, True)
