@@ -1201,12 +1201,14 @@ __global__ void __launch_bounds__(kFThreads, 1)
     __syncthreads();
   };
   lookup_slots();
-  if (f.svc_on) {
-    if (bid == 0 && threadIdx.x == 0) svc_write_log(f, a, s_need);
-    if (s_need) {  // the same verdict in every CTA (same ids, same table)
-      svc_fill<BITS>(f, a);
-      lookup_slots();
-    }
+  // the layer record for the host: before a park (the host serves from it),
+  // else after this CTA's copies are requested (a system-scope store costs
+  // a host round trip)
+  const bool log_late = f.svc_on && !s_need;
+  if (f.svc_on && s_need) {  // the same verdict in every CTA (same ids, same table)
+    if (bid == 0 && threadIdx.x == 0) svc_write_log(f, a, 1);
+    svc_fill<BITS>(f, a);
+    lookup_slots();
   }
 
   // source of this CTA's down tile s (null: the unit has no slot)
@@ -1253,6 +1255,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
     }
     if (!f.b_late) {
       issue_b();
+      if (log_late && bid == 0 && lane == 0) svc_write_log(f, a, 0);
     } else {
       // the down tiles share the gate/up stages: start their DRAM reads now
       // into L2, the copies into shared memory follow once phase A is done
@@ -1261,6 +1264,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
         const uint8_t* src = b_src(s, bytes);
         if (src) bulk_prefetch_l2(src, bytes);
       }
+      if (log_late && bid == 0 && lane == 0) svc_write_log(f, a, 0);
     }
   } else {
     // ---- activation fragments of the token (per-token scale first) ----

@@ -176,7 +176,7 @@ class SynthDecoder:
 
     @classmethod
     def from_checkpoint(cls, model_dir: str, index=None, device=None,
-                        max_len: int = 1024) -> "SynthDecoder":
+                        max_len: int = 2048) -> "SynthDecoder":
         with open(os.path.join(model_dir, "config.json")) as f:
             cfg = SynthConfig(**json.load(f)["streamlx_synthetic"])
         index = index or SafetensorsIndex(model_dir)
