@@ -77,11 +77,8 @@ size_t slx_switchglu_scratch_bytes(int T, int k, int inter, int shared_inter) {
   const size_t u = (size_t)T * k, ng = inter / 64, ngs = shared_inter / 64;
   // the first 256 bytes: grid-barrier words of the fused decode kernel (at
   // a fixed place, so calls of any shape sharing one scratch agree on them)
-  // then the split area of the one-launch decode path (T == 1): per CTA
-  // boundary, the rows of a down item that straddles it (slx_qgemv.cu)
   return 256 + align256(u * ng * 128) + align256(u * ng * 16) +
-         align256((size_t)T * ngs * 128) + align256((size_t)T * ngs * 16) +
-         align256(slx::split_area_bytes(k + (shared_inter > 0 ? 1 : 0)));
+         align256((size_t)T * ngs * 128) + align256((size_t)T * ngs * 16);
 }
 
 size_t slx_expert_tiled_bytes(int hidden, int inter, int bits) {
@@ -353,8 +350,6 @@ static int switchglu_impl(const slx_expert_bank* bank,
   uint32_t* hfrag_sh = reinterpret_cast<uint32_t*>(sp);
   sp += align256((size_t)T * ngs * 128);
   float* hpart_sh = reinterpret_cast<float*>(sp);
-  sp += align256((size_t)T * ngs * 16);
-  void* split = sp;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
 
   slx::GemvArgs a = {};
@@ -417,7 +412,7 @@ static int switchglu_impl(const slx_expert_bank* bank,
     d.tile_bytes_sh = Is ? (int)slx::single_tile_bytes(Is, bits) : 0;
     d.a_bytes = (long long)slx::expert_a_bytes(H, I, bits);
     d.a_bytes_sh = Is ? (long long)slx::expert_a_bytes(H, Is, bits) : 0;
-    rc = slx::launch_switchglu_fused(a, d, gbar, split, bits, s, svc, ep);
+    rc = slx::launch_switchglu_fused(a, d, gbar, bits, s, svc, ep);
     if (rc != SLX_ERR_UNSUPPORTED) {
       g_glu_kernels = rc ? 0 : 1;
       return rc ? cuda_check(rc, "slx_switchglu fused") : SLX_OK;

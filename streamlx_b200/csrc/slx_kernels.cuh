@@ -5,17 +5,6 @@
 
 namespace slx {
 
-// Largest grid of the one-launch decode SwitchGLU: its scratch keeps one
-// split record per CTA boundary (slx_switchglu_scratch_bytes).
-constexpr int kSplitMaxGrid = 512;
-
-inline size_t split_flag_bytes(int n_units) {
-  return ((size_t)kSplitMaxGrid * n_units * 4 + 255) / 256 * 256;
-}
-inline size_t split_area_bytes(int n_units) {
-  return split_flag_bytes(n_units) + (size_t)kSplitMaxGrid * n_units * 16 * 4;
-}
-
 struct GemvArgs {
   int mode;  // SLX_GEMV_GLU or SLX_GEMV_LINEAR
   const uint16_t* x;
@@ -94,10 +83,8 @@ struct RouterArgs {
 
 int launch_gemv(GemvArgs a, int bits, cudaStream_t stream, bool pdl_secondary);
 int launch_down(DownArgs a, int bits, cudaStream_t stream);
-// bar: the scratch's barrier words; split: its split area
-// (split_area_bytes(n_units) bytes)
 int launch_switchglu_fused(const GemvArgs& a, const DownArgs& d, void* bar,
-                           void* split, int bits, cudaStream_t stream,
+                           int bits, cudaStream_t stream,
                            const slx_fill_service* svc = nullptr,
                            const slx_ep_exchange* ep = nullptr);
 int launch_ep_combine_rmsnorm(const slx_ep_exchange& ep, const float* scores,

@@ -781,10 +781,6 @@ struct FusedArgs {
   const int32_t* ep_stamp;
   uint16_t* ep_recv[SLX_EP_MAX_RANKS];
   unsigned int* ep_count[SLX_EP_MAX_RANKS];
-  // split area of the scratch: per CTA boundary, the bf16 rows of the units
-  // of an item that straddles it, and one epoch flag per unit
-  float* split_y;          // [kSplitMaxGrid][n_units][16]
-  unsigned* split_flag;    // [kSplitMaxGrid][n_units]
 };
 
 SLX_DEV unsigned long long ld_acquire_u64(const unsigned long long* p) {
@@ -801,16 +797,12 @@ SLX_DEV void red_release_add_u64(unsigned long long* p, unsigned long long v) {
 // [n * nblocks, (n + 1) * nblocks) on entry (the earlier launches are
 // complete), add one each with a release reduction (no reply to wait for,
 // unlike a returning atomic), and wait until it reaches (n + 1) * nblocks.
-// `epoch` (optional) receives target / nblocks: a number no earlier barrier
-// on this counter produced.
 SLX_DEV bool grid_barrier(unsigned long long* cnt, int nblocks,
                           int32_t* status,
-                          unsigned long long limit_ns = kWaitLimitNs,
-                          unsigned long long* epoch = nullptr) {
+                          unsigned long long limit_ns = kWaitLimitNs) {
   const unsigned long long nb = (unsigned long long)nblocks;
   const unsigned long long v = ld_acquire_u64(cnt);
   const unsigned long long target = v - v % nb + nb;
-  if (epoch) *epoch = target / nb;
   red_release_add_u64(cnt, 1ull);
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 0; ld_acquire_u64(cnt) < target; ++i) {
@@ -1114,16 +1106,6 @@ __device__ __noinline__ void load_bfrag_lsu(const DownArgs& d, uint32_t* bfrag,
   }
 }
 
-// Phase B splits the token's (16-row item, unit) down tiles evenly over the
-// CTAs, item-major: CTA b owns tiles [NB b / G, NB (b + 1) / G).  An item
-// whose tiles straddle CTAs is combined by the CTA that owns its last unit:
-// the other parts leave their units' bf16 rows in the scratch's split area
-// (slot = the first CTA boundary inside the item) and a flag per unit that
-// holds the launch's barrier epoch, so no word ever needs resetting.
-SLX_DEV int split_slot(int item, int U, int NB, int G) {
-  return (int)((((long long)item * U + 1) * G + NB - 1) / NB);
-}
-
 template <int BITS>
 __global__ void __launch_bounds__(kFThreads, 1)
     k_switchglu_fused(const __grid_constant__ FusedArgs f) {
@@ -1151,7 +1133,6 @@ __global__ void __launch_bounds__(kFThreads, 1)
   __shared__ int s_slot[kFMaxUnits];
   __shared__ float s_score[kFMaxUnits];  // combine weight per unit (shared: 1)
   __shared__ int s_need;
-  __shared__ unsigned s_epoch;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G_ = gridDim.x, bid = blockIdx.x;
   const int nG = tile_ng(a.in);
@@ -1160,9 +1141,11 @@ __global__ void __launch_bounds__(kFThreads, 1)
   const int qa0 = (int)((long long)a.n_tiles * bid / G_);
   const int na = (int)((long long)a.n_tiles * (bid + 1) / G_) - qa0;
   const int U = d.n_units;
-  const int NB = d.n_items * U;
-  const int qb0 = (int)((long long)NB * bid / G_);
-  const int nbt = (int)((long long)NB * (bid + 1) / G_) - qb0;  // down tiles here
+  // phase B: whole 16-row items per CTA (an item's units combine in the
+  // CTA that computed them), item-major tiles [qb0, qb0 + nbt)
+  const int it0 = (int)((long long)d.n_items * bid / G_);
+  const int qb0 = it0 * U;
+  const int nbt = ((int)((long long)d.n_items * (bid + 1) / G_) - it0) * U;
   const int nGr = tile_ng(d.I), nGs = d.Is ? tile_ng(d.Is) : 0;
   const int nGmax = nGr > nGs ? nGr : nGs;
   const int nq = (nGmax + 3) >> 2;
@@ -1201,6 +1184,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
     __syncthreads();
   };
   lookup_slots();
+  if (threadIdx.x == 0) SLX_TRACE_AT(1, 12, globaltimer_ns());
   // the layer record for the host: before a park (the host serves from it),
   // else after this CTA's copies are requested (a system-scope store costs
   // a host round trip)
@@ -1249,13 +1233,8 @@ __global__ void __launch_bounds__(kFThreads, 1)
       else
         mbar_arrive(&fullA[lane]);
     }
-    for (int j = lane; j < U; j += 32) {
-      meta[kFMaxA + j] = j >= d.k || s_slot[j] >= 0;
-      s_score[j] = (d.scores && j < d.k) ? d.scores[j] : 1.f;
-    }
     if (!f.b_late) {
       issue_b();
-      if (log_late && bid == 0 && lane == 0) svc_write_log(f, a, 0);
     } else {
       // the down tiles share the gate/up stages: start their DRAM reads now
       // into L2, the copies into shared memory follow once phase A is done
@@ -1264,12 +1243,21 @@ __global__ void __launch_bounds__(kFThreads, 1)
         const uint8_t* src = b_src(s, bytes);
         if (src) bulk_prefetch_l2(src, bytes);
       }
-      if (log_late && bid == 0 && lane == 0) svc_write_log(f, a, 0);
     }
+    if (lane == 0) SLX_TRACE_AT(1, 13, globaltimer_ns());
+    // after every request (each copy instruction orders after the memory
+    // operations before it): the units' validity and combine weights, read
+    // in phase B, and the host record
+    for (int j = lane; j < U; j += 32) {
+      meta[kFMaxA + j] = j >= d.k || s_slot[j] >= 0;
+      s_score[j] = (d.scores && j < d.k) ? d.scores[j] : 1.f;
+    }
+    if (log_late && bid == 0 && lane == 0) svc_write_log(f, a, 0);
   } else {
     // ---- activation fragments of the token (per-token scale first) ----
     const int ct = threadIdx.x - 32;
     mbar_wait(fullX, 0, a.status);
+    SLX_TRACE_POINT(1, 14);
     const float m = absmax_part(xs, a.in, ct, kFW * 32);
     if (lane == 0) s_vmax[warp - 1] = m;
     named_bar_fused();
@@ -1279,15 +1267,16 @@ __global__ void __launch_bounds__(kFThreads, 1)
     if (ct == 0) s_vunit = pow2f(24 - ve);
     for (int p = ct; p < 4 * nG; p += kFW * 32)
       frag_task<BITS>(xs, p >> 2, p & 3, frag, part, a.status, pow2f(ve));
+    // the compute warps only: phase A need not wait for warp 0's requests
+    named_bar_fused();
+    frag_sums(part, xsum, nG, ct, kFW * 32);
+    named_bar_fused();
   }
-  __syncthreads();
-  const float vunit = s_vunit;
-  if (warp > 0) frag_sums(part, xsum, nG, threadIdx.x - 32, kFW * 32);
-  __syncthreads();
   SLX_TRACE_POINT(0, 1);
 
   // ---- phase A: gate/up groups ----
   if (warp > 0) {
+    const float vunit = s_vunit;
     const int cw = warp - 1;
     const int g = lane >> 2, tig = lane & 3;
     const int mat = tig >> 1;
@@ -1357,11 +1346,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
     else SLX_TRACE_POINT(1, 11);
   }
 #endif
-  if (threadIdx.x == 0) {
-    unsigned long long ep = 0;
-    grid_barrier(f.bar, G_, a.status, kWaitLimitNs, &ep);
-    s_epoch = (unsigned)ep;
-  }
+  if (threadIdx.x == 0) grid_barrier(f.bar, G_, a.status);
   __syncthreads();
   SLX_TRACE_POINT(0, 7);
   pdl_launch_dependents();
@@ -1369,7 +1354,6 @@ __global__ void __launch_bounds__(kFThreads, 1)
     if (f.ep_on) ep_signal(f);
     return;
   }
-  const unsigned epoch = s_epoch;
 
   // ---- phase B: fragments of the units (bulk copies from L2) ----
   if (f.bfrag_bulk) {
@@ -1426,8 +1410,6 @@ __global__ void __launch_bounds__(kFThreads, 1)
   // ---- per item: bf16 per unit, score weights, combine in unit order ----
   const int i_first = qb0 / U, i_last = (qb0 + nbt - 1) / U;
   for (int i = i_first + warp; i <= i_last; i += kFW + 1) {
-    const int j_lo = i * U < qb0 ? qb0 - i * U : 0;
-    const int j_hi = (i + 1) * U > qb0 + nbt ? qb0 + nbt - i * U : U;
     const int row0 = i * kRows;
     auto unit_y = [&](int j) {  // lane < 16: row lane of unit j
       const int s = i * U + j - qb0;
@@ -1437,76 +1419,21 @@ __global__ void __launch_bounds__(kFThreads, 1)
       return meta[kFMaxA + j] ? round_bf16(v) : 0.f;
     };
     if (f.ep_on) {
-      for (int j = j_lo; j < j_hi; ++j)
+      for (int j = 0; j < U; ++j)
         if (meta[kFMaxA + j]) ep_write_rows(f, d, j, row0, unit_y(j), lane);
       continue;
     }
     if (!d.scores) {
-      for (int j = j_lo; j < j_hi; ++j) {
+      for (int j = 0; j < U; ++j) {
         const float y = unit_y(j);
         if (lane < kRows) d.out[(size_t)j * d.H + row0 + lane] = f32_to_bf16(y);
       }
       continue;
     }
     float y_out = 0.f;  // lane < 16: row lane
-    if (j_lo == 0 && j_hi == U) {
-      for (int j = 0; j < U; ++j) {
-        const float y = unit_y(j);
-        y_out = (j < d.k) ? fmaf(s_score[j], y, y_out) : y_out + y;
-      }
-      if (lane < kRows) d.out[row0 + lane] = f32_to_bf16(y_out);
-      continue;
-    }
-    // the item straddles CTAs
-    const int slot = split_slot(i, U, NB, G_);
-    float* ys = f.split_y + (size_t)slot * U * kRows;
-    unsigned* fl = f.split_flag + (size_t)slot * U;
-    for (int j = j_lo; j < j_hi; ++j) {
+    for (int j = 0; j < U; ++j) {
       const float y = unit_y(j);
-      if (lane < kRows) ys[j * kRows + lane] = y;
-    }
-    __threadfence();
-    __syncwarp();
-    SLX_TRACE_POINT(1, 5);
-    if (j_hi < U) {
-      if (lane == 0)
-        for (int j = j_lo; j < j_hi; ++j)
-          asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(fl + j), "r"(epoch)
-                       : "memory");
-      continue;
-    }
-    // this CTA owns the item's last unit: wait for the other parts (one
-    // lane per flag), combine
-    {
-      const uint64_t t0 = globaltimer_ns();
-      for (uint32_t it = 0;; ++it) {
-        bool mine = true;
-        for (int j = lane; j < j_lo; j += 32) {
-          unsigned v;
-          asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(fl + j) : "memory");
-          mine &= v == epoch;
-        }
-        if (__all_sync(0xffffffffu, mine)) break;
-        bool late = (it & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs;
-        late = __shfl_sync(0xffffffffu, late, 0);
-        if (late) {
-          if (lane == 0) set_status(d.status, SLX_ERR_DEVICE_TIMEOUT);
-          break;
-        }
-      }
-    }
-    __syncwarp();
-    SLX_TRACE_POINT(1, 6);
-    for (int j0 = 0; j0 < U; j0 += 16) {  // the loads of 16 units at once
-      float yv[16];
-#pragma unroll
-      for (int q = 0; q < 16; ++q)
-        yv[q] = (j0 + q < U && lane < kRows) ? __ldcg(ys + (j0 + q) * kRows + lane) : 0.f;
-#pragma unroll
-      for (int q = 0; q < 16; ++q) {
-        const int j = j0 + q;
-        if (j < U) y_out = (j < d.k) ? fmaf(s_score[j], yv[q], y_out) : y_out + yv[q];
-      }
+      y_out = (j < d.k) ? fmaf(s_score[j], y, y_out) : y_out + y;
     }
     if (lane < kRows) d.out[row0 + lane] = f32_to_bf16(y_out);
   }
@@ -1529,7 +1456,7 @@ static int fused_layout(FusedArgs& f, int grid) {
   const int nG = tile_ng(a.in);
   const int U = d.n_units;
   const int na_max = (a.n_tiles + grid - 1) / grid;
-  const int nb_max = (d.n_items * U + grid - 1) / grid;
+  const int nb_max = (d.n_items + grid - 1) / grid * U;
   if (na_max > kFMaxA || nb_max > kFMaxB || U > kFMaxUnits || a.k > kFMaxUnits)
     return 0;
   const int nGr = tile_ng(d.I), nGs = d.Is ? tile_ng(d.Is) : 0;
@@ -1594,7 +1521,7 @@ static int launch_fused_t(FusedArgs f, cudaStream_t stream) {
       return SLX_ERR_CUDA;
     max_grid = per_sm >= 1 ? num_sms() : 0;
   }
-  if (max_grid <= 0 || max_grid > kSplitMaxGrid) return SLX_ERR_UNSUPPORTED;
+  if (max_grid <= 0) return SLX_ERR_UNSUPPORTED;
   const int grid = max_grid;
   const int bytes = fused_layout<BITS>(f, grid);
   if (bytes <= 0 || bytes > kFusedSmemMax) return SLX_ERR_UNSUPPORTED;
@@ -1624,17 +1551,14 @@ static int launch_fused_t(FusedArgs f, cudaStream_t stream) {
 }
 
 int launch_switchglu_fused(const GemvArgs& a, const DownArgs& d, void* bar,
-                           void* split, int bits, cudaStream_t stream,
+                           int bits, cudaStream_t stream,
                            const slx_fill_service* svc,
                            const slx_ep_exchange* ep) {
-  if (a.T != 1 || d.T != 1 || !split) return SLX_ERR_UNSUPPORTED;
+  if (a.T != 1 || d.T != 1) return SLX_ERR_UNSUPPORTED;
   FusedArgs f = {};
   f.a = a;
   f.d = d;
   f.bar = reinterpret_cast<unsigned long long*>(bar);
-  f.split_flag = reinterpret_cast<unsigned*>(split);
-  f.split_y = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(split) +
-                                       split_flag_bytes(d.n_units));
   if (ep) {
     f.ep_on = 1;
     f.ep_rank = ep->rank;
