@@ -845,9 +845,10 @@ __device__ __noinline__ void svc_write_log(const FusedArgs& f, const GemvArgs& a
     L[20 + j] = f.svc_pred_ids ? f.svc_pred_ids[j] : -1;
     L[36 + j] = f.svc_pred_scores ? __float_as_int(f.svc_pred_scores[j]) : 0;
   }
-  __threadfence_system();
-  L[0] = stamp;
-  __threadfence_system();
+  // the stamp last, with release semantics at system scope: a host that
+  // sees it sees the words above (one writer; the host reads in order)
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(f.svc_log), "r"(stamp)
+               : "memory");
 }
 
 // Every thread of every CTA calls this after the CTA agreed that some routed
@@ -1051,12 +1052,12 @@ __device__ __noinline__ void ep_write_rows(const FusedArgs& f, const DownArgs& d
 }
 
 // This CTA's rows are written (every thread's stores are ordered before
-// thread 0's by the preceding barrier): count the CTA on every rank.
+// thread 0's by the preceding barrier, and a release is cumulative over
+// them): count the CTA on every rank.
 SLX_DEV void ep_signal(const FusedArgs& f) {
   if (threadIdx.x != 0) return;
   const int stamp = *f.ep_stamp;
   const int slot = (stamp & 1) * f.ep_layers + f.ep_layer;
-  __threadfence_system();
   for (int r = 0; r < f.ep_nranks; ++r)
     asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(
                      f.ep_count[r] + slot)
