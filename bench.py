@@ -146,7 +146,8 @@ def traffic_from_profile(model: str) -> float | None:
     p = os.path.join(ROOT, "profiles", f"switchglu_decode_{model}.md")
     try:
         for line in open(p):
-            if line.startswith("traffic_bytes_per_launch_pair:"):
+            if line.startswith(("traffic_bytes_per_launch:",
+                                "traffic_bytes_per_launch_pair:")):
                 return float(line.split(":", 1)[1].strip())
     except OSError:
         pass
@@ -331,6 +332,94 @@ def run_prefill(args) -> None:
     if rank == 0:
         print(json.dumps({"metric": "prefill_tflops", "value": res["tflops"],
                           "unit": "TFLOP/s", "n_gpus": 1, **res}), flush=True)
+
+
+def run_glu(args) -> None:
+    """The decode SwitchGLU alone at the 117B shape: 256 2-bit experts
+    (H 2560, I 1024) in a 630 MB slot pool, 48 launches of top-10 with
+    different seeded routing per launch, back to back in a CUDA graph (PDL
+    between them), timed with CUDA events around the graph; checked against
+    the two-launch form on the same inputs first."""
+    import torch
+
+    from streamlx_b200 import _lib as L
+    rank, world, local = dist_env()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    c = PREFILL_SHAPE
+    H, I, E, k, n = c["hidden"], c["inter"], c["experts"], c["top_k"], 48
+    pool, stride = _random_experts(E, H, I, dev, SEED)
+    bank = L.bank_struct(pool, E, H, I, 2, stride)
+    table = torch.arange(E, dtype=torch.int32, device=dev)
+    rng = np.random.default_rng(SEED)
+    ids = torch.as_tensor(np.stack([rng.choice(E, k, replace=False)
+                                    for _ in range(n)]).astype(np.int32),
+                          device=dev).reshape(n, 1, k)
+    sc = rng.random((n, 1, k)).astype(np.float32)
+    sc /= sc.sum(-1, keepdims=True)
+    sc = torch.as_tensor(sc, device=dev)
+    g = torch.Generator(device=dev).manual_seed(SEED)
+    xs = (torch.randn(n, 1, H, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    out = torch.empty(n, 1, H, dtype=torch.bfloat16, device=dev)
+    ref = torch.empty_like(out)
+    scr = torch.zeros(L.switchglu_scratch_bytes(1, k, I), dtype=torch.uint8,
+                      device=dev)
+    st = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def launch_all(dst):
+        for i in range(n):
+            L.switchglu(bank, xs[i], ids[i], dst[i], scr, st, scores=sc[i],
+                        slot_table=table)
+    prev = L.set_switchglu_fused(False)
+    launch_all(ref)
+    L.set_switchglu_fused(True)
+    launch_all(out)
+    torch.cuda.synchronize()
+    if int(st.item()) != 0:
+        raise RuntimeError(f"switchglu status {int(st.item())}")
+    a = out.float().cpu().numpy()
+    b = ref.float().cpu().numpy()
+    rel = float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+    L.set_pdl(True)
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        for _ in range(args.warmup):
+            launch_all(out)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=s):
+            launch_all(out)
+    torch.cuda.synchronize()
+    ts = []
+    e0, e1 = (torch.cuda.Event(enable_timing=True),
+              torch.cuda.Event(enable_timing=True))
+    for _ in range(args.warmup + args.steps):
+        e0.record()
+        gr.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) * 1000.0 / n)
+    L.set_switchglu_fused(prev)
+    us = float(np.median(ts[args.warmup:]))
+    per_launch = k * synth_expert_bytes(H, I) + 2 * 2 * H
+    peak, peak_kind = measured_peak()
+    gbs = per_launch / (us * 1e-6) / 1e9
+    if rank == 0:
+        print(json.dumps({
+            "metric": "switchglu_decode_GBps", "value": round(gbs, 1),
+            "unit": "GB/s", "n_gpus": 1, "launch_us": round(us, 2),
+            "frac": round(gbs / peak, 4), "peak": peak,
+            "peak_kind": peak_kind, "bytes_per_launch": int(per_launch),
+            "launches_per_graph": n, "replays_timed": args.steps,
+            "vs_two_launch_rel_l2": rel,
+            "config": {"workload": "117B-shaped decode SwitchGLU: H 2560, "
+                       "I 1024, 2-bit g64, top-10 of 256 slots (630 MB pool)",
+                       "l2": "inputs larger than L2"}}), flush=True)
+
+
+def synth_expert_bytes(H: int, I: int) -> int:
+    from streamlx_b200 import synth
+    return synth.expert_bytes(H, I, 2, 64)
 
 
 def _random_experts(E, H, I, dev, seed, pool=None, ids=None):
@@ -819,8 +908,9 @@ def main():
     ap.add_argument("--check", action="store_true",
                     help="ep mode: compare with an all-experts computation")
     ap.add_argument("--mode", default="decode",
-                    choices=["decode", "prefill", "ep"],
-                    help="prefill: only the prefill measurement (its own line)")
+                    choices=["decode", "prefill", "ep", "glu"],
+                    help="prefill: only the prefill measurement (its own "
+                         "line); glu: only the decode SwitchGLU kernel")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -830,6 +920,8 @@ def main():
         run_prefill(args)
     elif args.mode == "ep":
         run_ep(args)
+    elif args.mode == "glu":
+        run_glu(args)
     else:
         run_ours(args)
 

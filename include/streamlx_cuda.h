@@ -386,7 +386,8 @@ int slx_router_topk_multi(const slx_router_head* heads, int n_heads,
  * calls on one device share that array, so calls that overlap (two streams,
  * or two host threads) race: order them on one stream.  The first call on
  * each device looks up the array's address (loading the module) and should
- * come before any stream capture. */
+ * come before any stream capture.  The address is kept for the life of the
+ * process: do not use this entry point across a cudaDeviceReset. */
 int slx_router_topk_noalloc(const void* x, const void* ratio,
                             const void* w_gate, const float* bias, int T,
                             int H, int E, int k, int norm_topk,

@@ -10,6 +10,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "../../include/streamlx_cuda.h"
 
 #define SLX_DEV __device__ __forceinline__
@@ -160,6 +162,19 @@ SLX_DEV void pdl_wait_primary() {
 
 // Launch setting of the calling host thread (slx_set_pdl).
 bool pdl_enabled();
+
+// A launcher's one-time per-device value (function attributes and occupancy
+// apply per device context; slots for devices 0..63, 0 = not yet known).
+constexpr int kMaxDevices = 64;
+struct PerDevice {
+  std::atomic<int> v[kMaxDevices];
+  // the slot of the calling thread's current device
+  std::atomic<int>& here() {
+    int d = 0;
+    if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= kMaxDevices) d = 0;
+    return v[d];
+  }
+};
 
 // <<<>>> replacement that adds the PDL attribute when pdl_enabled().
 template <typename... KArgs, typename... Args>

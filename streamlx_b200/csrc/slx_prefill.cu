@@ -746,20 +746,21 @@ SmemPlan plan_smem(int nG) {
   return p;
 }
 
-int g_num_sms_pf = 0;
+PerDevice g_num_sms_pf;
 
 template <int PHASE>
-int launch_phase(PrefillArgs a, int smem, cudaStream_t s) {
-  static int attr_set = 0;
-  if (!attr_set) {
+int launch_phase(PrefillArgs a, int smem, cudaStream_t s, int n_sms) {
+  static PerDevice attr_set;
+  std::atomic<int>& slot = attr_set.here();
+  if (!slot.load(std::memory_order_relaxed)) {
     if (cudaFuncSetAttribute(k_prefill<PHASE>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              227 * 1024) != cudaSuccess)
       return SLX_ERR_CUDA;
-    attr_set = 1;
+    slot.store(1, std::memory_order_relaxed);
   }
   if (a.n_items == 0) return SLX_OK;
-  const int grid = a.n_items < g_num_sms_pf ? a.n_items : g_num_sms_pf;
+  const int grid = a.n_items < n_sms ? a.n_items : n_sms;
   k_prefill<PHASE><<<grid, kThreads, smem, s>>>(a);
   return cudaGetLastError() == cudaSuccess ? SLX_OK : SLX_ERR_CUDA;
 }
@@ -777,12 +778,15 @@ int launch_prefill(const uint8_t* bank, long long slot_stride, int n_slots,
                    int n_blocks, const int32_t* out_row, uint16_t* out,
                    int n_out, uint8_t* scratch, int32_t* status,
                    cudaStream_t s) {
-  if (g_num_sms_pf == 0) {
+  std::atomic<int>& sm_slot = g_num_sms_pf.here();
+  int n_sms = sm_slot.load(std::memory_order_relaxed);
+  if (n_sms == 0) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&g_num_sms_pf, cudaDevAttrMultiProcessorCount,
-                               dev) != cudaSuccess)
+        cudaDeviceGetAttribute(&n_sms, cudaDevAttrMultiProcessorCount,
+                               dev) != cudaSuccess || n_sms <= 0)
       return SLX_ERR_CUDA;
+    sm_slot.store(n_sms, std::memory_order_relaxed);
   }
   const int nG1 = H / 64, nG2 = I / 64;
   if (nG1 > 64 || nG2 > 64 || I % 128 || H % kNW) return SLX_ERR_UNSUPPORTED;
@@ -825,7 +829,7 @@ int launch_prefill(const uint8_t* bank, long long slot_stride, int n_slots,
     p.off_x = sp.off_x; p.off_w = sp.off_w; p.off_stg = sp.off_stg;
     p.off_btab = sp.off_btab;
     if (sp.bytes > 227 * 1024) return SLX_ERR_UNSUPPORTED;
-    const int rc = launch_phase<1>(p, sp.bytes, s);
+    const int rc = launch_phase<1>(p, sp.bytes, s, n_sms);
     if (rc) return rc;
   }
   // phase 2: down projection -> per-pair outputs
@@ -840,7 +844,7 @@ int launch_prefill(const uint8_t* bank, long long slot_stride, int n_slots,
     p.off_x = sp.off_x; p.off_w = sp.off_w; p.off_stg = sp.off_stg;
     p.off_btab = sp.off_btab;
     if (sp.bytes > 227 * 1024) return SLX_ERR_UNSUPPORTED;
-    const int rc = launch_phase<2>(p, sp.bytes, s);
+    const int rc = launch_phase<2>(p, sp.bytes, s, n_sms);
     if (rc) return rc;
   }
   return SLX_OK;

@@ -710,15 +710,19 @@ __global__ void __launch_bounds__(kThreads, 2)
 
 // ------------------------------------------------------------ launchers ---
 
-static int g_num_sms = 0;
+static PerDevice g_num_sms;
 static int num_sms() {
-  if (!g_num_sms) {
+  std::atomic<int>& slot = g_num_sms.here();
+  int n = slot.load(std::memory_order_relaxed);
+  if (!n) {
     int dev = 0;
     cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-    if (g_num_sms <= 0) g_num_sms = 148;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) !=
+            cudaSuccess || n <= 0)
+      n = 148;
+    slot.store(n, std::memory_order_relaxed);
   }
-  return g_num_sms;
+  return n;
 }
 
 // ------------------------------------------------ fused decode SwitchGLU ---
@@ -1509,7 +1513,9 @@ static int fused_layout(FusedArgs& f, int grid) {
 
 template <int BITS>
 static int launch_fused_t(FusedArgs f, cudaStream_t stream) {
-  static int max_grid = -1;
+  static PerDevice grid_of;  // grid + 1 per device (1: cannot run)
+  std::atomic<int>& gslot = grid_of.here();
+  int max_grid = gslot.load(std::memory_order_relaxed) - 1;
   if (max_grid < 0) {
     int per_sm = 0;
     if (cudaFuncSetAttribute(k_switchglu_fused<BITS>,
@@ -1521,6 +1527,7 @@ static int launch_fused_t(FusedArgs f, cudaStream_t stream) {
         cudaSuccess)
       return SLX_ERR_CUDA;
     max_grid = per_sm >= 1 ? num_sms() : 0;
+    gslot.store(max_grid + 1, std::memory_order_relaxed);
   }
   if (max_grid <= 0) return SLX_ERR_UNSUPPORTED;
   const int grid = max_grid;
@@ -1539,12 +1546,13 @@ static int launch_fused_t(FusedArgs f, cudaStream_t stream) {
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  static int pdl_ok = 1;  // cleared if the driver refuses the combination
-  cfg.numAttrs = (pdl_ok && pdl_enabled()) ? 2 : 1;
+  static PerDevice pdl_refused;  // set if the driver refuses the combination
+  std::atomic<int>& pslot = pdl_refused.here();
+  cfg.numAttrs = (!pslot.load(std::memory_order_relaxed) && pdl_enabled()) ? 2 : 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, k_switchglu_fused<BITS>, f);
   if (e != cudaSuccess && cfg.numAttrs == 2) {
     (void)cudaGetLastError();
-    pdl_ok = 0;
+    pslot.store(1, std::memory_order_relaxed);
     cfg.numAttrs = 1;
     e = cudaLaunchKernelEx(&cfg, k_switchglu_fused<BITS>, f);
   }
@@ -1610,15 +1618,16 @@ constexpr int kSmemTarget = 113 * 1024;
 constexpr int kSmemBudget = kSmemTarget;
 constexpr int kSmemMax = 227 * 1024;
 
-// Raise the kernel's dynamic shared-memory limit once per instantiation
-// (one process drives one GPU).
+// Raise the kernel's dynamic shared-memory limit once per instantiation and
+// device.
 template <typename K, int TAG>
 static cudaError_t set_smem(K kern, int bytes) {
-  static int configured = 0;
-  if (bytes <= configured) return cudaSuccess;
+  static PerDevice configured;
+  std::atomic<int>& slot = configured.here();
+  if (bytes <= slot.load(std::memory_order_relaxed)) return cudaSuccess;
   const cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
-  if (e == cudaSuccess) configured = kSmemMax;
+  if (e == cudaSuccess) slot.store(kSmemMax, std::memory_order_relaxed);
   return e;
 }
 

@@ -546,13 +546,14 @@ int launch_router_heads(const RouterArgs* heads, int n_heads,
     W.n_heads = n_heads;
     W.ctas_per_head = (a.E + kWideRows - 1) / kWideRows;
     const int smem = kWideRows * a.H * 2;
-    static bool attr = false;
-    if (!attr) {
+    static PerDevice attr;
+    std::atomic<int>& slot = attr.here();
+    if (!slot.load(std::memory_order_relaxed)) {
       if (cudaFuncSetAttribute(k_router_wide,
                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                kWideRows * kRouterMaxH * 2) != cudaSuccess)
         return SLX_ERR_CUDA;
-      attr = true;
+      slot.store(1, std::memory_order_relaxed);
     }
     return launch_k(k_router_wide, dim3(W.ctas_per_head * n_heads),
                     dim3(kRouterThreads), smem, stream, W) == cudaSuccess

@@ -531,13 +531,14 @@ int launch_attn_decode(const uint16_t* qkv, int T, int nq, int nkv, int hd,
   if (hd != 128 || nq % nkv || nq / nkv > kAttnMaxRep) return SLX_ERR_UNSUPPORTED;
   if (T <= 0) return SLX_OK;
   if (T > 65535 || nkv > 65535) return SLX_ERR_INVALID;
-  static bool configured = false;
-  if (!configured) {
+  static PerDevice configured;
+  std::atomic<int>& slot = configured.here();
+  if (!slot.load(std::memory_order_relaxed)) {
     if (cudaFuncSetAttribute(k_attn_decode,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kAttnSmem) != cudaSuccess)
       return SLX_ERR_CUDA;
-    configured = true;
+    slot.store(1, std::memory_order_relaxed);
   }
   dim3 grid(kAttnCluster, nkv, T);
   const cudaError_t e = launch_k(k_attn_decode, grid, dim3(kAttnThreads),
