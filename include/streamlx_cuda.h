@@ -414,6 +414,17 @@ int slx_qk_norm_rope_cache(void* qkv, int T, int n_q, int n_kv, int head_dim,
 int slx_attn_decode(const void* qkv, int T, int n_q, int n_kv, int head_dim,
                     const void* k_cache, const void* v_cache,
                     const int32_t* pos, int max_len, void* out, void* stream);
+/* One decode token (T = 1): slx_qk_norm_rope_cache and slx_attn_decode in
+ * one launch.  Each cluster normalises and rotates its q heads and its kv
+ * head's key, appends key and value at position pos[0] of the caches and
+ * attends over positions 0..pos[0] (the new row taken from shared memory);
+ * results equal the two-launch form bit for bit.  The trunk of the
+ * synthetic decoders (mlx-lm's model code in the reference). */
+int slx_attn_rope_decode(const void* qkv, int n_q, int n_kv, int head_dim,
+                         const void* q_norm, const void* k_norm, float eps,
+                         const float* inv_freq, const int32_t* pos,
+                         int max_len, void* k_cache, void* v_cache, void* out,
+                         int32_t* status, void* stream);
 int slx_argmax(const void* logits, int T, int V, int32_t* out, void* stream);
 
 /* Read n byte ranges of files: fds[i] from offsets[i], sizes[i] bytes,

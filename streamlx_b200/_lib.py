@@ -33,7 +33,8 @@ EXPORTS = (
     "slx_switchglu_scratch_bytes",
     "slx_switchglu", "slx_qlinear", "slx_dequant_rows",
     "slx_router_scratch_bytes", "slx_router_topk", "slx_add_rmsnorm",
-    "slx_qk_norm_rope_cache", "slx_attn_decode", "slx_argmax",
+    "slx_qk_norm_rope_cache", "slx_attn_decode", "slx_attn_rope_decode",
+    "slx_argmax",
     "slx_copy_many", "slx_router_topk_noalloc", "slx_add_rmsnorm_out",
     "slx_event_record_external", "slx_event_elapsed_many",
     "slx_router_topk_multi", "slx_set_pdl", "slx_pread_many",
@@ -173,6 +174,10 @@ def lib() -> C.CDLL:
         L.slx_qk_norm_rope_cache.argtypes = [vp, i32, i32, i32, i32, vp, vp,
                                              C.c_float, vp, vp, i32, vp, vp,
                                              vp, vp]
+        L.slx_attn_rope_decode.restype = i32
+        L.slx_attn_rope_decode.argtypes = [vp, i32, i32, i32, vp, vp,
+                                           C.c_float, vp, vp, i32, vp, vp,
+                                           vp, vp, vp]
         L.slx_attn_decode.restype = i32
         L.slx_attn_decode.argtypes = [vp, i32, i32, i32, i32, vp, vp, vp, i32,
                                       vp, vp]
@@ -523,6 +528,18 @@ def attn_decode(qkv, n_q, n_kv, hd, k_cache, v_cache, pos, out,
                                pos.data_ptr(), k_cache.shape[0], out.data_ptr(),
                                stream_ptr(stream))
     _check("slx_attn_decode", rc)
+    _count(1)
+
+
+def attn_rope_decode(qkv, n_q, n_kv, hd, q_norm, k_norm, eps, inv_freq, pos,
+                     k_cache, v_cache, out, status, stream=None) -> None:
+    """One decode token: q/k norm + RoPE + cache append + attention."""
+    rc = lib().slx_attn_rope_decode(
+        qkv.data_ptr(), n_q, n_kv, hd, q_norm.data_ptr(), k_norm.data_ptr(),
+        eps, inv_freq.data_ptr(), pos.data_ptr(), k_cache.shape[0],
+        k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(),
+        status.data_ptr(), stream_ptr(stream))
+    _check("slx_attn_rope_decode", rc)
     _count(1)
 
 

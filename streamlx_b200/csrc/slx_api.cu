@@ -742,6 +742,26 @@ int slx_attn_decode(const void* qkv, int T, int n_q, int n_kv, int head_dim,
   return rc ? cuda_check(rc, "slx_attn_decode") : SLX_OK;
 }
 
+int slx_attn_rope_decode(const void* qkv, int n_q, int n_kv, int head_dim,
+                         const void* q_norm, const void* k_norm, float eps,
+                         const float* inv_freq, const int32_t* pos,
+                         int max_len, void* k_cache, void* v_cache, void* out,
+                         int32_t* status, void* stream) {
+  g_err.clear();
+  if (!qkv || !q_norm || !k_norm || !inv_freq || !pos || !k_cache ||
+      !v_cache || !out)
+    return fail(SLX_ERR_INVALID, "attn_rope: NULL");
+  if (n_q < 1 || n_kv < 1 || n_q % n_kv) return fail(SLX_ERR_INVALID, "heads");
+  if (!aligned16(k_cache) || !aligned16(v_cache) || !aligned16(qkv))
+    return fail(SLX_ERR_INVALID, "attn_rope: qkv / caches not 16-byte aligned");
+  const int rc = slx::launch_attn_rope_decode(
+      (const uint16_t*)qkv, n_q, n_kv, head_dim, (const uint16_t*)q_norm,
+      (const uint16_t*)k_norm, eps, inv_freq, pos, max_len,
+      (uint16_t*)k_cache, (uint16_t*)v_cache, (uint16_t*)out, status,
+      reinterpret_cast<cudaStream_t>(stream));
+  return rc ? cuda_check(rc, "slx_attn_rope_decode") : SLX_OK;
+}
+
 int slx_argmax(const void* logits, int T, int V, int32_t* out, void* stream) {
   g_err.clear();
   if (!logits || !out || V < 1) return fail(SLX_ERR_INVALID, "argmax");

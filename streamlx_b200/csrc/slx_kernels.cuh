@@ -119,6 +119,11 @@ int launch_attn_decode(const uint16_t* qkv, int T, int nq, int nkv, int hd,
                        const uint16_t* kc, const uint16_t* vc,
                        const int32_t* pos, int max_len, uint16_t* out,
                        cudaStream_t s);
+int launch_attn_rope_decode(const uint16_t* qkv, int nq, int nkv, int hd,
+                            const uint16_t* qn, const uint16_t* kn, float eps,
+                            const float* inv_freq, const int32_t* pos,
+                            int max_len, uint16_t* kc, uint16_t* vc,
+                            uint16_t* out, int32_t* status, cudaStream_t s);
 int launch_argmax(const uint16_t* logits, int T, int V, int32_t* out,
                   cudaStream_t s);
 size_t prefill_scratch_bytes(int n_blocks, int H, int I);

@@ -36,6 +36,12 @@ __global__ void __launch_bounds__(kNormThreads) k_add_rmsnorm(
     float eps, uint16_t* h_out, uint16_t* y) {
   __shared__ float red[32];
   pdl_launch_dependents();
+  uint4 wv[kNormMaxChunks];  // immutable norm weights, in flight before the wait
+#pragma unroll
+  for (int j = 0; j < kNormMaxChunks; ++j) {
+    const int c = (j * kNormThreads + threadIdx.x) * 8;
+    wv[j] = c < H ? *reinterpret_cast<const uint4*>(w + c) : make_uint4(0, 0, 0, 0);
+  }
   pdl_wait_primary();
   const int t = blockIdx.x;
   const uint16_t* hr = h_in + (size_t)t * H;
@@ -74,9 +80,8 @@ __global__ void __launch_bounds__(kNormThreads) k_add_rmsnorm(
   for (int j = 0; j < kNormMaxChunks; ++j) {
     const int c = (j * kNormThreads + threadIdx.x) * 8;
     if (c >= H) break;
-    const uint4 wv = *reinterpret_cast<const uint4*>(w + c);
     const uint32_t* pa = reinterpret_cast<const uint32_t*>(&v[j]);
-    const uint32_t* pw = reinterpret_cast<const uint32_t*>(&wv);
+    const uint32_t* pw = reinterpret_cast<const uint32_t*>(&wv[j]);
     uint4 o;
     uint32_t* po = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
@@ -94,15 +99,25 @@ __global__ void __launch_bounds__(kNormThreads) k_add_rmsnorm(
 // delta = bf16(sum_j fma(score_j, row_j) (+ shared row)) -- the same fp32
 // operations in the same unit order as the single-GPU fused kernel -- and
 // the residual add + RMSNorm of k_add_rmsnorm on it (same arithmetic).
+constexpr int kEpMaxK = SLX_FILL_MAX_K;  // routed units per token
+
 __global__ void __launch_bounds__(kNormThreads) k_ep_combine_rmsnorm(
     const slx_ep_exchange ep, const float* scores, int k, int H,
     int has_shared, const uint16_t* h_in, const uint16_t* w, float eps,
     uint16_t* h_out, uint16_t* y, int32_t* status) {
   __shared__ float red[32];
   __shared__ int s_ok;
+  __shared__ float s_sc[kEpMaxK];
   pdl_launch_dependents();
+  uint4 wv[kNormMaxChunks];  // immutable norm weights, in flight before the wait
+#pragma unroll
+  for (int j = 0; j < kNormMaxChunks; ++j) {
+    const int c = (j * kNormThreads + threadIdx.x) * 8;
+    wv[j] = c < H ? *reinterpret_cast<const uint4*>(w + c) : make_uint4(0, 0, 0, 0);
+  }
   pdl_wait_primary();
   const int stamp = *ep.stamp;
+  if (threadIdx.x < k && threadIdx.x < kEpMaxK) s_sc[threadIdx.x] = scores[threadIdx.x];
   if (threadIdx.x == 0) {
     s_ok = 1;
     if (ep.grid > 0) {
@@ -139,11 +154,18 @@ __global__ void __launch_bounds__(kNormThreads) k_ep_combine_rmsnorm(
     if (c >= H) break;
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     if (s_ok) {
-      for (int u = 0; u < k; ++u) {
-        const float sc = scores[u];
-        const uint4 r = __ldcg(reinterpret_cast<const uint4*>(
-            blk + (size_t)u * H + c));
-        const uint32_t rw[4] = {r.x, r.y, r.z, r.w};
+      // every unit's row first (one round trip), then the combine in unit
+      // order
+      uint4 rows[kEpMaxK];
+#pragma unroll
+      for (int u = 0; u < kEpMaxK; ++u)
+        if (u < k)
+          rows[u] = __ldcg(reinterpret_cast<const uint4*>(blk + (size_t)u * H + c));
+#pragma unroll
+      for (int u = 0; u < kEpMaxK; ++u) {
+        if (u >= k) break;
+        const float sc = s_sc[u];
+        const uint32_t rw[4] = {rows[u].x, rows[u].y, rows[u].z, rows[u].w};
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           acc[2 * q] = fmaf(sc, bf16_lo(rw[q]), acc[2 * q]);
@@ -184,9 +206,8 @@ __global__ void __launch_bounds__(kNormThreads) k_ep_combine_rmsnorm(
   for (int j = 0; j < kNormMaxChunks; ++j) {
     const int c = (j * kNormThreads + threadIdx.x) * 8;
     if (c >= H) break;
-    const uint4 wv = *reinterpret_cast<const uint4*>(w + c);
     const uint32_t* pa = reinterpret_cast<const uint32_t*>(&v[j]);
-    const uint32_t* pw = reinterpret_cast<const uint32_t*>(&wv);
+    const uint32_t* pw = reinterpret_cast<const uint32_t*>(&wv[j]);
     uint4 o;
     uint32_t* po = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
@@ -204,7 +225,8 @@ int launch_ep_combine_rmsnorm(const slx_ep_exchange& ep, const float* scores,
                               const uint16_t* h_in, const uint16_t* w,
                               float eps, uint16_t* h_out, uint16_t* y,
                               int32_t* status, cudaStream_t s) {
-  if (H % 8 || H > 8 * kNormThreads * kNormMaxChunks) return SLX_ERR_UNSUPPORTED;
+  if (H % 8 || H > 8 * kNormThreads * kNormMaxChunks || k < 1 || k > kEpMaxK)
+    return SLX_ERR_UNSUPPORTED;
   return launch_k(k_ep_combine_rmsnorm, dim3(1), dim3(kNormThreads), 0, s, ep,
                   scores, k, H, has_shared, h_in, w, eps, h_out, y, status) ==
                  cudaSuccess ? SLX_OK : SLX_ERR_CUDA;
@@ -280,11 +302,54 @@ constexpr int kAttnSmem = 2 * kAttnChunk * 128 * 2 + kAttnMaxRep * 128 * 4 +
                           kAttnMaxRep * kAttnChunk * 4 +
                           kAttnCluster * kAttnMaxRep * kAttnPart * 4;
 
+// One head vector of the token (128 bf16 at v) through the q/k RMSNorm and
+// rotate-half RoPE by one warp, with the arithmetic and summation order of
+// k_qk_rope_cache (lane l holds pairs l and l + 32 of the 64, each half of
+// the sum reduced as one 32-thread block would): rotated values (bf16) at
+// dst[i] and dst[i + 64].
+SLX_DEV void rope_head(const uint16_t* v, const uint16_t* nw, float eps, int p,
+                       const float* inv_freq, uint16_t* dst, int lane) {
+  float a[2], b[2], s2[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int i = lane + 32 * h;
+    a[h] = bf16_to_f32(v[i]);
+    b[h] = bf16_to_f32(v[i + 64]);
+    float x = a[h] * a[h] + b[h] * b[h];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    s2[h] = x;
+  }
+  const float inv = rsqrtf((s2[0] + s2[1]) / 128.f + eps);
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int i = lane + 32 * h;
+    const float an = round_bf16(a[h] * inv * bf16_to_f32(nw[i]));
+    const float bn = round_bf16(b[h] * inv * bf16_to_f32(nw[i + 64]));
+    const float ang = (float)p * inv_freq[i];
+    float sn, cs;
+    sincosf(ang, &sn, &cs);
+    dst[i] = f32_to_bf16(an * cs - bn * sn);
+    dst[i + 64] = f32_to_bf16(an * sn + bn * cs);
+  }
+}
+
+struct AttnRope {  // ROPE form: the token's q/k norm, RoPE and cache append
+  const uint16_t* qn;
+  const uint16_t* kn;
+  float eps;
+  const float* inv_freq;
+  uint16_t* kcache;
+  uint16_t* vcache;
+  int32_t* status;
+};
+
+template <bool ROPE>
 __global__ void __cluster_dims__(kAttnCluster, 1, 1)
     __launch_bounds__(kAttnThreads) k_attn_decode(
         const uint16_t* qkv, int nq, int nkv, int hd, const uint16_t* kcache,
         const uint16_t* vcache, const int32_t* pos, int max_len, float scale,
-        uint16_t* out) {
+        uint16_t* out, const AttnRope R) {
   namespace cg = cooperative_groups;
   extern __shared__ __align__(16) uint8_t attn_smem[];
   uint16_t* Ks = reinterpret_cast<uint16_t*>(attn_smem);
@@ -304,8 +369,42 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1)
   const size_t kstride = (size_t)nkv * hd;
   const uint16_t* q = qkv + (size_t)t * (nq + 2 * nkv) * hd +
                       (size_t)hk * rep * hd;
-  for (int i = threadIdx.x; i < rep * 128; i += kAttnThreads)
-    qs[i] = bf16_to_f32(q[i]);
+  // ROPE: the token's own key and value row (position n - 1), computed here
+  // and substituted when its chunk is staged; cluster rank 0 appends them
+  // to the cache for the later steps
+  __shared__ __align__(16) uint16_t knew[128], vnew[128];
+  __shared__ __align__(16) uint16_t qrot[kAttnMaxRep * 128];
+  if constexpr (ROPE) {
+    const uint16_t* base = qkv + (size_t)t * (nq + 2 * nkv) * hd;
+    if (!ok_n) {
+      if (threadIdx.x == 0 && rank == 0) set_status(R.status, SLX_ERR_OUT_OF_RANGE);
+    } else {
+      for (int h = warp; h <= rep; h += kAttnThreads / 32) {
+        if (h < rep)
+          rope_head(q + (size_t)h * hd, R.qn, R.eps, n - 1, R.inv_freq,
+                    qrot + h * 128, lane);
+        else
+          rope_head(base + (size_t)(nq + hk) * hd, R.kn, R.eps, n - 1,
+                    R.inv_freq, knew, lane);
+      }
+      if (threadIdx.x < 128) vnew[threadIdx.x] = base[(size_t)(nq + nkv + hk) * hd + threadIdx.x];
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < rep * 128; i += kAttnThreads)
+      qs[i] = bf16_to_f32(qrot[i]);
+    if (rank == 0 && ok_n && threadIdx.x < 32) {
+      const size_t off = (size_t)(n - 1) * kstride + (size_t)hk * hd;
+      if (threadIdx.x < 16)
+        reinterpret_cast<uint4*>(R.kcache + off)[threadIdx.x] =
+            reinterpret_cast<const uint4*>(knew)[threadIdx.x];
+      else
+        reinterpret_cast<uint4*>(R.vcache + off)[threadIdx.x - 16] =
+            reinterpret_cast<const uint4*>(vnew)[threadIdx.x - 16];
+    }
+  } else {
+    for (int i = threadIdx.x; i < rep * 128; i += kAttnThreads)
+      qs[i] = bf16_to_f32(q[i]);
+  }
   // running state: warp r < rep owns head r's (m, l); thread (d2, rg) owns
   // O of heads rg*2, rg*2+1 at dims 2*d2, 2*d2+1
   float m_run = -INFINITY, l_run = 0.f;
@@ -319,7 +418,10 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1)
     for (int u = threadIdx.x; u < kAttnChunk * 16; u += kAttnThreads) {
       const int r = u >> 4, cu = u & 15;
       uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-      if (r < np) {
+      if (ROPE && c0 + r == n - 1) {
+        kv = reinterpret_cast<const uint4*>(knew)[cu];
+        vv = reinterpret_cast<const uint4*>(vnew)[cu];
+      } else if (r < np) {
         const size_t off = (size_t)(c0 + r) * kstride + (size_t)hk * hd;
         kv = reinterpret_cast<const uint4*>(kcache + off)[cu];
         vv = reinterpret_cast<const uint4*>(vcache + off)[cu];
@@ -534,16 +636,42 @@ int launch_attn_decode(const uint16_t* qkv, int T, int nq, int nkv, int hd,
   static PerDevice configured;
   std::atomic<int>& slot = configured.here();
   if (!slot.load(std::memory_order_relaxed)) {
-    if (cudaFuncSetAttribute(k_attn_decode,
+    if (cudaFuncSetAttribute(k_attn_decode<false>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kAttnSmem) != cudaSuccess)
       return SLX_ERR_CUDA;
     slot.store(1, std::memory_order_relaxed);
   }
   dim3 grid(kAttnCluster, nkv, T);
-  const cudaError_t e = launch_k(k_attn_decode, grid, dim3(kAttnThreads),
+  const AttnRope R = {};
+  const cudaError_t e = launch_k(k_attn_decode<false>, grid, dim3(kAttnThreads),
                                  (size_t)kAttnSmem, s, qkv, nq, nkv, hd, kc, vc,
-                                 pos, max_len, 1.0f / sqrtf((float)hd), out);
+                                 pos, max_len, 1.0f / sqrtf((float)hd), out, R);
+  return e == cudaSuccess ? SLX_OK : SLX_ERR_CUDA;
+}
+
+int launch_attn_rope_decode(const uint16_t* qkv, int nq, int nkv, int hd,
+                            const uint16_t* qn, const uint16_t* kn, float eps,
+                            const float* inv_freq, const int32_t* pos,
+                            int max_len, uint16_t* kc, uint16_t* vc,
+                            uint16_t* out, int32_t* status, cudaStream_t s) {
+  if (hd != 128 || nq % nkv || nq / nkv > kAttnMaxRep) return SLX_ERR_UNSUPPORTED;
+  if (nkv > 65535) return SLX_ERR_INVALID;
+  static PerDevice configured;
+  std::atomic<int>& slot = configured.here();
+  if (!slot.load(std::memory_order_relaxed)) {
+    if (cudaFuncSetAttribute(k_attn_decode<true>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kAttnSmem) != cudaSuccess)
+      return SLX_ERR_CUDA;
+    slot.store(1, std::memory_order_relaxed);
+  }
+  dim3 grid(kAttnCluster, nkv, 1);
+  const AttnRope R = {qn, kn, eps, inv_freq, kc, vc, status};
+  const cudaError_t e = launch_k(k_attn_decode<true>, grid, dim3(kAttnThreads),
+                                 (size_t)kAttnSmem, s, qkv, nq, nkv, hd,
+                                 (const uint16_t*)kc, (const uint16_t*)vc, pos,
+                                 max_len, 1.0f / sqrtf((float)hd), out, R);
   return e == cudaSuccess ? SLX_OK : SLX_ERR_CUDA;
 }
 

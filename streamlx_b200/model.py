@@ -271,14 +271,11 @@ class SynthDecoder:
             L.add_rmsnorm(self.h, delta, layer.w_in, cfg.rms_eps, self.x)
             L.qlinear(layer.w_qkv, layer.n_qkv, cfg.hidden, cfg.trunk_bits,
                       self.x, self.qkv, self.status)
-            L.qk_norm_rope_cache(self.qkv, cfg.heads, cfg.kv_heads,
-                                 cfg.head_dim, layer.q_norm, layer.k_norm,
-                                 cfg.rms_eps, self.inv_freq, self.pos,
-                                 self.k_cache[i], self.v_cache[i],
-                                 self.status)
-            L.attn_decode(self.qkv, cfg.heads, cfg.kv_heads, cfg.head_dim,
-                          self.k_cache[i], self.v_cache[i], self.pos,
-                          self.att)
+            L.attn_rope_decode(self.qkv, cfg.heads, cfg.kv_heads,
+                               cfg.head_dim, layer.q_norm, layer.k_norm,
+                               cfg.rms_eps, self.inv_freq, self.pos,
+                               self.k_cache[i], self.v_cache[i], self.att,
+                               self.status)
             L.qlinear(layer.w_o, cfg.hidden, cfg.heads * cfg.head_dim,
                       cfg.trunk_bits, self.att, self.o, self.status)
             L.add_rmsnorm(self.h, self.o, layer.post_attention_layernorm,
@@ -404,13 +401,10 @@ class SynthDecoder:
                               self.g_s[i], self.x)
         L.qlinear(la.w_qkv, la.n_qkv, H, bits, self.x, self.qkv,
                   self.g_status)
-        L.qk_norm_rope_cache(self.qkv, cfg.heads, cfg.kv_heads, cfg.head_dim,
-                             la.q_norm, la.k_norm, eps, self.inv_freq,
-                             self.g_ctrl[0:1], self.k_cache[i],
-                             self.v_cache[i], self.g_status)
-        L.attn_decode(self.qkv, cfg.heads, cfg.kv_heads, cfg.head_dim,
-                      self.k_cache[i], self.v_cache[i], self.g_ctrl[0:1],
-                      self.att)
+        L.attn_rope_decode(self.qkv, cfg.heads, cfg.kv_heads, cfg.head_dim,
+                           la.q_norm, la.k_norm, eps, self.inv_freq,
+                           self.g_ctrl[0:1], self.k_cache[i], self.v_cache[i],
+                           self.att, self.g_status)
         L.qlinear(la.w_o, H, cfg.heads * cfg.head_dim, bits, self.att,
                   self.o, self.g_status)
         xm = self.g_xm[i]

@@ -358,6 +358,43 @@ def test_trunk_kernels(dev):
     assert out.cpu().tolist() == [OT.argmax_first(lg[0]), 77]
 
 
+@pytest.mark.parametrize("nq,nkv", [(16, 2), (24, 4)])
+def test_attn_rope_one_launch_equals_two(dev, nq, nkv):
+    """slx_attn_rope_decode (q/k norm + RoPE + cache append + attention in
+    one launch) against slx_qk_norm_rope_cache + slx_attn_decode: the same
+    bits in the output and in both caches, over 70 positions (two chunks of
+    the attention's 64-position split)."""
+    rng = np.random.default_rng(11)
+    hd, maxlen, eps = 128, 96, 1e-6
+    inv = torch.from_numpy(OT.rope_inv_freq(hd, 1e6)).to(dev)
+    qn = bf16_tensor(A.bf16_round((1 + 0.05 * rng.standard_normal(hd))
+                                  .astype(np.float32)), dev)
+    kn = bf16_tensor(A.bf16_round((1 + 0.05 * rng.standard_normal(hd))
+                                  .astype(np.float32)), dev)
+    caches = [(torch.zeros(maxlen, nkv, hd, dtype=torch.bfloat16, device=dev),
+               torch.zeros(maxlen, nkv, hd, dtype=torch.bfloat16, device=dev))
+              for _ in range(2)]
+    st = _status(dev)
+    for p in range(70):
+        qkv = bf16_tensor(A.bf16_round(
+            rng.standard_normal((1, (nq + 2 * nkv) * hd)).astype(np.float32)),
+            dev)
+        pos = torch.tensor([p], dtype=torch.int32, device=dev)
+        a1 = torch.empty(1, nq * hd, dtype=torch.bfloat16, device=dev)
+        a2 = torch.empty_like(a1)
+        q2 = qkv.clone()
+        L.qk_norm_rope_cache(q2, nq, nkv, hd, qn, kn, eps, inv, pos,
+                             caches[0][0], caches[0][1], st)
+        L.attn_decode(q2, nq, nkv, hd, caches[0][0], caches[0][1], pos, a1)
+        L.attn_rope_decode(qkv, nq, nkv, hd, qn, kn, eps, inv, pos,
+                           caches[1][0], caches[1][1], a2, st)
+        torch.cuda.synchronize()
+        assert torch.equal(a1.view(torch.int16), a2.view(torch.int16)), p
+    assert st.item() == 0
+    for c0, c1 in zip(*caches):
+        assert torch.equal(c0.view(torch.int16), c1.view(torch.int16))
+
+
 def test_router_two_heads_one_launch(dev):
     """Router + next-layer predictor in one launch equal two single calls."""
     T, H, E, k = 3, 2048, 256, 8
