@@ -375,6 +375,17 @@ int slx_router_topk_multi(const slx_router_head* heads, int n_heads,
                           const void* x, int T, int H, int E, int k,
                           int norm_topk, int32_t* status, void* stream);
 
+/* One decode token: the residual add + RMSNorm that produces the router's
+ * input (h_out = h_in + delta, x_out = RMSNorm(h_out) * norm_weight, as
+ * slx_add_rmsnorm_out computes them, bit for bit) and the 1-2 router heads
+ * on x_out, in one launch.  h_out may not alias h_in.  The router's input
+ * norm is mlx-lm's (the reference's MoE block sits after it). */
+int slx_router_topk_multi_norm(const slx_router_head* heads, int n_heads,
+                               const void* h_in, const void* delta,
+                               const void* norm_weight, float eps,
+                               void* h_out, void* x_out, int H, int E, int k,
+                               int norm_topk, int32_t* status, void* stream);
+
 /* Router GEMV + softmax + top-k exactly as slx_router_topk, for callers
  * that hold no device allocator: a host binding that reaches the library
  * only through this C ABI (ctypes, cgo, JNI) and would otherwise have to

@@ -34,6 +34,7 @@ EXPORTS = (
     "slx_switchglu", "slx_qlinear", "slx_dequant_rows",
     "slx_router_scratch_bytes", "slx_router_topk", "slx_add_rmsnorm",
     "slx_qk_norm_rope_cache", "slx_attn_decode", "slx_attn_rope_decode",
+    "slx_router_topk_multi_norm",
     "slx_argmax",
     "slx_copy_many", "slx_router_topk_noalloc", "slx_add_rmsnorm_out",
     "slx_event_record_external", "slx_event_elapsed_many",
@@ -157,6 +158,10 @@ def lib() -> C.CDLL:
         L.slx_router_topk_multi.argtypes = [C.POINTER(slx_router_head), i32,
                                             vp, i32, i32, i32, i32, i32, vp,
                                             vp]
+        L.slx_router_topk_multi_norm.restype = i32
+        L.slx_router_topk_multi_norm.argtypes = [
+            C.POINTER(slx_router_head), i32, vp, vp, vp, C.c_float, vp, vp,
+            i32, i32, i32, i32, vp, vp]
         L.slx_router_topk_noalloc.restype = i32
         L.slx_router_topk_noalloc.argtypes = [vp, vp, vp, vp, i32, i32, i32,
                                               i32, i32, vp, vp, vp, vp, vp, vp]
@@ -471,6 +476,21 @@ def router_topk_multi(x: torch.Tensor, heads: list, E: int, k: int,
                                      k, 1 if norm_topk else 0,
                                      status.data_ptr(), stream_ptr(stream))
     _check("slx_router_topk_multi", rc)
+    _count(1)
+
+
+def router_topk_multi_norm(heads: list, h_in, delta, norm_weight, eps: float,
+                           h_out, x_out, E: int, k: int, norm_topk: bool,
+                           status: torch.Tensor, stream=None) -> None:
+    """One decode token: h_out = h_in + delta, x_out = RMSNorm(h_out) * w,
+    and 1-2 router heads on x_out, in one launch."""
+    H = h_in.shape[-1]
+    arr = (slx_router_head * len(heads))(*heads)
+    rc = lib().slx_router_topk_multi_norm(
+        arr, len(heads), h_in.data_ptr(), ptr(delta), norm_weight.data_ptr(),
+        eps, h_out.data_ptr(), x_out.data_ptr(), H, E, k,
+        1 if norm_topk else 0, status.data_ptr(), stream_ptr(stream))
+    _check("slx_router_topk_multi_norm", rc)
     _count(1)
 
 

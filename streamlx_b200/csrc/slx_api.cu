@@ -604,10 +604,43 @@ int slx_router_topk(const void* x, const void* ratio, const void* w_gate,
   return rc ? cuda_check(rc, "slx_router_topk") : SLX_OK;
 }
 
+static int router_multi_impl(const slx_router_head* heads, int n_heads,
+                             const void* x, int T, int H, int E, int k,
+                             int norm_topk, int32_t* status, void* stream,
+                             const slx::RouterNorm* norm);
+
 int slx_router_topk_multi(const slx_router_head* heads, int n_heads,
                           const void* x, int T, int H, int E, int k,
                           int norm_topk, int32_t* status, void* stream) {
   g_err.clear();
+  return router_multi_impl(heads, n_heads, x, T, H, E, k, norm_topk, status,
+                           stream, nullptr);
+}
+
+int slx_router_topk_multi_norm(const slx_router_head* heads, int n_heads,
+                               const void* h_in, const void* delta,
+                               const void* norm_weight, float eps,
+                               void* h_out, void* x_out, int H, int E, int k,
+                               int norm_topk, int32_t* status, void* stream) {
+  g_err.clear();
+  if (!h_in || !norm_weight || !h_out || !x_out)
+    return fail(SLX_ERR_INVALID, "router_multi_norm: NULL pointer");
+  if (!aligned16(h_in) || !aligned16(norm_weight) || !aligned16(h_out) ||
+      !aligned16(x_out) || (delta && !aligned16(delta)))
+    return fail(SLX_ERR_INVALID, "router_multi_norm: operands not 16-byte aligned");
+  if (h_out == h_in)
+    return fail(SLX_ERR_INVALID, "router_multi_norm: h_out may not alias h_in");
+  const slx::RouterNorm nm = {(const uint16_t*)h_in, (const uint16_t*)delta,
+                              (const uint16_t*)norm_weight, eps,
+                              (uint16_t*)h_out, (uint16_t*)x_out};
+  return router_multi_impl(heads, n_heads, x_out, 1, H, E, k, norm_topk,
+                           status, stream, &nm);
+}
+
+static int router_multi_impl(const slx_router_head* heads, int n_heads,
+                             const void* x, int T, int H, int E, int k,
+                             int norm_topk, int32_t* status, void* stream,
+                             const slx::RouterNorm* norm) {
   if (!heads || n_heads < 1 || n_heads > 2)
     return fail(SLX_ERR_INVALID, "router_multi: 1 or 2 heads");
   if (!x || !aligned16(x))
@@ -654,8 +687,10 @@ int slx_router_topk_multi(const slx_router_head* heads, int n_heads,
         router_bound_bytes(T, E));
     a[i].status = status;
   }
-  const int rc = slx::launch_router_heads(a, n_heads,
-                                          reinterpret_cast<cudaStream_t>(stream));
+  const int rc = slx::launch_router_heads(
+      a, n_heads, reinterpret_cast<cudaStream_t>(stream), norm);
+  if (rc == SLX_ERR_UNSUPPORTED && norm)
+    return fail(rc, "router_multi_norm: one token, H <= 8192, H %% 32 == 0");
   return rc ? cuda_check(rc, "slx_router_topk_multi") : SLX_OK;
 }
 

@@ -97,8 +97,18 @@ int launch_dequant_rows(const uint32_t* w, const uint16_t* s, const uint16_t* b,
                         int nrows, int n_src_rows, void* out, int out_bf16,
                         int32_t* status, cudaStream_t stream);
 int launch_router(const RouterArgs& a, cudaStream_t stream);
+// The residual add + RMSNorm that produces a one-token router's input.
+struct RouterNorm {
+  const uint16_t* h_in;   // [H]
+  const uint16_t* delta;  // [H] or null
+  const uint16_t* w;      // [H] norm weight
+  float eps;
+  uint16_t* h_out;        // [H] h_in + delta (may not alias h_in)
+  uint16_t* y;            // [H] the normalised x
+};
+
 int launch_router_heads(const RouterArgs* heads, int n_heads,
-                        cudaStream_t stream);
+                        cudaStream_t stream, const RouterNorm* norm = nullptr);
 int launch_pack_experts(const void* const* gw, const void* const* gs,
                         const void* const* gb, const void* const* uw,
                         const void* const* us, const void* const* ub,

@@ -426,7 +426,91 @@ struct WideLaunch {
   RouterArgs h[2];
   float* bound[2];  // [E] per head
   int n_heads, ctas_per_head;
+  RouterNorm norm;  // norm.w != null: x = RMSNorm(h_in + delta) first
 };
+
+// The token's x = bf16(bf16(h_in + delta) * rsqrt(mean + eps) * w) into
+// s_x (times the ratio, rounded, when `ratio`), with the arithmetic and the
+// summation order of k_add_rmsnorm (256 threads of 8-value chunks, chunk c
+// of thread t = (j * 256 + t) * 8, each warp's sum by butterfly, the warps'
+// sums added in order); CTA 0 also stores h_in + delta and x.  All threads
+// of the CTA call this.
+constexpr int kNormT = 256, kNormJ = 4;
+SLX_DEV void norm_stage(const RouterNorm& nm, int H, const uint16_t* ratio,
+                        float* s_x, float* red, bool store) {
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  uint4 v[kNormJ];
+  float ss = 0.f;
+  if (t < kNormT) {
+#pragma unroll
+    for (int j = 0; j < kNormJ; ++j) {
+      const int c = (j * kNormT + t) * 8;
+      if (c >= H) break;
+      uint4 a = *reinterpret_cast<const uint4*>(nm.h_in + c);
+      if (nm.delta) {
+        const uint4 b = *reinterpret_cast<const uint4*>(nm.delta + c);
+        uint32_t* pa = reinterpret_cast<uint32_t*>(&a);
+        const uint32_t* pb = reinterpret_cast<const uint32_t*>(&b);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float lo = round_bf16(bf16_lo(pa[q]) + bf16_lo(pb[q]));
+          const float hi = round_bf16(bf16_hi(pa[q]) + bf16_hi(pb[q]));
+          pa[q] = (uint32_t)f32_to_bf16(lo) | ((uint32_t)f32_to_bf16(hi) << 16);
+        }
+      }
+      if (store) *reinterpret_cast<uint4*>(nm.h_out + c) = a;
+      const uint32_t* pa = reinterpret_cast<const uint32_t*>(&a);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float lo = bf16_lo(pa[q]), hi = bf16_hi(pa[q]);
+        ss += lo * lo + hi * hi;
+      }
+      v[j] = a;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  __syncthreads();
+  if (lane == 0 && warp < kNormT / 32) red[warp] = ss;
+  __syncthreads();
+  float tot = red[0];
+  for (int w = 1; w < kNormT / 32; ++w) tot += red[w];
+  const float inv = rsqrtf(tot / (float)H + nm.eps);
+  if (t < kNormT) {
+#pragma unroll
+    for (int j = 0; j < kNormJ; ++j) {
+      const int c = (j * kNormT + t) * 8;
+      if (c >= H) break;
+      const uint4 wv = *reinterpret_cast<const uint4*>(nm.w + c);
+      const uint32_t* pa = reinterpret_cast<const uint32_t*>(&v[j]);
+      const uint32_t* pw = reinterpret_cast<const uint32_t*>(&wv);
+      uint4 o;
+      uint32_t* po = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint16_t lo = f32_to_bf16(bf16_lo(pa[q]) * inv * bf16_lo(pw[q]));
+        const uint16_t hi = f32_to_bf16(bf16_hi(pa[q]) * inv * bf16_hi(pw[q]));
+        po[q] = (uint32_t)lo | ((uint32_t)hi << 16);
+      }
+      if (store) *reinterpret_cast<uint4*>(nm.y + c) = o;
+      uint32_t rw[4] = {0, 0, 0, 0};
+      if (ratio) {
+        const uint4 rv = *reinterpret_cast<const uint4*>(ratio + c);
+        rw[0] = rv.x; rw[1] = rv.y; rw[2] = rv.z; rw[3] = rv.w;
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float x0 = bf16_lo(po[q]), x1 = bf16_hi(po[q]);
+        if (ratio) {
+          x0 = round_bf16(x0 * bf16_lo(rw[q]));
+          x1 = round_bf16(x1 * bf16_hi(rw[q]));
+        }
+        s_x[c + 2 * q] = x0;
+        s_x[c + 2 * q + 1] = x1;
+      }
+    }
+  }
+}
 
 __global__ void __launch_bounds__(kRouterThreads, 1)
     k_router_wide(const __grid_constant__ WideLaunch L) {
@@ -458,7 +542,11 @@ __global__ void __launch_bounds__(kRouterThreads, 1)
   }
   pdl_launch_dependents();
   pdl_wait_primary();
+  __shared__ float s_red[32];
   const uint16_t* xr = a.x;  // one token
+  if (L.norm.w) {
+    norm_stage(L.norm, H, a.ratio, s_x, s_red, blockIdx.x == 0);
+  } else {
   for (int c = threadIdx.x * 8; c < H; c += kRouterThreads * 8) {
     const uint4 xv = *reinterpret_cast<const uint4*>(xr + c);
     const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
@@ -477,6 +565,7 @@ __global__ void __launch_bounds__(kRouterThreads, 1)
       s_x[c + 2 * q] = x0;
       s_x[c + 2 * q + 1] = x1;
     }
+  }
   }
   __syncthreads();
   const bool ok = mbar_wait(&s_bar, 0, a.status);
@@ -523,7 +612,7 @@ __global__ void __launch_bounds__(kRouterThreads, 1)
 }
 
 int launch_router_heads(const RouterArgs* heads, int n_heads,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, const RouterNorm* norm) {
   if (n_heads < 1 || n_heads > 2) return SLX_ERR_INVALID;
   const RouterArgs& a = heads[0];
   for (int i = 0; i < n_heads; ++i) {
@@ -536,9 +625,12 @@ int launch_router_heads(const RouterArgs* heads, int n_heads,
   }
   if (a.T <= 0) return SLX_OK;
   if (a.T > 65535) return SLX_ERR_INVALID;
-  if (a.T == 1 && a.H % (8 * kWideSplit) == 0 && heads[0].bound &&
-      (n_heads < 2 || heads[1].bound)) {
+  const bool wide = a.T == 1 && a.H % (8 * kWideSplit) == 0 && heads[0].bound &&
+                    (n_heads < 2 || heads[1].bound);
+  if (norm && (!wide || a.H > 8 * kNormT * kNormJ)) return SLX_ERR_UNSUPPORTED;
+  if (wide) {
     WideLaunch W = {};
+    if (norm) W.norm = *norm;
     W.h[0] = heads[0];
     W.h[1] = n_heads > 1 ? heads[1] : heads[0];
     W.bound[0] = heads[0].bound;
@@ -569,7 +661,7 @@ int launch_router_heads(const RouterArgs* heads, int n_heads,
 }
 
 int launch_router(const RouterArgs& a, cudaStream_t stream) {
-  return launch_router_heads(&a, 1, stream);
+  return launch_router_heads(&a, 1, stream, nullptr);
 }
 
 }  // namespace slx

@@ -408,8 +408,6 @@ class SynthDecoder:
         L.qlinear(la.w_o, H, cfg.heads * cfg.head_dim, bits, self.att,
                   self.o, self.g_status)
         xm = self.g_xm[i]
-        L.add_rmsnorm_out(self.g_s[i], self.o, la.post_attention_layernorm,
-                          eps, self.g_m[i], xm)
         heads = [L.router_head(blk.w_gate, blk.bias, self.g_ids[i],
                                self.g_scores[i], blk.scratch,
                                force=self.g_ctrl[1 + i:2 + i],
@@ -421,8 +419,12 @@ class SynthDecoder:
             heads.append(L.router_head(nxt.w_gate, nxt.bias,
                                        self.g_pf_ids[i], self.g_pf_scores[i],
                                        blk.pf_scratch, ratio=ratio))
-        L.router_topk_multi(xm, heads, cfg.n_experts, k, cfg.norm_topk_prob,
-                            self.g_status)
+        # the post-attention residual add + RMSNorm runs inside the router
+        # launch (g_m[i] = g_s[i] + o, xm = the MoE input)
+        L.router_topk_multi_norm(heads, self.g_s[i], self.o,
+                                 la.post_attention_layernorm, eps,
+                                 self.g_m[i], xm, cfg.n_experts, k,
+                                 cfg.norm_topk_prob, self.g_status)
         pool = w.pool
         sh = w.shared
         ev = self.g_ev[i]

@@ -395,6 +395,45 @@ def test_attn_rope_one_launch_equals_two(dev, nq, nkv):
         assert torch.equal(c0.view(torch.int16), c1.view(torch.int16))
 
 
+def test_router_with_norm_equals_norm_then_router(dev):
+    """slx_router_topk_multi_norm (residual add + RMSNorm + two router heads
+    in one launch) against slx_add_rmsnorm_out + slx_router_topk_multi: the
+    same bits in h_out, x_out, the ids and the scores."""
+    H, E, k = 2560, 256, 10
+    rng = np.random.default_rng(13)
+    h = bf16_tensor(A.bf16_round(rng.standard_normal((1, H)).astype(np.float32) * 4), dev)
+    d = bf16_tensor(A.bf16_round(rng.standard_normal((1, H)).astype(np.float32)), dev)
+    w = bf16_tensor(A.bf16_round((1 + 0.05 * rng.standard_normal(H)).astype(np.float32)), dev)
+    ratio = bf16_tensor(A.bf16_round((1 + 0.05 * rng.standard_normal(H)).astype(np.float32)), dev)
+    gates = [bf16_tensor(A.bf16_round((rng.standard_normal((E, H)) / np.sqrt(H))
+                                      .astype(np.float32)), dev) for _ in range(2)]
+    bias = torch.from_numpy(synth.zipf_bias(E, 1.1, 3)).to(dev)
+    st = _status(dev)
+    outs = []
+    for fused in (False, True):
+        ho = torch.empty(1, H, dtype=torch.bfloat16, device=dev)
+        xo = torch.empty(1, H, dtype=torch.bfloat16, device=dev)
+        ids = [torch.empty(1, k, dtype=torch.int32, device=dev) for _ in range(2)]
+        sc = [torch.empty(1, k, dtype=torch.float32, device=dev) for _ in range(2)]
+        scr = [torch.zeros(L.router_scratch_bytes(1, E), dtype=torch.uint8,
+                           device=dev) for _ in range(2)]
+        heads = [L.router_head(gates[0], bias, ids[0], sc[0], scr[0]),
+                 L.router_head(gates[1], bias, ids[1], sc[1], scr[1],
+                               ratio=ratio)]
+        for _ in range(2):   # tickets left at zero for the next call
+            if fused:
+                L.router_topk_multi_norm(heads, h, d, w, 1e-6, ho, xo, E, k,
+                                         True, st)
+            else:
+                L.add_rmsnorm_out(h, d, w, 1e-6, ho, xo)
+                L.router_topk_multi(xo, heads, E, k, True, st)
+        torch.cuda.synchronize()
+        assert st.item() == 0
+        outs.append([t.clone() for t in (ho, xo, *ids, *sc)])
+    for a, b in zip(*outs):
+        assert torch.equal(a.view(torch.uint8), b.view(torch.uint8))
+
+
 def test_router_two_heads_one_launch(dev):
     """Router + next-layer predictor in one launch equal two single calls."""
     T, H, E, k = 3, 2048, 256, 8
