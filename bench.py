@@ -417,6 +417,72 @@ def run_glu(args) -> None:
                        "l2": "inputs larger than L2"}}), flush=True)
 
 
+def run_sweep(args) -> None:
+    """Expert-major prefill with streaming: one
+    2048-token chunk of seeded N(0,1) bf16 hidden states through every MoE
+    layer of the 117B-shaped checkpoint (the same chunk into each layer),
+    experts in 7.5 GiB pools, every needed expert read once per layer from
+    the shards in expert-id order through the sweep (STREAMLX_PREFILL=sweep)
+    and the hottest adopted.  Timed twice: with the shards' pages dropped
+    from the page cache first (cold), then again (warm)."""
+    import torch
+
+    from streamlx_b200 import synth
+    from streamlx_b200.integrate import aggregate_stats, load_streaming_model
+    rank, world, local = dist_env()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    preset = args.preset or "laguna_c3"
+    d = synth_dir(preset, SEED, local, lambda: None)
+    cfg = synth.load_config(d)
+    budget = args.budget_gib if args.budget_gib is not None else 7.5
+    model, _, pools, reader = load_streaming_model(
+        d, int(budget * (1 << 30)), k=cfg.top_k, device=dev)
+    g = torch.Generator(device=dev).manual_seed(SEED)
+    T = PREFILL_SHAPE["tokens"]
+    x = torch.randn(T, cfg.hidden, generator=g, device=dev).to(torch.bfloat16)
+    shards = [os.path.join(d, f) for f in sorted(os.listdir(d))
+              if f.endswith(".safetensors")]
+    runs = {}
+    for label in ("cold", "warm"):
+        if label == "cold":
+            for f in shards:
+                fd = os.open(f, os.O_RDONLY)
+                try:
+                    os.posix_fadvise(fd, 0, 0, os.POSIX_FADV_DONTNEED)
+                finally:
+                    os.close(fd)
+        for p in pools.values():
+            p.reset_stats()
+        r0 = (reader.bytes_read, reader.reads)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for layer in range(cfg.layers):
+            model.moe_forward(layer, x)
+        torch.cuda.synchronize()
+        secs = time.perf_counter() - t0
+        st = aggregate_stats(pools)
+        runs[label] = {"seconds": round(secs, 3),
+                       "tok_s": round(T / secs, 1),
+                       "bytes_read": reader.bytes_read - r0[0],
+                       "reads": reader.reads - r0[1],
+                       "sweep_experts": st["sweep_experts"],
+                       "sweep_fetch_s": round(st["sweep_fetch_s"], 3),
+                       "adopted": st["adopted"]}
+    reader.close()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "prefill_tok_s_streaming", "value": runs["cold"]["tok_s"],
+            "unit": "tok/s", "n_gpus": 1, "higher_is_better": True,
+            "cold": runs["cold"], "warm": runs["warm"],
+            "config": {"workload": "2048-token chunk through every MoE layer "
+                       "of the 117B-shaped checkpoint (the same seeded "
+                       "hidden states into each layer)", "model": preset,
+                       "layers": cfg.layers, "expert_budget_gib": budget,
+                       "prefill": os.environ.get("STREAMLX_PREFILL", "sweep")},
+            "data": "synthetic (seeded)"}), flush=True)
+
+
 def synth_expert_bytes(H: int, I: int) -> int:
     from streamlx_b200 import synth
     return synth.expert_bytes(H, I, 2, 64)
@@ -908,9 +974,11 @@ def main():
     ap.add_argument("--check", action="store_true",
                     help="ep mode: compare with an all-experts computation")
     ap.add_argument("--mode", default="decode",
-                    choices=["decode", "prefill", "ep", "glu"],
+                    choices=["decode", "prefill", "ep", "glu", "sweep"],
                     help="prefill: only the prefill measurement (its own "
-                         "line); glu: only the decode SwitchGLU kernel")
+                         "line); glu: only the decode SwitchGLU kernel; "
+                         "sweep: 2048-token prefill through every MoE layer "
+                         "with expert streaming (cold and warm page cache)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -922,6 +990,8 @@ def main():
         run_ep(args)
     elif args.mode == "glu":
         run_glu(args)
+    elif args.mode == "sweep":
+        run_sweep(args)
     else:
         run_ours(args)
 

@@ -21,14 +21,45 @@ from streamlx_b200 import synth  # noqa: E402
 from streamlx_b200.integrate import load_streaming_model  # noqa: E402
 
 
-def decode(model, toks):
+def decode(model, toks, ids=None):
     out = []
     for t in toks:
         model.step(torch.tensor([int(t)], dtype=torch.int32,
                                 device=model.device))
         out.append(model.logits.clone())
+        if ids is not None:
+            ids.append(model.g_ids.reshape(model.cfg.layers, -1).cpu().numpy())
     torch.cuda.synchronize()
     return torch.cat(out).cpu()
+
+
+def oracle_check(d, toks, ids, got):
+    """The sharded run against the CPU oracle: the same ordered experts at
+    every layer and step (the temporal-reuse decisions taken from the GPU
+    run, as in tests/test_model_gpu.py), logits within 2e-2 max-abs and
+    5e-3 rel-L2 (the bf16 pipeline's own spread on these decoders)."""
+    from oracle import affine as A
+    from oracle.model import OracleDecoder
+    o = OracleDecoder(d)
+    prev = None
+    worst_rel = worst_abs = 0.0
+    ids_ok = True
+    for t, tk in enumerate(toks):
+        forced = {} if prev is None else {
+            i: prev[i] for i in range(len(prev))
+            if np.array_equal(ids[t][i], prev[i])}
+        want, routed = o.step(int(tk), forced=forced)
+        ids_ok &= all(np.array_equal(ids[t][i], routed[i])
+                      for i in range(len(routed)))
+        g = A.bf16_from_bits(got[t].view(torch.int16).numpy().view(np.uint16))
+        w = A.bf16_round(want)
+        worst_rel = max(worst_rel, A.rel_l2(g, w))
+        worst_abs = max(worst_abs, float(np.max(np.abs(g - w))))
+        prev = ids[t]
+    return {"oracle_ids_equal": bool(ids_ok), "oracle_rel_l2": worst_rel,
+            "oracle_max_abs": worst_abs,
+            "oracle_ok": bool(ids_ok and worst_rel <= 5e-3 and
+                              worst_abs <= 2e-2)}
 
 
 def main():
@@ -50,7 +81,8 @@ def main():
     model, _, pools, reader = load_streaming_model(d, 0, k=cfg.top_k,
                                                    device=dev,
                                                    expert_parallel=True)
-    got = decode(model, toks)
+    ids = []
+    got = decode(model, toks, ids)
     local_experts = sum(p.n_slots for p in pools.values())
     model.ep.close()
     dist.barrier()
@@ -64,6 +96,7 @@ def main():
         res["max_abs"] = float((got.float() - want.float()).abs().max())
         res["tokens_equal"] = bool(torch.equal(got.argmax(-1),
                                                want.argmax(-1)))
+        res.update(oracle_check(d, toks, ids, got))
         print(json.dumps(res), flush=True)
     dist.barrier()
     dist.destroy_process_group()

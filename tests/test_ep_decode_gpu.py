@@ -3,7 +3,9 @@ torchrun ranks (one per GPU), the owned experts' output rows exchanged over
 NVLink peer memory inside the SwitchGLU launch and combined by each rank
 (slx_switchglu_ep / slx_ep_combine_rmsnorm).  The combine sums in the same
 order as the single-GPU kernel, so the logits must be bit-identical to the
-same model decoded on one GPU with every expert resident.  One rank runs on
+same model decoded on one GPU with every expert resident; the sharded run is
+also checked against the CPU oracle (ordered experts at every layer and step,
+logits within the decoder tolerance).  One rank runs on
 any box; two ranks need two GPUs."""
 
 import json
@@ -45,6 +47,7 @@ def test_ep_decode_one_rank_bit_identical(preset, tmp_path):
     res = _run(1, preset, 12, tmp_path)
     assert res["world"] == 1
     assert res["bit_identical"], res
+    assert res["oracle_ok"], res
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or
@@ -54,3 +57,4 @@ def test_ep_decode_two_ranks_bit_identical(preset, tmp_path):
     res = _run(2, preset, 12, tmp_path)
     assert res["world"] == 2
     assert res["bit_identical"], res
+    assert res["oracle_ok"], res
