@@ -753,6 +753,7 @@ SLX_DEV void named_bar_fused() {
 constexpr int kFMaxA = 8;                 // gate/up tiles per CTA
 constexpr int kFMaxB = 64;                // down tiles per CTA
 constexpr int kFMaxUnits = 64;
+constexpr int kFTable = 1024;             // slot tables staged in shared memory
 
 struct FusedArgs {
   GemvArgs a;
@@ -1136,6 +1137,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
   __shared__ float s_vmax[kFW];
   __shared__ float s_vunit;
   __shared__ int s_slot[kFMaxUnits];
+  __shared__ int s_table[kFTable];
   __shared__ float s_score[kFMaxUnits];  // combine weight per unit (shared: 1)
   __shared__ int s_need;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1172,14 +1174,29 @@ __global__ void __launch_bounds__(kFThreads, 1)
   }
 
   // slots of the routed experts, one lane each; s_need: one has none
+  // the expert -> slot table comes in whole, beside the ids (one L2 round
+  // trip for both instead of ids, then table entries)
+  const bool tab_smem = a.slot_table && a.n_table <= kFTable;
   auto lookup_slots = [&]() {
+    if (tab_smem && warp > 0)
+      for (int e = threadIdx.x - 32; e < a.n_table; e += kFW * 32)
+        s_table[e] = __ldcg(a.slot_table + e);
+    int e_id = -1;
+    if (warp == 0 && lane < a.k) e_id = a.ids[lane];
+    __syncthreads();
     if (warp == 0) {
       unsigned miss = 0u;
       for (int j0 = 0; j0 < a.k; j0 += 32) {
         const int j = j0 + lane;
         int sl = -1;
         if (j < a.k) {
-          sl = lookup_slot(a.ids, j, a.slot_table, a.n_table, a.n_slots);
+          if (tab_smem) {
+            const int e = j0 == 0 ? e_id : a.ids[j];
+            sl = (e >= 0 && e < a.n_table) ? s_table[e] : -1;
+            if (sl >= a.n_slots) sl = -1;
+          } else {
+            sl = lookup_slot(a.ids, j, a.slot_table, a.n_table, a.n_slots);
+          }
           s_slot[j] = sl;
         }
         miss |= __ballot_sync(0xffffffffu, j < a.k && sl < 0);
@@ -1240,14 +1257,6 @@ __global__ void __launch_bounds__(kFThreads, 1)
     }
     if (!f.b_late) {
       issue_b();
-    } else {
-      // the down tiles share the gate/up stages: start their DRAM reads now
-      // into L2, the copies into shared memory follow once phase A is done
-      for (int s = lane; s < nbt; s += 32) {
-        int bytes = 0;
-        const uint8_t* src = b_src(s, bytes);
-        if (src) bulk_prefetch_l2(src, bytes);
-      }
     }
     if (lane == 0) SLX_TRACE_AT(1, 13, globaltimer_ns());
     // after every request (each copy instruction orders after the memory
@@ -1258,6 +1267,18 @@ __global__ void __launch_bounds__(kFThreads, 1)
       s_score[j] = (d.scores && j < d.k) ? d.scores[j] : 1.f;
     }
     if (log_late && bid == 0 && lane == 0) svc_write_log(f, a, 0);
+    if (f.b_late) {
+      // the down tiles share the gate/up stages: once this CTA's gate/up
+      // bytes are in, start the down tiles' DRAM reads into L2 (they land
+      // during the epilogue and the grid barrier); the copies into shared
+      // memory follow once phase A is done
+      if (na > 0) mbar_wait(&fullA[na - 1], 0, a.status);
+      for (int s = lane; s < nbt; s += 32) {
+        int bytes = 0;
+        const uint8_t* src = b_src(s, bytes);
+        if (src) bulk_prefetch_l2(src, bytes);
+      }
+    }
   } else {
     // ---- activation fragments of the token (per-token scale first) ----
     const int ct = threadIdx.x - 32;
