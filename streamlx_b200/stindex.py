@@ -16,7 +16,14 @@ quantized-checkpoint conventions, not any particular loader):
   ``[out, in / group_size]``; ``config.json``'s ``quantization`` object holds
   the default ``bits`` / ``group_size`` and, as nested objects keyed by module
   path, per-module overrides (mlx-vlm exports prefix paths with
-  ``language_model.``, which is ignored when matching).
+  ``language_model.``, which is ignored when matching);
+* an mlx-vlm export of a text-only model (every key of
+  ``model.safetensors.index.json``'s ``weight_map`` starting with
+  ``language_model.``) also names the router matrix ``….mlp.gate.proj.…``
+  where mlx-lm has ``….mlp.gate.…``.  ``get`` / ``read_tensor`` resolve the
+  mlx-lm name against such an export, the remap streamlx installs as a
+  sanitize hook (streamlx/integrate.py:349-394, ``_vlm_export_shim``);
+  native exports are untouched.
 
 The public surface is the one streamlx's loader, reader and pool call
 (streamlx/stindex.py:22-119): ``TensorLoc`` with ``row_stride`` /
@@ -106,6 +113,24 @@ def _module_key(name: str) -> str:
     return name
 
 
+def _mlx_lm_name(key: str) -> str:
+    """mlx-lm's name for a tensor key of an mlx-vlm export."""
+    return key[len(_VLM_PREFIX):].replace(".mlp.gate.proj.", ".mlp.gate.")
+
+
+def vlm_aliases(model_dir: str, keys) -> dict[str, str]:
+    """{mlx-lm name: stored key} when ``model_dir`` is an mlx-vlm export
+    (its index's weight map non-empty and every key prefixed), else {}."""
+    p = os.path.join(model_dir, "model.safetensors.index.json")
+    if not os.path.exists(p):
+        return {}
+    with open(p) as f:
+        wm = json.load(f).get("weight_map") or {}
+    if not wm or not all(k.startswith(_VLM_PREFIX) for k in wm):
+        return {}
+    return {_mlx_lm_name(k): k for k in keys if k.startswith(_VLM_PREFIX)}
+
+
 class QuantTable:
     """``config.json``'s quantization object: defaults plus per-module
     overrides (keys compared without the ``language_model.`` prefix)."""
@@ -157,6 +182,7 @@ class SafetensorsIndex:
             raise FileNotFoundError(
                 f"{self.model_dir}: no model-*.safetensors shard with tensors")
         self.quant = QuantTable.from_model_dir(self.model_dir)
+        self.aliases = vlm_aliases(self.model_dir, self.tensors)
         # layer -> {(proj, part): TensorLoc}, in tensor order (a later key
         # with the same (proj, part) suffix replaces an earlier one)
         self._switch: dict[int, dict] = {}
@@ -210,12 +236,20 @@ class SafetensorsIndex:
         return in_features, w.shape[1], bits, group
 
     def get(self, name: str) -> TensorLoc:
-        return self.tensors[name]
+        """The tensor stored as ``name``, or under the mlx-vlm key that
+        mlx-lm calls ``name``."""
+        loc = self.tensors.get(name)
+        if loc is None:
+            alias = self.aliases.get(name)
+            if alias is None:
+                raise KeyError(name)
+            loc = self.tensors[alias]
+        return loc
 
     def read_tensor(self, name: str) -> bytes:
         """All bytes of one tensor (trunk weights; experts go through the
         reader)."""
-        loc = self.tensors[name]
+        loc = self.get(name)
         buf = bytearray(loc.nbytes)
         view = memoryview(buf)
         done = 0

@@ -153,6 +153,33 @@ def test_graph_step_trace_equals_eager(tiny, name, slots, policy, monkeypatch):
     assert sum(x[0]["misses"] for x in s1) > 0
 
 
+def test_vlm_export_decodes_like_native(tiny, tmp_path, monkeypatch):
+    """A checkpoint rewritten as an mlx-vlm export (prefixed keys, router
+    matrix under ``.mlp.gate.proj.``) loads through load_streaming_model and
+    decodes to the same logits bit for bit as the native export."""
+    from .vlm_copy import write_vlm_copy
+    monkeypatch.setenv("STREAMLX_EVICT", "lru")
+    d = tiny["tiny_dec"]
+    v = write_vlm_copy(d, str(tmp_path / "vlm"))
+    cfg = synth.load_config(d)
+    bpe = synth.expert_bytes(cfg.hidden, cfg.inter, cfg.expert_bits, 64)
+    seq = np.random.default_rng(4).integers(0, cfg.vocab, 10)
+    out = []
+    for path in (d, v):
+        model, _, pools, reader = load_streaming_model(
+            path, budget_bytes=6 * bpe * cfg.layers, k=cfg.top_k)
+        lg = []
+        for tk in seq:
+            model.step(torch.tensor([int(tk)], dtype=torch.int32,
+                                    device=model.device))
+            lg.append(model.logits.clone())
+        torch.cuda.synchronize()
+        out.append((torch.cat(lg).cpu(), aggregate_stats(pools)["misses"]))
+        reader.close()
+    assert torch.equal(out[0][0].view(torch.int16), out[1][0].view(torch.int16))
+    assert out[0][1] == out[1][1] > 0
+
+
 def test_pool_dropin_call_matches_oracle(tiny):
     d = tiny["tiny_dec"]
     cfg = synth.load_config(d)

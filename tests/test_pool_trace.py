@@ -227,3 +227,43 @@ def test_pool_argument_errors(models):
     p = StreamingSwitchMLP(models["e32"], 0, 2, store="null")
     with pytest.raises(ValueError):
         p(None, [1, 2, 3])          # k > n_slots (streamlx/pool.py:300-301)
+
+
+def test_vlm_export_names_resolve(tmp_path):
+    """An mlx-vlm export of a text-only checkpoint (keys and quantization
+    overrides prefixed with ``language_model.``, router matrix under
+    ``.mlp.gate.proj.``) resolves every mlx-lm name to the same bytes, and
+    its expert tensors to the same ranges and quantization parameters, as
+    the native export (streamlx/integrate.py:349-394)."""
+    from .vlm_copy import write_vlm_copy
+    cfg = synth.PRESETS["tiny_dec"]
+    d = synth.write_model(str(tmp_path / "native"), cfg, seed=5)
+    v = write_vlm_copy(d, str(tmp_path / "vlm"))
+    a, b = SafetensorsIndex(d), SafetensorsIndex(v)
+    assert a.aliases == {} and len(b.aliases) == len(a.tensors)
+    assert any(".mlp.gate.proj." in k for k in b.tensors)
+    for name, loc in a.tensors.items():
+        got = b.get(name)
+        assert (got.nbytes, got.dtype, got.shape) == \
+            (loc.nbytes, loc.dtype, loc.shape), name
+        assert b.read_tensor(name) == a.read_tensor(name), name
+    for L in range(cfg.layers):
+        ta, tb = a.switch_triples(L), b.switch_triples(L)
+        assert a.layer_expert_bytes(L) == b.layer_expert_bytes(L)
+        for p in PROJS:
+            assert b.quant_params(tb[p]) == a.quant_params(ta[p])
+            for q in PARTS:
+                for e in (0, cfg.n_experts - 1):
+                    (pa, oa, na), (pb, ob, nb) = (ta[p][q].expert_range(e),
+                                                  tb[p][q].expert_range(e))
+                    with open(pa, "rb") as fa, open(pb, "rb") as fb:
+                        assert os.pread(fa.fileno(), na, oa) == \
+                            os.pread(fb.fileno(), nb, ob)
+    with pytest.raises(KeyError):
+        b.get("model.layers.0.mlp.nothing.weight")
+    # one unprefixed key in the weight map: a native export, no remap
+    p = os.path.join(v, "model.safetensors.index.json")
+    wm = json.load(open(p))
+    wm["weight_map"]["lm_head.weight"] = "x"
+    json.dump(wm, open(p, "w"))
+    assert SafetensorsIndex(v).aliases == {}
