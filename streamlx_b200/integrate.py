@@ -454,7 +454,8 @@ def load_streaming_model(model_dir: str, budget_bytes: int, k: int = 8,
     ``expert_parallel``: one process per GPU under torch.distributed; this
     rank keeps only its block of every layer's experts, all resident (the
     budget is not used), and decode steps exchange the experts' outputs
-    over NVLink peer memory (no reference counterpart)."""
+    over NVLink peer memory (no reference counterpart).  A group of one
+    rank holds every expert and decodes without the exchange."""
     from .model import SynthDecoder
     index = SafetensorsIndex(model_dir)
     reader = ExpertReader(index)
@@ -488,9 +489,14 @@ def load_streaming_model(model_dir: str, budget_bytes: int, k: int = 8,
                 pool.ensure(list(range(e0, min(e0 + 32, n_exp[i]))))
         model.layers[i].mlp.switch_mlp = StreamingSwitchGLU(
             pool, model.layers[i].mlp.shared_struct())
-        pools[i] = pool
-    for pool in pools.values():     # stats first finish deferred steps
-        pool.flush_hook = model.flush
+        pool.flush_hook = model.flush   # stats first finish deferred steps
+        if i in res_layers:
+            # every expert in its slot for good: the reference runs these
+            # layers on the stock path, outside the returned pools
+            pool.sync_device()
+            model.static_glu[i] = True
+        else:
+            pools[i] = pool
     if os.environ.get("STREAMLX_PREFETCH", "1") != "0":
         linked = model.link_prefetch({i: pools[i] for i in streamed})
         if linked:
@@ -525,7 +531,11 @@ def _load_expert_parallel(model, model_dir, index, reader, moe_layers,
         pools[i] = pool
     for pool in pools.values():
         pool.flush_hook = model.flush
-    model.enable_expert_parallel(group)
+    model.static_glu = [True] * len(model.layers)
+    if world > 1:
+        model.enable_expert_parallel(group)
+    # one rank holds every expert: no rows to exchange, so the step keeps
+    # the single-GPU form (the SwitchGLU launch combines the experts itself)
     return model, IdTokenizer(), pools, reader
 
 

@@ -168,6 +168,9 @@ class SynthDecoder:
                            "parks": 0, "park_steps": 0}
         self._step_active = False
         self.ep = None              # EpExchange when experts are sharded
+        # layers whose pool holds every expert for good (fully resident):
+        # their launch needs no slot fill and the host no bookkeeping
+        self.static_glu = [False] * cfg.layers
         # temporal-reuse routing override of the workloads: per (token,
         # layer) a seeded coin decides whether the previous token's expert
         # set is kept (applied identically to the CPU oracle)
@@ -510,7 +513,8 @@ class SynthDecoder:
                                   capture_error_mode="thread_local"):
                 self.g_lstatus.zero_()
                 for i in range(n):
-                    self._record_layer(i)
+                    self._record_layer(i, serviced=not self.static_glu[i]
+                                       or self.ep is not None)
                 self._record_tail()
             self._kernels_full = L.LAUNCHES[0] - c0
         finally:
@@ -578,10 +582,12 @@ class SynthDecoder:
         idle = 0
         while True:
             busy = False
-            while nxt < n and int(log[nxt, 0]) == stamp:
-                t0 = time.perf_counter()
-                self._on_record(nxt, log[nxt].copy())
-                ht["bookkeeping"] += time.perf_counter() - t0
+            while nxt < n and (self.static_glu[nxt] or
+                               int(log[nxt, 0]) == stamp):
+                if not self.static_glu[nxt]:    # static layers write none
+                    t0 = time.perf_counter()
+                    self._on_record(nxt, log[nxt].copy())
+                    ht["bookkeeping"] += time.perf_counter() - t0
                 nxt += 1
                 busy = True
             pk = svc.pending_park(stamp)
@@ -660,8 +666,8 @@ class SynthDecoder:
         t1 = time.perf_counter()
         parks0 = ht["parks"]
         try:
-            if self.ep is not None:
-                self._ev_done.synchronize()     # resident shards: no service
+            if self.ep is not None or all(self.static_glu):
+                self._ev_done.synchronize()     # resident experts: no service
             else:
                 self._serve_step(stamp)
         except BaseException:

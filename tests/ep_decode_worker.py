@@ -84,7 +84,8 @@ def main():
     ids = []
     got = decode(model, toks, ids)
     local_experts = sum(p.n_slots for p in pools.values())
-    model.ep.close()
+    if model.ep is not None:        # one rank: every expert local, no exchange
+        model.ep.close()
     dist.barrier()
     res = {"rank": rank, "world": dist.get_world_size(),
            "local_experts": local_experts}

@@ -5,8 +5,9 @@ NVLink peer memory inside the SwitchGLU launch and combined by each rank
 order as the single-GPU kernel, so the logits must be bit-identical to the
 same model decoded on one GPU with every expert resident; the sharded run is
 also checked against the CPU oracle (ordered experts at every layer and step,
-logits within the decoder tolerance).  One rank runs on
-any box; two ranks need two GPUs."""
+logits within the decoder tolerance).  One rank holds every expert and
+decodes without the exchange (the loader's process-group path on one GPU);
+it runs on any box.  Two ranks need two GPUs."""
 
 import json
 import os

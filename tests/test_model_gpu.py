@@ -180,6 +180,44 @@ def test_vlm_export_decodes_like_native(tiny, tmp_path, monkeypatch):
     assert out[0][1] == out[1][1] > 0
 
 
+def test_resident_layers_skip_the_pool(tiny, monkeypatch):
+    """Fully resident layers (plan_residency) run without slot service or
+    host bookkeeping and stay out of the returned pools, as the reference's
+    stock-path layers do (streamlx/integrate.py:425-437); the logits equal
+    the streamed run's bit for bit, also with one layer put back on the
+    serviced path between two static ones."""
+    monkeypatch.setenv("STREAMLX_EVICT", "lru")
+    d = tiny["tiny_dec"]
+    cfg = synth.load_config(d)
+    bpe = synth.expert_bytes(cfg.hidden, cfg.inter, cfg.expert_bits, 64)
+    seq = np.random.default_rng(6).integers(0, cfg.vocab, 8)
+
+    def run(budget, resident=None, serviced_layer=None):
+        model, _, pools, reader = load_streaming_model(
+            d, budget_bytes=budget, k=cfg.top_k, resident=resident)
+        if serviced_layer is not None:
+            model.static_glu[serviced_layer] = False
+        lg = []
+        for tk in seq:
+            model.step(torch.tensor([int(tk)], dtype=torch.int32,
+                                    device=model.device))
+            lg.append(model.logits.clone())
+        torch.cuda.synchronize()
+        st = (list(model.static_glu), sorted(pools),
+              aggregate_stats(pools)["misses"])
+        reader.close()
+        return torch.cat(lg).cpu().view(torch.int16), st
+
+    a, sa = run(6 * bpe * cfg.layers)
+    b, sb = run(10 ** 13, resident="on")
+    c, sc = run(10 ** 13, resident="on", serviced_layer=1)
+    assert sa == ([False] * cfg.layers, list(range(cfg.layers)), sa[2])
+    assert sa[2] > 0
+    assert sb == ([True] * cfg.layers, [], 0)
+    assert sc[0] == [True, False] + [True] * (cfg.layers - 2)
+    assert torch.equal(a, b) and torch.equal(a, c)
+
+
 def test_pool_dropin_call_matches_oracle(tiny):
     d = tiny["tiny_dec"]
     cfg = synth.load_config(d)
