@@ -47,6 +47,7 @@ extern "C" int slx_trace_read(unsigned long long* host) {
 namespace slx {
 
 constexpr int kNW = 8;                    // consumer warps
+constexpr int kXTasks = 1;  // activation tasks a consumer thread holds in registers
 constexpr int kThreads = 32 * (kNW + 1);  // + producer warp
 constexpr int kMaxStages = 32;
 constexpr int kRows = 16;
@@ -167,12 +168,22 @@ SLX_DEV float absmax_part(const uint16_t* x, int n, int t, int nt) {
   return m;
 }
 
+// Largest |x| of the 16 bf16 values of one (group, tig) task.
+SLX_DEV float absmax16(const uint4& q0, const uint4& q1) {
+  const uint32_t w8[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+  float m = 0.f;
+#pragma unroll
+  for (int q = 0; q < 8; ++q)
+    m = fmaxf(m, fmaxf(fabsf(bf16_lo(w8[q])), fabsf(bf16_hi(w8[q]))));
+  return m;
+}
+
+// Fragment words and partial sum of task (G, tig) from its 16 values
+// (columns 64G + 16 tig .. + 15, eight per uint4).
 template <int BITS>
-SLX_DEV void frag_task(const uint16_t* __restrict__ x, int G, int tig,
+SLX_DEV void frag_from(const uint4& q0, const uint4& q1, int G, int tig,
                        uint32_t* frag, float* part, int32_t* status,
                        float vscale) {
-  const uint4* src = reinterpret_cast<const uint4*>(x + 64 * G + 16 * tig);
-  const uint4 q0 = src[0], q1 = src[1];
   const uint32_t w8[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
   float s = 0.f;
 #pragma unroll
@@ -190,11 +201,39 @@ SLX_DEV void frag_task(const uint16_t* __restrict__ x, int G, int tig,
   part[G * 4 + tig] = s;
 }
 
+template <int BITS>
+SLX_DEV void frag_task(const uint16_t* __restrict__ x, int G, int tig,
+                       uint32_t* frag, float* part, int32_t* status,
+                       float vscale) {
+  const uint4* src = reinterpret_cast<const uint4*>(x + 64 * G + 16 * tig);
+  frag_from<BITS>(src[0], src[1], G, tig, frag, part, status, vscale);
+}
+
 // Sum the four per-tig partials of every group (fixed order).
 SLX_DEV void frag_sums(const float* part, float* xsum, int n, int tid,
                        int nthr) {
   for (int i = tid; i < n; i += nthr)
     xsum[i] = (part[4 * i] + part[4 * i + 1]) + (part[4 * i + 2] + part[4 * i + 3]);
+}
+
+// The activation fragments of a token too wide for one task per consumer
+// thread (two rounds of loads); returns the fold's unit.  All consumer
+// threads call this.
+SLX_DEV void named_bar_consumers();
+template <int BITS>
+__device__ __noinline__ float frag_wide(const uint16_t* xr, int in, int nG,
+                                        int ct, uint32_t* frag, float* part,
+                                        float* s_vmax, int32_t* status) {
+  named_bar_consumers();  // every consumer is past the previous token's MMAs
+  const float m = absmax_part(xr, in, ct, kNW * 32);
+  if ((ct & 31) == 0) s_vmax[ct >> 5] = m;
+  named_bar_consumers();
+  float mm = 0.f;
+  for (int w = 0; w < kNW; ++w) mm = fmaxf(mm, s_vmax[w]);
+  const int ve = vec_exp(mm);
+  for (int p = ct; p < 4 * nG; p += kNW * 32)
+    frag_task<BITS>(xr, p >> 2, p & 3, frag, part, status, pow2f(ve));
+  return pow2f(24 - ve);
 }
 
 SLX_DEV void load_frag(const uint32_t* frag, int G, int tig, uint32_t (&b)[8]) {
@@ -337,8 +376,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   float* part = xsum + nG;     // [nG][4]
   float* red = part + 4 * nG;  // [NS][kNW][32]
   const int NS = a.n_stages;
+  float* s_vmax = red + NS * kNW * 32;  // [kNW] consumer warps' max |x|
   uint8_t* stages = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(red + NS * kNW * 32) + 127) & ~uintptr_t(127));
+      (reinterpret_cast<uintptr_t>(s_vmax + kNW) + 127) & ~uintptr_t(127));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q_begin = (int)((long long)a.n_tiles * blockIdx.x / gridDim.x);
@@ -406,21 +446,44 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int st = i % NS;
     const TileInfo t = gemv_tile(a, q, scache);
     if (t.token != cached_token) {
-      named_bar_consumers();
       const uint16_t* xr = a.x + (size_t)t.token * a.in;
-      // per-token scale: the consumers' max |x| meets in frag[] (rebuilt
-      // right after, and nobody reads the old fragments any more)
-      const float m = absmax_part(xr, a.in, ct, kNW * 32);
-      if (lane == 0) reinterpret_cast<float*>(frag)[cw] = m;
-      named_bar_consumers();
-      float mm = 0.f;
-      for (int w = 0; w < kNW; ++w)
-        mm = fmaxf(mm, reinterpret_cast<const float*>(frag)[w]);
-      const int ve = vec_exp(mm);
-      vunit = pow2f(24 - ve);
-      named_bar_consumers();
-      for (int p = ct; p < 4 * nG; p += kNW * 32)
-        frag_task<BITS>(xr, p >> 2, p & 3, frag, part, a.status, pow2f(ve));
+      if (4 * nG <= kXTasks * kNW * 32) {
+        // one round of global loads: the thread's (group, tig) tasks keep
+        // their 16 values in registers for the scale and the fragments
+        uint4 xv[kXTasks][2];
+        float m = 0.f;
+#pragma unroll
+        for (int j = 0; j < kXTasks; ++j) {
+          const int p = ct + j * kNW * 32;
+          if (p < 4 * nG) {
+            const uint4* src = reinterpret_cast<const uint4*>(
+                xr + 64 * (p >> 2) + 16 * (p & 3));
+            xv[j][0] = src[0];
+            xv[j][1] = src[1];
+            m = fmaxf(m, absmax16(xv[j][0], xv[j][1]));
+          }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+          m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) s_vmax[cw] = m;
+        // also: every consumer is past the previous token's MMAs, so its
+        // fragments may be overwritten
+        named_bar_consumers();
+        float mm = 0.f;
+        for (int w = 0; w < kNW; ++w) mm = fmaxf(mm, s_vmax[w]);
+        const int ve = vec_exp(mm);
+        vunit = pow2f(24 - ve);
+#pragma unroll
+        for (int j = 0; j < kXTasks; ++j) {
+          const int p = ct + j * kNW * 32;
+          if (p < 4 * nG)
+            frag_from<BITS>(xv[j][0], xv[j][1], p >> 2, p & 3, frag, part,
+                            a.status, pow2f(ve));
+        }
+      } else {
+        vunit = frag_wide<BITS>(xr, a.in, nG, ct, frag, part, s_vmax, a.status);
+      }
       named_bar_consumers();
       frag_sums(part, xsum, nG, ct, kNW * 32);
       named_bar_consumers();
@@ -1658,7 +1721,7 @@ static int launch_gemv_t(GemvArgs a, cudaStream_t stream, bool pdl_secondary) {
   a.tile_bytes = (int)pair_tile_bytes(a.in, BITS);
   a.stage_bytes = (a.tile_bytes + 127) & ~127;
   // fixed part + per stage (tile + its kNW x 32 partials)
-  const int fixed = 3 * kMaxStages * 8 + nG * 32 * 4 + nG * 4 * 5 + 128;
+  const int fixed = 3 * kMaxStages * 8 + nG * 32 * 4 + nG * 4 * 5 + kNW * 4 + 128;
   const int per_stage = a.stage_bytes + kNW * 32 * 4;
   int ns = (kSmemBudget - fixed) / per_stage;
   if (ns < 2) ns = (kSmemMax - fixed) / per_stage;

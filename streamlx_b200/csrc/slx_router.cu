@@ -436,8 +436,30 @@ struct WideLaunch {
 // sums added in order); CTA 0 also stores h_in + delta and x.  All threads
 // of the CTA call this.
 constexpr int kNormT = 256, kNormJ = 4;
+
+// The thread's chunks of the norm weight and the ratio: fixed weights,
+// loaded before the kernel waits on its predecessor.
+struct NormWeights {
+  uint4 w[kNormJ];
+  uint4 r[kNormJ];
+};
+
+SLX_DEV void norm_weights(const RouterNorm& nm, int H, const uint16_t* ratio,
+                          NormWeights& nw) {
+  const int t = threadIdx.x;
+  if (t >= kNormT) return;
+#pragma unroll
+  for (int j = 0; j < kNormJ; ++j) {
+    const int c = (j * kNormT + t) * 8;
+    if (c >= H) break;
+    nw.w[j] = __ldg(reinterpret_cast<const uint4*>(nm.w + c));
+    if (ratio) nw.r[j] = __ldg(reinterpret_cast<const uint4*>(ratio + c));
+  }
+}
+
 SLX_DEV void norm_stage(const RouterNorm& nm, int H, const uint16_t* ratio,
-                        float* s_x, float* red, bool store) {
+                        const NormWeights& nw, float* s_x, float* red,
+                        bool store) {
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   uint4 v[kNormJ];
   float ss = 0.f;
@@ -481,7 +503,7 @@ SLX_DEV void norm_stage(const RouterNorm& nm, int H, const uint16_t* ratio,
     for (int j = 0; j < kNormJ; ++j) {
       const int c = (j * kNormT + t) * 8;
       if (c >= H) break;
-      const uint4 wv = *reinterpret_cast<const uint4*>(nm.w + c);
+      const uint4 wv = nw.w[j];
       const uint32_t* pa = reinterpret_cast<const uint32_t*>(&v[j]);
       const uint32_t* pw = reinterpret_cast<const uint32_t*>(&wv);
       uint4 o;
@@ -495,7 +517,7 @@ SLX_DEV void norm_stage(const RouterNorm& nm, int H, const uint16_t* ratio,
       if (store) *reinterpret_cast<uint4*>(nm.y + c) = o;
       uint32_t rw[4] = {0, 0, 0, 0};
       if (ratio) {
-        const uint4 rv = *reinterpret_cast<const uint4*>(ratio + c);
+        const uint4 rv = nw.r[j];
         rw[0] = rv.x; rw[1] = rv.y; rw[2] = rv.z; rw[3] = rv.w;
       }
 #pragma unroll
@@ -540,12 +562,18 @@ __global__ void __launch_bounds__(kRouterThreads, 1)
     mbar_arrive_expect_tx(&s_bar, (uint32_t)nr * H * 2);
     bulk_g2s_plain(wsm, a.w + (size_t)e0 * H, (uint32_t)nr * H * 2, &s_bar);
   }
+  // fixed weights in flight before the wait: the norm weight and ratio
+  // chunks of this thread, the bias of its row
+  NormWeights nw;
+  if (L.norm.w) norm_weights(L.norm, H, a.ratio, nw);
+  const float row_bias =
+      (a.bias && threadIdx.x < nr) ? __ldg(a.bias + e0 + threadIdx.x) : 0.f;
   pdl_launch_dependents();
   pdl_wait_primary();
   __shared__ float s_red[32];
   const uint16_t* xr = a.x;  // one token
   if (L.norm.w) {
-    norm_stage(L.norm, H, a.ratio, s_x, s_red, blockIdx.x == 0);
+    norm_stage(L.norm, H, a.ratio, nw, s_x, s_red, blockIdx.x == 0);
   } else {
   for (int c = threadIdx.x * 8; c < H; c += kRouterThreads * 8) {
     const uint4 xv = *reinterpret_cast<const uint4*>(xr + c);
@@ -589,14 +617,14 @@ __global__ void __launch_bounds__(kRouterThreads, 1)
     const int rr = threadIdx.x, e = e0 + rr;
     const float S = (s_part[rr][0][0] + s_part[rr][1][0]) + (s_part[rr][2][0] + s_part[rr][3][0]);
     const float A = (s_part[rr][0][1] + s_part[rr][1][1]) + (s_part[rr][2][1] + s_part[rr][3][1]);
-    const float l = a.bias ? S + a.bias[e] : S;
+    const float l = a.bias ? S + row_bias : S;
     a.logits[e] = l;
     gbound[e] = logit_bound(S, A, l, depth);
-    __threadfence();
   }
+  // the CTA's stores are ordered before the ticket by the barrier and the
+  // ticket's release (cumulative); its acquire orders the last CTA's reads
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence();
     const int old = ticket_acq_rel(a.tickets);
     s_last = old == L.ctas_per_head - 1;
     if (s_last) *reinterpret_cast<volatile int32_t*>(a.tickets) = 0;

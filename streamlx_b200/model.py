@@ -171,6 +171,9 @@ class SynthDecoder:
         # layers whose pool holds every expert for good (fully resident):
         # their launch needs no slot fill and the host no bookkeeping
         self.static_glu = [False] * cfg.layers
+        self._all_pooled = None     # cached layer-set facts, set on first use
+        self._store_list = None
+        self._pf_layers = None
         # temporal-reuse routing override of the workloads: per (token,
         # layer) a seeded coin decides whether the previous token's expert
         # set is kept (applied identically to the CPU oracle)
@@ -254,8 +257,7 @@ class SynthDecoder:
         the pool bookkeeping in step and serves layers that park on a miss
         (_step_graph).  Otherwise the step runs layer by layer with one host
         sync on the routed ids per layer (_step_eager)."""
-        if self.ep is not None or (self.use_graphs and all(
-                hasattr(la.mlp.switch_mlp, "route") for la in self.layers)):
+        if self.ep is not None or (self.use_graphs and self._pooled()):
             return self._step_graph(token)
         self.flush()
         return self._step_eager(token)
@@ -476,7 +478,13 @@ class SynthDecoder:
         L.qlinear(self.w_lm, cfg.vocab, cfg.hidden, cfg.trunk_bits, self.x,
                   self.logits, self.g_status)
         L.argmax(self.logits, self.g_tok_out)
-        # a plain async copy (no allocator event) so it captures as a node
+        # plain async copies (no allocator event) so they capture as nodes:
+        # the step's ids become the next step's reuse candidates (not in the
+        # capture's initialising pass, which must not replace them), and the
+        # log goes to the host
+        if serviced:
+            L.copy_many([self.g_prev_ids.data_ptr()], [self.g_ids.data_ptr()],
+                        [self.g_ids.numel() * 4])
         L.copy_many([self.g_log_host.data_ptr()], [self.g_log.data_ptr()],
                     [self.g_log.numel() * 4])
 
@@ -507,6 +515,9 @@ class SynthDecoder:
                 self._record_tail(serviced=False)
             s.synchronize()
             self._pred_flags = [self._pred_on(i) for i in range(n)]
+            self._pf_layers = [i for i in range(n)
+                               if self.layers[i].mlp.pf_link is not None]
+            self._store_list = None
             full = torch.cuda.CUDAGraph()
             c0 = L.LAUNCHES[0]
             with torch.cuda.graph(full, stream=s,
@@ -540,11 +551,24 @@ class SynthDecoder:
                 L.event_elapsed_many([e[0] for e in ev], [e[1] for e in ev])
                 .tolist())
 
+    def _pooled(self) -> bool:
+        """Every layer's SwitchGLU is pool-backed (the graph step's
+        condition; the layers are fixed once the loader returns)."""
+        if self._all_pooled is None:
+            self._all_pooled = all(hasattr(la.mlp.switch_mlp, "route")
+                                   for la in self.layers)
+        return self._all_pooled
+
     def _stores(self):
-        for la in self.layers:
-            w = la.mlp.switch_mlp
-            if hasattr(w, "pool") and hasattr(w.pool.store, "deferred"):
-                yield w.pool
+        """Pools whose fills a step may defer: the static layers' pools
+        never fill."""
+        if self._store_list is None:
+            self._store_list = [
+                la.mlp.switch_mlp.pool for i, la in enumerate(self.layers)
+                if not self.static_glu[i]
+                and hasattr(la.mlp.switch_mlp, "pool")
+                and hasattr(la.mlp.switch_mlp.pool.store, "deferred")]
+        return self._store_list
 
     def flush(self) -> None:
         """Apply every recorded slot fill and table push now (on the current
@@ -631,7 +655,8 @@ class SynthDecoder:
         if self.n_pos >= self.max_len:
             raise RuntimeError("KV cache full")
         if self._graphs is not None and any(
-                self._pred_flags[i] != self._pred_on(i) for i in range(n)):
+                self._pred_flags[i] != self._pred_on(i)
+                for i in self._pf_layers):
             self._graphs = None     # a prediction gate closed: recapture
         if self._graphs is None:
             self._capture()
@@ -642,9 +667,11 @@ class SynthDecoder:
             stamp = 1
         ch = self.g_ctrl_host.numpy()
         ch[0] = self.n_pos
-        for i in range(n):
-            ch[1 + i] = int(bool(self.repeat_p) and self.n_pos > 0 and
-                            self._rng.random() < self.repeat_p)
+        if self.repeat_p and self.n_pos > 0:
+            # one draw per layer, in layer order (the eager path's sequence)
+            ch[1:1 + n] = self._rng.random(n) < self.repeat_p
+        else:
+            ch[1:1 + n] = 0
         ch[n + 2] = stamp
         tok = token.reshape(1)
         if tok.dtype != torch.int32 or tok.device != self.device:
@@ -693,7 +720,6 @@ class SynthDecoder:
             self.g_lstatus.zero_()
             raise L.SlxError("device", st or bad[0], "decode step device error")
         self._glu_timing()
-        self.g_prev_ids.copy_(self.g_ids)
         self.n_pos += 1
         nxt = torch.empty(1, dtype=torch.int32, device=self.device)
         nxt.copy_(self.g_tok_out)
