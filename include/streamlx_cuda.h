@@ -430,7 +430,12 @@ int slx_attn_decode(const void* qkv, int T, int n_q, int n_kv, int head_dim,
  * head's key, appends key and value at position pos[0] of the caches and
  * attends over positions 0..pos[0] (the new row taken from shared memory);
  * results equal the two-launch form bit for bit.  The trunk of the
- * synthetic decoders (mlx-lm's model code in the reference). */
+ * synthetic decoders (mlx-lm's model code in the reference).
+ * Under programmatic dependent launch (slx_set_pdl) pos[0] and the cache
+ * rows before it are read before the kernel waits on the preceding one:
+ * they must be complete before that kernel's chain started (written in an
+ * earlier step, with a stream synchronisation, a graph boundary or a
+ * launch without programmatic serialisation in between). */
 int slx_attn_rope_decode(const void* qkv, int n_q, int n_kv, int head_dim,
                          const void* q_norm, const void* k_norm, float eps,
                          const float* inv_freq, const int32_t* pos,

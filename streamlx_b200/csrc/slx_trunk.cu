@@ -307,8 +307,28 @@ constexpr int kAttnSmem = 2 * kAttnChunk * 128 * 2 + kAttnMaxRep * 128 * 4 +
 // k_qk_rope_cache (lane l holds pairs l and l + 32 of the 64, each half of
 // the sum reduced as one 32-thread block would): rotated values (bf16) at
 // dst[i] and dst[i + 64].
-SLX_DEV void rope_head(const uint16_t* v, const uint16_t* nw, float eps, int p,
-                       const float* inv_freq, uint16_t* dst, int lane) {
+// The lane's norm weights (pairs lane and lane + 32: dims i and i + 64) and
+// inverse frequencies, fixed inputs loaded before the kernel waits.
+struct RopeLane {
+  float w[2][2];  // [pair][dim i, dim i + 64]
+  float f[2];
+};
+
+SLX_DEV RopeLane rope_lane(const uint16_t* nw, const float* inv_freq,
+                           int lane) {
+  RopeLane r;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int i = lane + 32 * h;
+    r.w[h][0] = bf16_to_f32(__ldg(nw + i));
+    r.w[h][1] = bf16_to_f32(__ldg(nw + i + 64));
+    r.f[h] = __ldg(inv_freq + i);
+  }
+  return r;
+}
+
+SLX_DEV void rope_head(const uint16_t* v, const RopeLane& rl, float eps, int p,
+                       uint16_t* dst, int lane) {
   float a[2], b[2], s2[2];
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
@@ -324,13 +344,31 @@ SLX_DEV void rope_head(const uint16_t* v, const uint16_t* nw, float eps, int p,
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const int i = lane + 32 * h;
-    const float an = round_bf16(a[h] * inv * bf16_to_f32(nw[i]));
-    const float bn = round_bf16(b[h] * inv * bf16_to_f32(nw[i + 64]));
-    const float ang = (float)p * inv_freq[i];
+    const float an = round_bf16(a[h] * inv * rl.w[h][0]);
+    const float bn = round_bf16(b[h] * inv * rl.w[h][1]);
+    const float ang = (float)p * rl.f[h];
     float sn, cs;
     sincosf(ang, &sn, &cs);
     dst[i] = f32_to_bf16(an * cs - bn * sn);
     dst[i + 64] = f32_to_bf16(an * sn + bn * cs);
+  }
+}
+
+// K and V rows c0 .. c0 + np - 1 of kv head hk into Ks / Vs (64 x 128
+// bf16 each; rows from np on, and row `skip`, zero).  All threads call this.
+SLX_DEV void stage_chunk(uint16_t* Ks, uint16_t* Vs, const uint16_t* kcache,
+                         const uint16_t* vcache, size_t kstride, int hk,
+                         int hd, int c0, int np, int skip) {
+  for (int u = threadIdx.x; u < kAttnChunk * 16; u += kAttnThreads) {
+    const int r = u >> 4, cu = u & 15;
+    uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+    if (r < np && c0 + r != skip) {
+      const size_t off = (size_t)(c0 + r) * kstride + (size_t)hk * hd;
+      kv = reinterpret_cast<const uint4*>(kcache + off)[cu];
+      vv = reinterpret_cast<const uint4*>(vcache + off)[cu];
+    }
+    reinterpret_cast<uint4*>(Ks)[u] = kv;
+    reinterpret_cast<uint4*>(Vs)[u] = vv;
   }
 }
 
@@ -360,13 +398,32 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1)
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
   pdl_launch_dependents();
-  pdl_wait_primary();
   const int hk = blockIdx.y, t = blockIdx.z;
   const int rep = nq / nkv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n = pos[t] + 1;
-  const bool ok_n = n > 0 && n <= max_len;
   const size_t kstride = (size_t)nkv * hd;
+  // ROPE: the position and the cache rows before the token's own (n - 1)
+  // are inputs of earlier steps, not of the preceding kernel, so this CTA's
+  // first chunk is staged before the wait (the token's row is filled in
+  // after it), as are the fixed norm weights and frequencies
+  int n = ROPE ? pos[t] + 1 : 0;
+  bool ok_n = n > 0 && n <= max_len;
+  int nchunks = ok_n ? (n + kAttnChunk - 1) / kAttnChunk : 0;
+  RopeLane rq, rk;
+  const bool early = ROPE && rank < nchunks;
+  if constexpr (ROPE) {
+    rq = rope_lane(R.qn, R.inv_freq, lane);
+    rk = rope_lane(R.kn, R.inv_freq, lane);
+    if (early) stage_chunk(Ks, Vs, kcache, vcache, kstride, hk, hd,
+                           rank * kAttnChunk, min(kAttnChunk, n - rank * kAttnChunk),
+                           n - 1);
+  }
+  pdl_wait_primary();
+  if constexpr (!ROPE) {
+    n = pos[t] + 1;
+    ok_n = n > 0 && n <= max_len;
+    nchunks = ok_n ? (n + kAttnChunk - 1) / kAttnChunk : 0;
+  }
   const uint16_t* q = qkv + (size_t)t * (nq + 2 * nkv) * hd +
                       (size_t)hk * rep * hd;
   // ROPE: the token's own key and value row (position n - 1), computed here
@@ -381,11 +438,11 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1)
     } else {
       for (int h = warp; h <= rep; h += kAttnThreads / 32) {
         if (h < rep)
-          rope_head(q + (size_t)h * hd, R.qn, R.eps, n - 1, R.inv_freq,
-                    qrot + h * 128, lane);
+          rope_head(q + (size_t)h * hd, rq, R.eps, n - 1, qrot + h * 128,
+                    lane);
         else
-          rope_head(base + (size_t)(nq + hk) * hd, R.kn, R.eps, n - 1,
-                    R.inv_freq, knew, lane);
+          rope_head(base + (size_t)(nq + hk) * hd, rk, R.eps, n - 1, knew,
+                    lane);
       }
       if (threadIdx.x < 128) vnew[threadIdx.x] = base[(size_t)(nq + nkv + hk) * hd + threadIdx.x];
     }
@@ -410,24 +467,19 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1)
   float m_run = -INFINITY, l_run = 0.f;
   const int d2 = threadIdx.x & 63, rg = threadIdx.x >> 6;
   float oa0 = 0.f, oa1 = 0.f, ob0 = 0.f, ob1 = 0.f;
-  const int nchunks = ok_n ? (n + kAttnChunk - 1) / kAttnChunk : 0;
   for (int c = rank; c < nchunks; c += kAttnCluster) {
     const int c0 = c * kAttnChunk;
     const int np = min(kAttnChunk, n - c0);
     __syncthreads();  // previous chunk's K/V/p reads are done
-    for (int u = threadIdx.x; u < kAttnChunk * 16; u += kAttnThreads) {
-      const int r = u >> 4, cu = u & 15;
-      uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-      if (ROPE && c0 + r == n - 1) {
-        kv = reinterpret_cast<const uint4*>(knew)[cu];
-        vv = reinterpret_cast<const uint4*>(vnew)[cu];
-      } else if (r < np) {
-        const size_t off = (size_t)(c0 + r) * kstride + (size_t)hk * hd;
-        kv = reinterpret_cast<const uint4*>(kcache + off)[cu];
-        vv = reinterpret_cast<const uint4*>(vcache + off)[cu];
-      }
-      reinterpret_cast<uint4*>(Ks)[u] = kv;
-      reinterpret_cast<uint4*>(Vs)[u] = vv;
+    if (!(early && c == rank))
+      stage_chunk(Ks, Vs, kcache, vcache, kstride, hk, hd, c0, np,
+                  ROPE ? n - 1 : -1);
+    if (ROPE && c0 <= n - 1 && n - 1 < c0 + np && threadIdx.x < 16) {
+      const int r = n - 1 - c0;  // the token's own row
+      reinterpret_cast<uint4*>(Ks + r * 128)[threadIdx.x] =
+          reinterpret_cast<const uint4*>(knew)[threadIdx.x];
+      reinterpret_cast<uint4*>(Vs + r * 128)[threadIdx.x] =
+          reinterpret_cast<const uint4*>(vnew)[threadIdx.x];
     }
     __syncthreads();
     {  // scores: thread = (position, quarter of the 128 dims)

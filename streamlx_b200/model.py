@@ -171,6 +171,10 @@ class SynthDecoder:
         # layers whose pool holds every expert for good (fully resident):
         # their launch needs no slot fill and the host no bookkeeping
         self.static_glu = [False] * cfg.layers
+        # with every layer static, launch a step's graph before checking the
+        # previous one (its device errors are raised one step late)
+        self.overlap_steps = True
+        self._inflight = None       # log buffer of an unchecked step
         self._all_pooled = None     # cached layer-set facts, set on first use
         self._store_list = None
         self._pf_layers = None
@@ -339,7 +343,12 @@ class SynthDecoder:
         # device log read back once per step: layer status [n] | status |
         # next token
         self.g_log = torch.zeros(n + 2, dtype=torch.int32, device=dev)
-        self.g_log_host = torch.zeros(n + 2, dtype=torch.int32).pin_memory()
+        # host copies of the log and of the control words alternate between
+        # two buffers, so a step can be launched while the previous one's
+        # copies are still pending (overlapped steps)
+        self._log_host = [torch.zeros(n + 2, dtype=torch.int32).pin_memory()
+                          for _ in range(2)]
+        self.g_log_host = self._log_host[0]
         self.g_lstatus = self.g_log[0:n]
         self.g_status = self.g_log[n:n + 1]
         self.g_tok_out = self.g_log[n + 1:n + 2]
@@ -348,7 +357,9 @@ class SynthDecoder:
         # control, written with one copy per step:
         # pos | force[n] | token | stamp
         self.g_ctrl = torch.zeros(n + 3, dtype=torch.int32, device=dev)
-        self.g_ctrl_host = torch.zeros(n + 3, dtype=torch.int32).pin_memory()
+        self._ctrl_host = [torch.zeros(n + 3, dtype=torch.int32).pin_memory()
+                           for _ in range(2)]
+        self.g_ctrl_host = self._ctrl_host[0]
         sh = [la.mlp.switch_mlp.shared for la in self.layers]
         s_inter = max([x[2] for x in sh if x] or [0])
         self.g_glu_scratch = torch.zeros(
@@ -370,7 +381,8 @@ class SynthDecoder:
         for pair in self.g_ev:      # torch creates the CUDA event on first use
             for e in pair:
                 e.record()
-        self._ev_done = torch.cuda.Event()
+        self._ev_step = [torch.cuda.Event(), torch.cuda.Event()]
+        self._ev_done = self._ev_step[0]
 
     def _pred_on(self, i: int) -> bool:
         """Layer i computes the next-layer prediction in its router launch:
@@ -478,15 +490,12 @@ class SynthDecoder:
         L.qlinear(self.w_lm, cfg.vocab, cfg.hidden, cfg.trunk_bits, self.x,
                   self.logits, self.g_status)
         L.argmax(self.logits, self.g_tok_out)
-        # plain async copies (no allocator event) so they capture as nodes:
+        # a plain async copy (no allocator event) so it captures as a node:
         # the step's ids become the next step's reuse candidates (not in the
-        # capture's initialising pass, which must not replace them), and the
-        # log goes to the host
+        # capture's initialising pass, which must not replace them)
         if serviced:
             L.copy_many([self.g_prev_ids.data_ptr()], [self.g_ids.data_ptr()],
                         [self.g_ids.numel() * 4])
-        L.copy_many([self.g_log_host.data_ptr()], [self.g_log.data_ptr()],
-                    [self.g_log.numel() * 4])
 
     def _capture(self) -> None:
         """Capture the graph of one whole step."""
@@ -575,6 +584,7 @@ class SynthDecoder:
         stream); nothing of a decode step is left pending after it."""
         if self._step_active:
             return
+        self._drain()
         stream = torch.cuda.current_stream(self.device)
         for pool in self._stores():
             if pool.store.has_pending():
@@ -636,6 +646,37 @@ class SynthDecoder:
                     raise RuntimeError(f"decode step ended without layer "
                                        f"{nxt}'s record")
 
+    def _overlapped(self) -> bool:
+        """Steps are launched before the previous one is checked: every
+        layer static (no slot service, no bookkeeping), no expert
+        exchange, no per-step timing events."""
+        return (self.overlap_steps and self.ep is None and
+                not self.glu_events and all(self.static_glu))
+
+    def _check_log(self, b: int) -> None:
+        """Raise the device errors a step's log (host copy b) reports."""
+        n = self.cfg.layers
+        log = self._log_host[b].numpy()
+        st = int(log[n])
+        bad = [int(v) for v in log[:n] if int(v) != 0]
+        if st != 0 or bad:
+            self.g_status.zero_()
+            self.g_lstatus.zero_()
+            raise L.SlxError("device", st or bad[0], "decode step device error")
+
+    def _drain(self) -> None:
+        """Wait for an overlapped step still unchecked and check it."""
+        prev, self._inflight = self._inflight, None
+        if prev is not None:
+            self._ev_step[prev].synchronize()
+            self._check_log(prev)
+
+    def sync(self) -> None:
+        """Finish every launched step: with overlapped steps a step's device
+        errors are raised by the next step, or here."""
+        self._drain()
+        torch.cuda.current_stream(self.device).synchronize()
+
     def _abort_step(self, stamp: int) -> None:
         """After a host-side failure: release any parked layer without
         fills, let the step finish and put the stores back in direct mode."""
@@ -665,7 +706,9 @@ class SynthDecoder:
         if stamp == 0:
             self._stamp += 1
             stamp = 1
-        ch = self.g_ctrl_host.numpy()
+        b = stamp & 1
+        ctrl = self._ctrl_host[b]   # its copy two steps ago has run
+        ch = ctrl.numpy()
         ch[0] = self.n_pos
         if self.repeat_p and self.n_pos > 0:
             # one draw per layer, in layer order (the eager path's sequence)
@@ -679,8 +722,8 @@ class SynthDecoder:
         cur = torch.cuda.current_stream(self.device)
         L.copy_many([self.g_ctrl.data_ptr(), self.g_ctrl.data_ptr() + 4 * (n + 1),
                      self.g_ctrl.data_ptr() + 4 * (n + 2)],
-                    [self.g_ctrl_host.data_ptr(), tok.data_ptr(),
-                     self.g_ctrl_host.data_ptr() + 4 * (n + 2)],
+                    [ctrl.data_ptr(), tok.data_ptr(),
+                     ctrl.data_ptr() + 4 * (n + 2)],
                     [4 * (n + 1), 4, 4])
         ht = self.host_times
         t0 = time.perf_counter()
@@ -689,8 +732,27 @@ class SynthDecoder:
         self._step_active = True
         self._graphs.replay()
         L._count(self._kernels_full)
+        L.copy_many([self._log_host[b].data_ptr()], [self.g_log.data_ptr()],
+                    [self.g_log.numel() * 4])
+        self._ev_done = self._ev_step[b]
         self._ev_done.record(cur)
         t1 = time.perf_counter()
+        if self._overlapped():
+            # nothing for the host to serve: check the previous step (long
+            # finished or about to) while this one runs
+            self._step_active = False
+            prev, self._inflight = self._inflight, b
+            if prev is not None:
+                self._ev_step[prev].synchronize()
+                self._check_log(prev)
+            ht["launch"] += t1 - t0
+            ht["serve"] += time.perf_counter() - t1
+            ht["steps"] += 1
+            self.n_pos += 1
+            nxt = torch.empty(1, dtype=torch.int32, device=self.device)
+            nxt.copy_(self.g_tok_out)
+            return nxt
+        self._drain()
         parks0 = ht["parks"]
         try:
             if self.ep is not None or all(self.static_glu):
@@ -712,13 +774,7 @@ class SynthDecoder:
         ht["flush"] += t3 - t2
         ht["steps"] += 1
         ht["park_steps"] += int(ht["parks"] > parks0)
-        log = self.g_log_host.numpy()
-        st = int(log[n])
-        bad = [int(v) for v in log[:n] if int(v) != 0]
-        if st != 0 or bad:
-            self.g_status.zero_()
-            self.g_lstatus.zero_()
-            raise L.SlxError("device", st or bad[0], "decode step device error")
+        self._check_log(b)
         self._glu_timing()
         self.n_pos += 1
         nxt = torch.empty(1, dtype=torch.int32, device=self.device)
