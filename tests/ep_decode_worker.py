@@ -81,6 +81,9 @@ def main():
     model, _, pools, reader = load_streaming_model(d, 0, k=cfg.top_k,
                                                    device=dev,
                                                    expert_parallel=True)
+    if model.ep is None and os.environ.get("EP_FORCE") == "1":
+        model.enable_expert_parallel()      # one rank, exchange form anyway
+    exchange = model.ep is not None
     ids = []
     got = decode(model, toks, ids)
     local_experts = sum(p.n_slots for p in pools.values())
@@ -88,7 +91,7 @@ def main():
         model.ep.close()
     dist.barrier()
     res = {"rank": rank, "world": dist.get_world_size(),
-           "local_experts": local_experts}
+           "local_experts": local_experts, "exchange": exchange}
     if rank == 0:
         ref, _, _, rd = load_streaming_model(d, 10**13, k=cfg.top_k,
                                              device=dev, resident="on")

@@ -30,8 +30,9 @@ def _port() -> int:
     return p
 
 
-def _run(n: int, preset: str, steps: int, tmp) -> dict:
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0", EP_TEST_DIR=str(tmp))
+def _run(n: int, preset: str, steps: int, tmp, force_ep: bool = False) -> dict:
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", EP_TEST_DIR=str(tmp),
+               EP_FORCE="1" if force_ep else "0")
     cmd = ["timeout", "-k", "30", "600", sys.executable, "-m",
            "torch.distributed.run", "--nnodes=1", "--nproc-per-node", str(n),
            "--master-addr", "127.0.0.1", "--master-port", str(_port()),
@@ -43,10 +44,14 @@ def _run(n: int, preset: str, steps: int, tmp) -> dict:
     return json.loads(line)
 
 
+@pytest.mark.parametrize("force_ep", [False, True])
 @pytest.mark.parametrize("preset", ["tiny_dec", "tiny_dec2"])
-def test_ep_decode_one_rank_bit_identical(preset, tmp_path):
-    res = _run(1, preset, 12, tmp_path)
+def test_ep_decode_one_rank_bit_identical(preset, force_ep, tmp_path):
+    """force_ep: the exchange form anyway (rows written to this rank's own
+    receive block, then slx_ep_combine_rmsnorm), which one GPU can run."""
+    res = _run(1, preset, 12, tmp_path, force_ep)
     assert res["world"] == 1
+    assert res["exchange"] == force_ep
     assert res["bit_identical"], res
     assert res["oracle_ok"], res
 
