@@ -96,6 +96,9 @@ class Clocks:
         self.p = None
 
     def start(self):
+        """Start sampling and return once the first sample is written (at
+        most 5 s): nvidia-smi takes a while to start, longer than a short
+        timed region."""
         try:
             self.f = open(self.path, "w")
             self.p = subprocess.Popen(
@@ -104,6 +107,11 @@ class Clocks:
                 stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:   # noqa: BLE001 - clocks are best effort
             self.p = None
+            return
+        t_end = time.time() + 5.0
+        while (time.time() < t_end and self.p.poll() is None and
+               os.path.getsize(self.path) == 0):
+            time.sleep(0.01)
 
     def stop(self) -> dict:
         if self.p is None:
@@ -799,9 +807,9 @@ def run_ours(args) -> None:
         model.host_times[k_] = 0
     l0 = L.LAUNCHES[0]
     c0 = pool_counts()
+    clocks.start()              # sampling before any rank starts timing
     barrier()
     torch.cuda.synchronize()
-    clocks.start()
     e0, e1 = (torch.cuda.Event(enable_timing=True),
               torch.cuda.Event(enable_timing=True))
     e0.record()

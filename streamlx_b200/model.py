@@ -648,10 +648,11 @@ class SynthDecoder:
 
     def _overlapped(self) -> bool:
         """Steps are launched before the previous one is checked: every
-        layer static (no slot service, no bookkeeping), no expert
-        exchange, no per-step timing events."""
-        return (self.overlap_steps and self.ep is None and
-                not self.glu_events and all(self.static_glu))
+        layer static (no slot service, no bookkeeping; the expert-parallel
+        form is, its exchange is ordered on the device by the step stamp)
+        and no per-step timing events."""
+        return (self.overlap_steps and not self.glu_events and
+                (self.ep is not None or all(self.static_glu)))
 
     def _check_log(self, b: int) -> None:
         """Raise the device errors a step's log (host copy b) reports."""
