@@ -1141,8 +1141,22 @@ __device__ __noinline__ void load_bfrag_lsu(const DownArgs& d, uint32_t* bfrag,
   auto touched = [&](int j) { return nbt >= U || (j - w0 + U) % U < nbt; };
   const int pu = nGmax * 8;  // uint4 per unit
   const int total = U * pu;
+  const int totp = U * nGmax;  // float4 partial sums
   uint4* bf4 = reinterpret_cast<uint4*>(bfrag);
-  for (int base = threadIdx.x; base < total; base += 4 * kFThreads) {
+  auto part_of = [&](int q) {
+    const int j = q / nGmax, G = q % nGmax;
+    const bool sh = j >= d.k;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (touched(j) && G < (sh ? nGs : nGr))
+      v = __ldcg(reinterpret_cast<const float4*>(
+                     sh ? d.hpart_sh : d.hpart + (size_t)j * d.unit_part_floats) +
+                 G);
+    return v;
+  };
+  // the fragments and (in the first round) the partial sums in one round
+  // of loads per thread
+  for (int base = threadIdx.x, it = 0; base < total || it == 0;
+       base += 4 * kFThreads, ++it) {
     uint4 v[4];
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
@@ -1157,22 +1171,18 @@ __device__ __noinline__ void load_bfrag_lsu(const DownArgs& d, uint32_t* bfrag,
                         o);
       }
     }
+    float4 pv = make_float4(0.f, 0.f, 0.f, 0.f);
+    const bool has_p = it == 0 && (int)threadIdx.x < totp;
+    if (has_p) pv = part_of(threadIdx.x);
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
       const int p = base + r * kFThreads;
       if (p < total) bf4[p] = v[r];
     }
+    if (has_p) reinterpret_cast<float4*>(bpart)[threadIdx.x] = pv;
   }
-  for (int p = threadIdx.x; p < U * nGmax; p += kFThreads) {
-    const int j = p / nGmax, G = p % nGmax;
-    const bool sh = j >= d.k;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (touched(j) && G < (sh ? nGs : nGr))
-      v = __ldcg(reinterpret_cast<const float4*>(
-                     sh ? d.hpart_sh : d.hpart + (size_t)j * d.unit_part_floats) +
-                 G);
-    reinterpret_cast<float4*>(bpart)[p] = v;
-  }
+  for (int q = threadIdx.x + kFThreads; q < totp; q += kFThreads)
+    reinterpret_cast<float4*>(bpart)[q] = part_of(q);
 }
 
 template <int BITS>
