@@ -778,9 +778,10 @@ def run_ours(args) -> None:
         model, tok_, pools, reader = load_streaming_model(
             d, int(budget_gib * (1 << 30)), k=cfg.top_k, device=dev)
     t_load = time.time() - t_load
-    # no timing events inside the timed steps' graphs: an event node
-    # serialises its launch against the neighbours (the bracketed in-step
-    # SwitchGLU times are taken in a separate loop after the timed ones)
+    # no timing events inside the timed steps' graphs (the decoder's
+    # default): an event node serialises its launch against the neighbours;
+    # the bracketed in-step SwitchGLU times come from a separate loop after
+    # the timed ones
     model.glu_events = False
     rng = np.random.default_rng(SEED)      # the same prompt on every rank
     prompt = rng.integers(0, cfg.vocab, args.prompt)

@@ -158,7 +158,9 @@ class SynthDecoder:
         self.n_pos = 0
         self.use_graphs = cfg.has_trunk
         self.pdl = True             # captured kernels chain with PDL
-        self.glu_events = True      # time sampled SwitchGLU pairs in graphs
+        # time sampled SwitchGLU launches with event pairs in the step graph
+        # (a measurement aid: the event nodes cost the step a few us)
+        self.glu_events = False
         self._graphs = None
         self.glu_times: list | None = None
         # host seconds per phase of the graph-launched step (launch, the
@@ -745,7 +747,13 @@ class SynthDecoder:
             prev, self._inflight = self._inflight, b
             if prev is not None:
                 self._ev_step[prev].synchronize()
-                self._check_log(prev)
+                try:
+                    self._check_log(prev)
+                except L.SlxError:
+                    # the step just launched ran on the same (sticky) status
+                    # words: its log goes with the error
+                    self._inflight = None
+                    raise
             ht["launch"] += t1 - t0
             ht["serve"] += time.perf_counter() - t1
             ht["steps"] += 1

@@ -218,6 +218,49 @@ def test_resident_layers_skip_the_pool(tiny, monkeypatch):
     assert torch.equal(a, b) and torch.equal(a, c)
 
 
+@pytest.mark.parametrize("resident", [True, False])
+def test_step_device_error_is_raised(tiny, resident, monkeypatch):
+    """A token id outside the vocabulary (the embedding kernel's bounds check
+    sets SLX_ERR_OUT_OF_RANGE; nothing faults) is raised as SlxError: with
+    every layer static the steps overlap, so the error surfaces at the next
+    step or at sync(); with pools at the step itself.  The decoder keeps
+    working afterwards."""
+    from streamlx_b200 import _lib as L
+    monkeypatch.setenv("STREAMLX_EVICT", "lru")
+    d = tiny["tiny_dec"]
+    cfg = synth.load_config(d)
+    bpe = synth.expert_bytes(cfg.hidden, cfg.inter, cfg.expert_bits, 64)
+    if resident:
+        model, _, pools, reader = load_streaming_model(
+            d, 10 ** 13, k=cfg.top_k, resident="on")
+        assert model._overlapped()
+    else:
+        model, _, pools, reader = load_streaming_model(
+            d, 6 * bpe * cfg.layers, k=cfg.top_k)
+        assert not model._overlapped()
+
+    def tok(t):
+        return torch.tensor([t], dtype=torch.int32, device=model.device)
+
+    for t in (3, 9):
+        model.step(tok(t))
+    with pytest.raises(L.SlxError):
+        model.step(tok(cfg.vocab + 5))
+        model.sync()
+    for t in (4, 8):
+        model.step(tok(t))
+    model.sync()
+    if resident:        # raised by the next step, and only once
+        model.step(tok(cfg.vocab + 7))
+        with pytest.raises(L.SlxError):
+            model.step(tok(5))
+        for t in (6, 2):
+            model.step(tok(t))
+        model.sync()
+    assert int(model.g_status.item()) == 0
+    reader.close()
+
+
 def test_pool_dropin_call_matches_oracle(tiny):
     d = tiny["tiny_dec"]
     cfg = synth.load_config(d)
