@@ -1744,6 +1744,9 @@ static int launch_gemv_t(GemvArgs a, cudaStream_t stream, bool pdl_secondary) {
   a.wait_primary = pdl_secondary ? 1 : 0;
   if (a.n_tiles <= 0) return SLX_OK;
   int grid = num_sms();
+  // a long dense GEMV (the lm_head) streams from HBM: two CTAs per SM keep
+  // twice the tiles in flight (the shared-memory request fits two)
+  if (a.mode == SLX_GEMV_LINEAR && a.n_tiles >= 8 * grid) grid *= 2;
   if (grid > a.n_tiles) grid = a.n_tiles;
   cudaError_t e = set_smem<decltype(&k_qgemv<BITS>), BITS>(k_qgemv<BITS>, smem);
   if (e != cudaSuccess) return SLX_ERR_CUDA;

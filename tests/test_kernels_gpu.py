@@ -217,7 +217,8 @@ def test_switchglu_host_errors(dev):
 
 @pytest.mark.parametrize("shape", [(4608, 2048, 4, 1), (1024, 512, 4, 2),
                                    (2560, 3072, 4, 1), (512, 2560, 2, 1),
-                                   (272, 1024, 8, 1)])
+                                   (272, 1024, 8, 1),
+                                   (40960, 512, 4, 1)])   # two CTAs per SM
 def test_qlinear_parity(dev, shape):
     out_f, in_f, bits, T = shape
     pk, s, b = quant_stack(1, out_f, in_f, bits, seed=out_f)
