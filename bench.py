@@ -850,7 +850,7 @@ def run_ours(args) -> None:
     f0.record()
     for _ in range(args.steps):
         t_in[0] = tok_host      # the last step's copy from it has finished
-        out = model.step(t_in.to(dev, non_blocking=True))
+        out = model.step(t_in)  # host token: copied with the step's controls
         tok_host = int(out.item())
     f1.record()
     torch.cuda.synchronize()

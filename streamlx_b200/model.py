@@ -255,8 +255,9 @@ class SynthDecoder:
 
     @torch.no_grad()
     def step(self, token: torch.Tensor) -> torch.Tensor:
-        """One decode step for the token id in `token` (device int32 [1]);
-        returns the greedy next token (device int32 [1]).
+        """One decode step for the token id in `token` (int32 [1], on the
+        device or in host memory); returns the greedy next token (device
+        int32 [1]).
 
         With ``use_graphs`` the step runs as one captured CUDA graph whose
         layers report their routing to the host as they run; the host keeps
@@ -266,6 +267,8 @@ class SynthDecoder:
         if self.ep is not None or (self.use_graphs and self._pooled()):
             return self._step_graph(token)
         self.flush()
+        if token.device != self.device or token.dtype != torch.int32:
+            token = token.to(device=self.device, dtype=torch.int32)
         return self._step_eager(token)
 
     @torch.no_grad()
@@ -720,14 +723,21 @@ class SynthDecoder:
             ch[1:1 + n] = 0
         ch[n + 2] = stamp
         tok = token.reshape(1)
-        if tok.dtype != torch.int32 or tok.device != self.device:
-            tok = tok.to(device=self.device, dtype=torch.int32)
         cur = torch.cuda.current_stream(self.device)
-        L.copy_many([self.g_ctrl.data_ptr(), self.g_ctrl.data_ptr() + 4 * (n + 1),
-                     self.g_ctrl.data_ptr() + 4 * (n + 2)],
-                    [ctrl.data_ptr(), tok.data_ptr(),
-                     ctrl.data_ptr() + 4 * (n + 2)],
-                    [4 * (n + 1), 4, 4])
+        if tok.device.type == "cpu":
+            # a host token travels with the control words: one copy
+            ch[n + 1] = int(tok[0])
+            L.copy_many([self.g_ctrl.data_ptr()], [ctrl.data_ptr()],
+                        [4 * (n + 3)])
+        else:
+            if tok.dtype != torch.int32 or tok.device != self.device:
+                tok = tok.to(device=self.device, dtype=torch.int32)
+            L.copy_many([self.g_ctrl.data_ptr(),
+                         self.g_ctrl.data_ptr() + 4 * (n + 1),
+                         self.g_ctrl.data_ptr() + 4 * (n + 2)],
+                        [ctrl.data_ptr(), tok.data_ptr(),
+                         ctrl.data_ptr() + 4 * (n + 2)],
+                        [4 * (n + 1), 4, 4])
         ht = self.host_times
         t0 = time.perf_counter()
         for pool in self._stores():

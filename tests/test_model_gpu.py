@@ -219,6 +219,34 @@ def test_resident_layers_skip_the_pool(tiny, monkeypatch):
 
 
 @pytest.mark.parametrize("resident", [True, False])
+def test_host_token_equals_device_token(tiny, resident, monkeypatch):
+    """step() with the token in pinned host memory (copied with the step's
+    control words) decodes exactly as with a device token."""
+    monkeypatch.setenv("STREAMLX_EVICT", "lru")
+    d = tiny["tiny_dec"]
+    cfg = synth.load_config(d)
+    bpe = synth.expert_bytes(cfg.hidden, cfg.inter, cfg.expert_bits, 64)
+    seq = np.random.default_rng(8).integers(0, cfg.vocab, 8)
+    out = []
+    for host in (False, True):
+        if resident:
+            model, _, _, reader = load_streaming_model(
+                d, 10 ** 13, k=cfg.top_k, resident="on")
+        else:
+            model, _, _, reader = load_streaming_model(
+                d, 6 * bpe * cfg.layers, k=cfg.top_k)
+        lg = []
+        for t in seq:
+            tk = torch.tensor([int(t)], dtype=torch.int32)
+            model.step(tk.pin_memory() if host else tk.to(model.device))
+            lg.append(model.logits.clone())
+        model.sync()
+        out.append(torch.cat(lg).cpu().view(torch.int16))
+        reader.close()
+    assert torch.equal(out[0], out[1])
+
+
+@pytest.mark.parametrize("resident", [True, False])
 def test_step_device_error_is_raised(tiny, resident, monkeypatch):
     """A token id outside the vocabulary (the embedding kernel's bounds check
     sets SLX_ERR_OUT_OF_RANGE; nothing faults) is raised as SlxError: with
