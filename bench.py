@@ -426,7 +426,7 @@ def run_glu(args) -> None:
 
 
 def run_sweep(args) -> None:
-    """Expert-major prefill with streaming: one
+    """Expert-major prefill with streaming (the C4 workload): one
     2048-token chunk of seeded N(0,1) bf16 hidden states through every MoE
     layer of the 117B-shaped checkpoint (the same chunk into each layer),
     experts in 7.5 GiB pools, every needed expert read once per layer from

@@ -9,7 +9,7 @@ import torch
 from oracle import affine as A
 from streamlx_b200 import synth
 
-TOL_MAX_ABS = 2e-2   # north-star tolerance on bf16 layer outputs
+TOL_MAX_ABS = 2e-2   # parity tolerance on bf16 layer outputs
 TOL_REL_L2 = 1e-3
 
 
