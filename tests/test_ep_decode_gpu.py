@@ -7,7 +7,7 @@ same model decoded on one GPU with every expert resident; the sharded run is
 also checked against the CPU oracle (ordered experts at every layer and step,
 logits within the decoder tolerance).  One rank holds every expert and
 decodes without the exchange (the loader's process-group path on one GPU);
-it runs on any box.  Two ranks need two GPUs."""
+it runs on any machine with a GPU.  Two ranks need two GPUs."""
 
 import json
 import os

@@ -4,7 +4,7 @@ Each rank checks its combined outputs against the same tokens run through
 all 256 experts on its own GPU (``bench.py --mode ep --check``): batch-1
 decode (replicated token, all-reduce), batch-64 decode and a 2048-token
 prefill (sharded tokens, dispatch/combine).  Needs two GPUs; skipped on a
-one-GPU box."""
+machine with one GPU."""
 
 import os
 import socket
