@@ -396,6 +396,41 @@ def test_attn_rope_one_launch_equals_two(dev, nq, nkv):
         assert torch.equal(c0.view(torch.int16), c1.view(torch.int16))
 
 
+@pytest.mark.parametrize("pos", [511, 512, 575, 599, 1040])
+def test_attn_rope_long_context_equals_two(dev, pos):
+    """The fused decode attention at positions whose chunks outnumber the
+    cluster's CTAs (the first chunk staged before the wait, later ones
+    after it, the token's own row substituted in either): same bits as the
+    two-launch form over a randomly filled cache."""
+    rng = np.random.default_rng(pos)
+    nq, nkv, hd, maxlen, eps = 24, 4, 128, 1100, 1e-6
+    inv = torch.from_numpy(OT.rope_inv_freq(hd, 1e6)).to(dev)
+    qn = bf16_tensor(A.bf16_round((1 + 0.05 * rng.standard_normal(hd))
+                                  .astype(np.float32)), dev)
+    kn = bf16_tensor(A.bf16_round((1 + 0.05 * rng.standard_normal(hd))
+                                  .astype(np.float32)), dev)
+    fill = bf16_tensor(A.bf16_round(
+        rng.standard_normal((maxlen, nkv, hd)).astype(np.float32)), dev)
+    caches = [(fill.clone(), fill.clone()) for _ in range(2)]
+    qkv = bf16_tensor(A.bf16_round(
+        rng.standard_normal((1, (nq + 2 * nkv) * hd)).astype(np.float32)), dev)
+    p = torch.tensor([pos], dtype=torch.int32, device=dev)
+    st = _status(dev)
+    a1 = torch.empty(1, nq * hd, dtype=torch.bfloat16, device=dev)
+    a2 = torch.empty_like(a1)
+    q2 = qkv.clone()
+    L.qk_norm_rope_cache(q2, nq, nkv, hd, qn, kn, eps, inv, p,
+                         caches[0][0], caches[0][1], st)
+    L.attn_decode(q2, nq, nkv, hd, caches[0][0], caches[0][1], p, a1)
+    L.attn_rope_decode(qkv, nq, nkv, hd, qn, kn, eps, inv, p,
+                       caches[1][0], caches[1][1], a2, st)
+    torch.cuda.synchronize()
+    assert st.item() == 0
+    assert torch.equal(a1.view(torch.int16), a2.view(torch.int16))
+    for c0, c1 in zip(*caches):
+        assert torch.equal(c0.view(torch.int16), c1.view(torch.int16))
+
+
 def test_router_with_norm_equals_norm_then_router(dev):
     """slx_router_topk_multi_norm (residual add + RMSNorm + two router heads
     in one launch) against slx_add_rmsnorm_out + slx_router_topk_multi: the
